@@ -1,0 +1,165 @@
+/* nutllm_cuda.h — C ABI of libnutcuda.so, the B200 (sm_100a) token loop.
+ *
+ * Plain pointers and sizes only.  Every entry point returns a nut_status;
+ * nut_last_error() gives the calling thread's message for the last failure,
+ * formatted "component: reason" like the reference's exceptions.  The status
+ * codes map one-to-one onto the exception classes the reference throws for
+ * the same conditions, so a C++ wrapper can re-throw the same type.
+ *
+ * Citations are to the reference project (MokiMeow/nutllm) interface each
+ * entry point replaces.
+ */
+#ifndef NUTLLM_CUDA_H
+#define NUTLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nut_status {
+    NUT_OK = 0,
+    NUT_INVALID_ARGUMENT = 1, /* std::invalid_argument */
+    NUT_OUT_OF_RANGE = 2,     /* std::out_of_range */
+    NUT_LENGTH_ERROR = 3,     /* std::length_error */
+    NUT_RUNTIME_ERROR = 4,    /* std::runtime_error, CUDA failures included */
+    NUT_RANGE_ERROR = 5,      /* std::range_error */
+    NUT_DEVICE_TIMEOUT = 6    /* a bounded device-side wait gave up */
+} nut_status;
+
+/* QuantType (include/quant.hpp:9-12). */
+enum { NUT_QUANT_INT8 = 0, NUT_QUANT_INT4 = 1 };
+
+/* ModelConfig (include/model.hpp:8-24); kv_heads 0 means kv_heads = heads. */
+typedef struct nut_config {
+    int64_t layers, heads, dim, head_dim, ffn_dim, vocab_size, max_seq,
+        eos_token, kv_heads;
+} nut_config;
+
+/* Host view of a QuantizedMatrix's storage (include/quant.hpp:14-50):
+ * [rows][cols] row-major, flattened blocks of block_size (must be 32)
+ * weights, INT8 one byte per weight or INT4 two's-complement nibbles with
+ * the even flattened index in the low nibble, one fp16 scale (bits) per
+ * block. */
+typedef struct nut_qmatrix_view {
+    const uint8_t *data;
+    const uint16_t *scales;
+    int64_t rows, cols, block_size;
+    int32_t type;
+} nut_qmatrix_view;
+
+/* QuantizedLayerWeights (include/quant_model.hpp:9-29): projections are
+ * [out][in]: query (dim x dim), key/value (kv_dim x dim), output
+ * (dim x dim), gate/up (ffn x dim), down (dim x ffn). */
+typedef struct nut_layer_view {
+    nut_qmatrix_view query, key, value, output, gate, up, down;
+    const float *attention_norm, *ffn_norm; /* [dim] each */
+} nut_layer_view;
+
+/* QuantizedModelWeights (include/quant_model.hpp:31-46).  lm_head is
+ * ignored when tied_embeddings is set (output_weights() == embeddings). */
+typedef struct nut_model_view {
+    nut_config config;
+    int32_t quant_type;
+    int32_t tied_embeddings;
+    const float *embeddings; /* [vocab][dim] */
+    const float *final_norm; /* [dim] */
+    const float *lm_head;    /* [vocab][dim] */
+    const nut_layer_view *layers;
+    int64_t n_layers;
+} nut_model_view;
+
+/* GenerationStats (include/generate.hpp:19-24), device-event timed. */
+typedef struct nut_generation_stats {
+    int64_t prefill_tokens, generated_tokens;
+    double prefill_seconds, decode_seconds;
+} nut_generation_stats;
+
+typedef struct nut_qmatrix nut_qmatrix;
+typedef struct nut_model nut_model;
+typedef struct nut_kv nut_kv;
+
+/* Message of the calling thread's last failure ("" if none). */
+const char *nut_last_error(void);
+
+/* Number of visible CUDA devices. */
+nut_status nut_device_count(int *count);
+
+/* ---- QuantizedMatrix device mirror (src/quant.cpp:154-321) ---------- */
+
+/* Uploads one quantised matrix to `device`. */
+nut_status nut_qmatrix_create(const nut_qmatrix_view *view, int device,
+                              nut_qmatrix **out);
+nut_status nut_qmatrix_destroy(nut_qmatrix *matrix);
+/* Reads the device copy back in the reference storage layout. */
+nut_status nut_qmatrix_download(const nut_qmatrix *matrix, uint8_t *data,
+                                uint16_t *scales);
+/* matvec_quantized_threaded (src/quant.cpp:262-321) with HOST buffers:
+ * y[rows] = Q x[cols].  Synchronous. */
+nut_status nut_qmatvec(nut_qmatrix *matrix, const float *x, float *y);
+/* The same product on DEVICE buffers, enqueued on `stream` (a
+ * cudaStream_t, NULL = the legacy default stream). */
+nut_status nut_qmatvec_async(nut_qmatrix *matrix, const float *x_device,
+                             float *y_device, void *stream);
+
+/* ---- Model weights (include/quant_model.hpp:31-46) ------------------- */
+
+/* Copies a QuantizedModelWeights image to `device` (layout private to the
+ * library).  Fails with NUT_INVALID_ARGUMENT for an invalid config or a
+ * layer whose shape does not match it (src/quant_model.cpp:161-166). */
+nut_status nut_model_create(const nut_model_view *view, int device,
+                            nut_model **out);
+nut_status nut_model_destroy(nut_model *model);
+/* QuantizedModelWeights::storage_bytes (src/quant_model.cpp:140-156). */
+nut_status nut_model_storage_bytes(const nut_model *model, uint64_t *bytes);
+
+/* ---- KV cache and decode state (include/kvcache.hpp:8-31) ------------ */
+
+/* KVCache(config) (src/kvcache.cpp:173-177): fp32 keys and values of
+ * capacity config.max_seq, resident on the model's device, plus the
+ * sequence's decode state (last hidden vector, logits). */
+nut_status nut_kv_create(nut_model *model, nut_kv **out);
+nut_status nut_kv_destroy(nut_kv *kv);
+nut_status nut_kv_reset(nut_kv *kv);                   /* KVCache::reset */
+nut_status nut_kv_length(const nut_kv *kv, int64_t *length);
+nut_status nut_kv_set_length(nut_kv *kv, int64_t length); /* :231-235 */
+nut_status nut_kv_memory_bytes(const nut_kv *kv, uint64_t *bytes);
+/* KVCache::key / KVCache::value (src/kvcache.cpp:207-214): copies one
+ * head_dim vector of each to the host (either pointer may be NULL). */
+nut_status nut_kv_read(const nut_kv *kv, int64_t layer, int64_t head,
+                       int64_t position, float *key, float *value);
+
+/* ---- Token loop -------------------------------------------------------- */
+
+/* decode_quantized_token (src/quant_model.cpp:158-206): runs one token
+ * through every layer at position kv length, appends its keys and values
+ * and advances the length.  hidden (dim floats, host) may be NULL; the
+ * pre-final-norm hidden vector stays on the device for nut_logits. */
+nut_status nut_decode_token(nut_model *model, nut_kv *kv, int32_t token,
+                            float *hidden);
+/* prefill_quantized (src/quant_model.cpp:208-220): resets the cache and
+ * feeds the prompt; hidden (dim floats, host) may be NULL. */
+nut_status nut_prefill(nut_model *model, nut_kv *kv, const int32_t *tokens,
+                       int64_t n, float *hidden);
+/* Final rmsnorm + fp32 lm_head + first-index argmax over the last hidden
+ * vector (src/generate.cpp:197-201).  Either output may be NULL. */
+nut_status nut_logits(nut_model *model, nut_kv *kv, float *logits,
+                      int32_t *argmax);
+/* Greedy generate_tokens_cached (src/generate.cpp:174-216): prefill, then
+ * up to max_tokens greedy steps, the whole loop on the device.  With
+ * stop_at_eos set, a chosen eos_token ends the loop without being emitted
+ * (the reference behaviour); with it clear, exactly max_tokens ids are
+ * produced (the parity-harness form).  ids has room for max_tokens;
+ * logits (max_tokens x vocab, host) and stats may be NULL. */
+nut_status nut_generate_greedy(nut_model *model, nut_kv *kv,
+                               const int32_t *prompt, int64_t n,
+                               int64_t max_tokens, int32_t stop_at_eos,
+                               int32_t *ids, int64_t *n_generated,
+                               float *logits, nut_generation_stats *stats);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NUTLLM_CUDA_H */

@@ -1,0 +1,380 @@
+"""Test infrastructure only: CPU checkers for the nutllm token loop.
+
+* ``Oracle``    — ctypes binding of ``_build/liboracle.so``, the plain-C
+  restatement of the reference algorithm (nut_oracle.c).
+* ``Reference`` — ctypes binding of ``_ref/libnutref.so``, the unmodified
+  reference sources compiled by this directory's Makefile (present only
+  where the reference was available at build time).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's cpu_baseline and
+reference legs may import this package, and only as the checker or the
+timed CPU baseline — never as the product path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from typing import Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_LIB = os.path.join(HERE, "_build", "liboracle.so")
+REF_LIB = os.path.join(HERE, "_ref", "libnutref.so")
+
+_P = C.c_void_p
+_I64 = C.c_int64
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def build_oracle() -> str:
+    """Builds liboracle.so with gcc if it is missing (it is plain C)."""
+    if not os.path.exists(ORACLE_LIB):
+        subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    return ORACLE_LIB
+
+
+# ---------------------------------------------------------------- oracle
+
+
+class _Config(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in (
+        "layers", "heads", "dim", "head_dim", "ffn_dim", "vocab_size",
+        "max_seq", "eos_token", "kv_heads")]
+
+
+class _QM(C.Structure):
+    _fields_ = [("data", _P), ("scales", _P), ("rows", _I64), ("cols", _I64)]
+
+
+class _Layer(C.Structure):
+    _fields_ = [(n, _QM) for n in ("q", "k", "v", "o", "gate", "up", "down")] + [
+        ("attention_norm", _P), ("ffn_norm", _P)]
+
+
+class _Model(C.Structure):
+    _fields_ = [("config", _Config), ("type", C.c_int), ("embeddings", _P),
+                ("final_norm", _P), ("lm_head", _P), ("layers", C.POINTER(_Layer))]
+
+
+class _KV(C.Structure):
+    _fields_ = [("keys", _P), ("values", _P), ("length", _I64)]
+
+
+class Oracle:
+    def __init__(self):
+        lib = C.CDLL(build_oracle())
+        lib.orc_last_error.restype = C.c_char_p
+        lib.orc_half_from_float.argtypes = [C.c_float, C.POINTER(C.c_int)]
+        lib.orc_half_from_float.restype = C.c_uint16
+        lib.orc_half_to_float.argtypes = [C.c_uint16]
+        lib.orc_half_to_float.restype = C.c_float
+        lib.orc_quantize.argtypes = [_P, _I64, _I64, C.c_int, _P, _P]
+        lib.orc_qmatvec.argtypes = [C.c_int, _I64, _I64, _P, _P, _P, _P]
+        lib.orc_set_threads.argtypes = [C.c_int]
+        lib.orc_set_threads.restype = None
+        lib.orc_rmsnorm.argtypes = [_P, _P, _P, _I64, C.c_float]
+        lib.orc_rmsnorm.restype = None
+        lib.orc_rope.argtypes = [_P, _I64, _I64]
+        lib.orc_rope.restype = None
+        lib.orc_matvec_f32.argtypes = [_P, _I64, _I64, _P, _P]
+        lib.orc_matvec_f32.restype = None
+        lib.orc_argmax.argtypes = [_P, _I64]
+        lib.orc_argmax.restype = _I64
+        lib.orc_decode_token.argtypes = [C.POINTER(_Model), C.POINTER(_KV),
+                                         C.c_int, _P]
+        lib.orc_logits.argtypes = [C.POINTER(_Model), _P, _P, C.POINTER(_I64)]
+        lib.orc_generate.argtypes = [C.POINTER(_Model), C.POINTER(_KV), _P,
+                                     _I64, _I64, _P, _P, _P]
+        self.lib = lib
+
+    def _check(self, status):
+        if status != 0:
+            raise RuntimeError(f"oracle status {status}: "
+                               f"{self.lib.orc_last_error().decode()}")
+
+    def set_threads(self, n: int) -> None:
+        self.lib.orc_set_threads(n)
+
+    def half_from_float(self, v: float) -> int:
+        st = C.c_int(0)
+        h = self.lib.orc_half_from_float(v, C.byref(st))
+        self._check(st.value)
+        return h
+
+    def half_to_float(self, h: int) -> float:
+        return self.lib.orc_half_to_float(h)
+
+    def quantize(self, w: np.ndarray, qtype: int):
+        w = np.ascontiguousarray(w, np.float32)
+        rows, cols = w.shape
+        n = rows * cols
+        data = np.zeros(n if qtype == 0 else (n + 1) // 2, np.uint8)
+        scales = np.zeros((n + 31) // 32, np.uint16)
+        self._check(self.lib.orc_quantize(_ptr(w), rows, cols, qtype,
+                                          _ptr(data), _ptr(scales)))
+        return data, scales
+
+    def qmatvec(self, qtype, rows, cols, data, scales, x):
+        y = np.empty(rows, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        self._check(self.lib.orc_qmatvec(qtype, rows, cols, _ptr(data),
+                                         _ptr(scales), _ptr(x), _ptr(y)))
+        return y
+
+    def rmsnorm(self, x, w, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty_like(x)
+        self.lib.orc_rmsnorm(_ptr(x), _ptr(w), _ptr(out), x.size, eps)
+        return out
+
+    def matvec_f32(self, w, x):
+        w = np.ascontiguousarray(w, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(w.shape[0], np.float32)
+        self.lib.orc_matvec_f32(_ptr(w), w.shape[0], w.shape[1], _ptr(x), _ptr(y))
+        return y
+
+    def model(self, weights) -> "OracleModel":
+        return OracleModel(self, weights)
+
+
+class OracleModel:
+    """Oracle view of an nutllm_b200.ModelWeights host image (same bytes)."""
+
+    def __init__(self, oracle: Oracle, w):
+        self.o = oracle
+        self.w = w
+        c = w.config
+        self.config = c
+        layers = (_Layer * int(c.layers))()
+        for i, lw in enumerate(w.layers):
+            for name, m in zip(("q", "k", "v", "o", "gate", "up", "down"),
+                               lw.projections()):
+                setattr(layers[i], name, _QM(m.data.ctypes.data,
+                                             m.scales.ctypes.data, m.rows, m.cols))
+            layers[i].attention_norm = lw.attention_norm.ctypes.data
+            layers[i].ffn_norm = lw.ffn_norm.ctypes.data
+        self._layers = layers
+        m = _Model()
+        m.config = _Config(*[int(getattr(c, n)) for n, _ in _Config._fields_])
+        m.config.kv_heads = c.kv_heads or c.heads
+        m.type = w.qtype
+        m.embeddings = w.embeddings.ctypes.data
+        m.final_norm = w.final_norm.ctypes.data
+        m.lm_head = w.output_weights().ctypes.data
+        m.layers = C.cast(layers, C.POINTER(_Layer))
+        self._model = m
+        kvh = c.kv_heads or c.heads
+        n = int(c.layers * kvh * c.max_seq * c.head_dim)
+        self.keys = np.zeros(n, np.float32)
+        self.values = np.zeros(n, np.float32)
+        self.kv = _KV(self.keys.ctypes.data, self.values.ctypes.data, 0)
+
+    def reset(self):
+        self.kv.length = 0
+
+    def decode(self, token: int) -> np.ndarray:
+        h = np.empty(self.config.dim, np.float32)
+        self.o._check(self.o.lib.orc_decode_token(C.byref(self._model),
+                                                  C.byref(self.kv), token, _ptr(h)))
+        return h
+
+    def logits(self, hidden: np.ndarray):
+        out = np.empty(self.config.vocab_size, np.float32)
+        best = _I64(0)
+        self.o._check(self.o.lib.orc_logits(C.byref(self._model), _ptr(hidden),
+                                            _ptr(out), C.byref(best)))
+        return out, best.value
+
+    def generate(self, prompt: Sequence[int], steps: int):
+        """prefill + `steps` greedy tokens; returns (ids, logits, prefill hidden)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(max(steps, 1), np.int32)
+        lg = np.empty((max(steps, 1), self.config.vocab_size), np.float32)
+        hid = np.empty(self.config.dim, np.float32)
+        self.o._check(self.o.lib.orc_generate(C.byref(self._model), C.byref(self.kv),
+                                              _ptr(p), p.size, steps, _ptr(ids),
+                                              _ptr(lg), _ptr(hid)))
+        return ids[:steps], lg[:steps], hid
+
+
+# ------------------------------------------------------------- reference
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_LIB)
+
+
+class Reference:
+    """The unmodified reference (oracle/_ref/libnutref.so)."""
+
+    def __init__(self):
+        if not reference_available():
+            raise RuntimeError("reference build missing: make -C oracle ref")
+        lib = C.CDLL(REF_LIB)
+        lib.ref_last_error.restype = C.c_char_p
+        S = C.c_size_t
+        lib.ref_quantize.argtypes = [_P, S, S, C.c_int, _P, S, _P, S]
+        lib.ref_qmatrix_info.argtypes = [_P, S, S, C.c_int, C.POINTER(S), _P, _P]
+        lib.ref_qmatvec.argtypes = [C.c_int, S, S, _P, _P, _P, _P, S]
+        lib.ref_qmatvec_time.argtypes = [C.c_int, S, S, _P, _P, _P, _P, S, S,
+                                         C.POINTER(C.c_double)]
+        lib.ref_rmsnorm.argtypes = [_P, _P, _P, S, C.c_float]
+        lib.ref_matvec_threaded.argtypes = [_P, S, S, _P, _P, S]
+        lib.ref_matvec_time.argtypes = [_P, S, S, _P, _P, S, S, C.POINTER(C.c_double)]
+        lib.ref_matmul_threaded.argtypes = [_P, _P, _P, S, S, S, S, S,
+                                            C.POINTER(C.c_double)]
+        lib.ref_model_new.argtypes = [C.POINTER(_I64), C.c_int, C.c_int, C.POINTER(_P)]
+        lib.ref_model_free.argtypes = [_P]
+        lib.ref_model_free.restype = None
+        lib.ref_model_set_embeddings.argtypes = [_P, _P]
+        lib.ref_model_set_final.argtypes = [_P, _P, _P]
+        lib.ref_model_add_layer.argtypes = [_P, C.POINTER(_P), _P, _P]
+        lib.ref_model_storage_bytes.argtypes = [_P, C.POINTER(S)]
+        lib.ref_model_layer_bytes.argtypes = [_P, S, C.c_int, _P, S, _P, S]
+        lib.ref_generate.argtypes = [_P, _P, S, S, S, _P, _P, _P,
+                                     C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        lib.ref_trace.argtypes = [_P, _P, S, S, S, _P]
+        lib.ref_llama2c_generate.argtypes = [C.c_char_p, C.c_int, _P, S, S, _P,
+                                             C.POINTER(S)]
+        self.lib = lib
+
+    def _check(self, status):
+        if status != 0:
+            raise RuntimeError(f"reference status {status}: "
+                               f"{self.lib.ref_last_error().decode()}")
+
+    def quantize(self, w: np.ndarray, qtype: int):
+        w = np.ascontiguousarray(w, np.float32)
+        rows, cols = w.shape
+        n = rows * cols
+        data = np.zeros(n if qtype == 0 else (n + 1) // 2, np.uint8)
+        scales = np.zeros((n + 31) // 32, np.uint16)
+        self._check(self.lib.ref_quantize(_ptr(w), rows, cols, qtype, _ptr(data),
+                                          data.size, _ptr(scales), scales.size))
+        return data, scales
+
+    def quantized_values(self, w: np.ndarray, qtype: int):
+        w = np.ascontiguousarray(w, np.float32)
+        rows, cols = w.shape
+        values = np.empty_like(w)
+        bounds = np.empty_like(w)
+        nbytes = C.c_size_t(0)
+        self._check(self.lib.ref_qmatrix_info(_ptr(w), rows, cols, qtype,
+                                              C.byref(nbytes), _ptr(values),
+                                              _ptr(bounds)))
+        return values, bounds, nbytes.value
+
+    def qmatvec(self, qtype, rows, cols, data, scales, x, threads=1):
+        y = np.empty(rows, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        self._check(self.lib.ref_qmatvec(qtype, rows, cols, _ptr(data), _ptr(scales),
+                                         _ptr(x), _ptr(y), threads))
+        return y
+
+    def qmatvec_time(self, qtype, rows, cols, data, scales, x, threads, reps):
+        y = np.empty(rows, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        sec = C.c_double(0)
+        self._check(self.lib.ref_qmatvec_time(qtype, rows, cols, _ptr(data),
+                                              _ptr(scales), _ptr(x), _ptr(y),
+                                              threads, reps, C.byref(sec)))
+        return sec.value, y
+
+    def rmsnorm(self, x, w, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self._check(self.lib.ref_rmsnorm(_ptr(x), _ptr(np.ascontiguousarray(w, np.float32)),
+                                         _ptr(out), x.size, eps))
+        return out
+
+    def matvec_f32(self, w, x, threads=1):
+        w = np.ascontiguousarray(w, np.float32)
+        y = np.empty(w.shape[0], np.float32)
+        self._check(self.lib.ref_matvec_threaded(_ptr(w), w.shape[0], w.shape[1],
+                                                 _ptr(np.ascontiguousarray(x, np.float32)),
+                                                 _ptr(y), threads))
+        return y
+
+    def model(self, config, qtype: int, seed: int, tied: bool = False,
+              layer_fp32=None, embeddings=None, lm_head=None) -> "RefModel":
+        return RefModel(self, config, qtype, seed, tied, layer_fp32, embeddings,
+                        lm_head)
+
+    def llama2c_generate(self, path: str, qtype: int, prompt, max_tokens: int):
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(max_tokens, np.int32)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_llama2c_generate(path.encode(), qtype, _ptr(p),
+                                                  p.size, max_tokens, _ptr(ids),
+                                                  C.byref(n)))
+        return ids[:n.value]
+
+
+class RefModel:
+    """A QuantizedModelWeights built inside the reference from seeded fp32
+    weights, quantised by the reference's own quantiser."""
+
+    def __init__(self, ref: Reference, c, qtype, seed, tied, layer_fp32=None,
+                 embeddings=None, lm_head=None):
+        from nutllm_b200 import synthetic as syn
+        self.r = ref
+        self.config = c
+        cfg = (_I64 * 9)(*[int(getattr(c, n)) for n, _ in _Config._fields_])
+        h = _P()
+        ref._check(ref.lib.ref_model_new(cfg, qtype, int(tied), C.byref(h)))
+        self.h = h
+        emb = embeddings if embeddings is not None else syn.embeddings_fp32(c, seed)
+        ref._check(ref.lib.ref_model_set_embeddings(h, _ptr(emb)))
+        ones = np.ones(c.dim, np.float32)
+        lm = None if tied else (lm_head if lm_head is not None else syn.lm_head_fp32(c, seed))
+        ref._check(ref.lib.ref_model_set_final(h, _ptr(ones), _ptr(lm)))
+        for layer in range(c.layers):
+            mats = ([layer_fp32(layer, j) for j in range(7)] if layer_fp32
+                    else [syn.projection_fp32(c, seed, layer, j) for j in range(7)])
+            arr = (_P * 7)(*[m.ctypes.data for m in mats])
+            ref._check(ref.lib.ref_model_add_layer(h, arr, _ptr(ones), _ptr(ones)))
+
+    def storage_bytes(self) -> int:
+        n = C.c_size_t(0)
+        self.r._check(self.r.lib.ref_model_storage_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def layer_bytes(self, layer: int, which: int, rows: int, cols: int, qtype: int):
+        n = rows * cols
+        data = np.zeros(n if qtype == 0 else (n + 1) // 2, np.uint8)
+        scales = np.zeros((n + 31) // 32, np.uint16)
+        self.r._check(self.r.lib.ref_model_layer_bytes(self.h, layer, which, _ptr(data),
+                                                       data.size, _ptr(scales), scales.size))
+        return data, scales
+
+    def generate(self, prompt, steps, threads=1, want_logits=True):
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(max(steps, 1), np.int32)
+        lg = (np.empty((max(steps, 1), self.config.vocab_size), np.float32)
+              if want_logits else None)
+        hid = np.empty(self.config.dim, np.float32)
+        ps, ds = C.c_double(0), C.c_double(0)
+        self.r._check(self.r.lib.ref_generate(self.h, _ptr(p), p.size, steps, threads,
+                                              _ptr(ids), _ptr(lg), _ptr(hid),
+                                              C.byref(ps), C.byref(ds)))
+        return ids[:steps], (lg[:steps] if lg is not None else None), hid, ps.value, ds.value
+
+    def trace(self, prompt, steps, threads=1):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.empty((p.size + steps, self.config.dim), np.float32)
+        self.r._check(self.r.lib.ref_trace(self.h, _ptr(p), p.size, steps, threads,
+                                           _ptr(out)))
+        return out
+
+    def __del__(self):
+        try:
+            self.r.lib.ref_model_free(self.h)
+        except Exception:
+            pass

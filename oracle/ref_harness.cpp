@@ -1,0 +1,388 @@
+/* Test infrastructure only — never linked into the product.
+ *
+ * C entry points over the UNMODIFIED reference sources, compiled from where
+ * they lie by oracle/Makefile into oracle/_ref/libnutref.so.  The tests use it
+ * to pin the C restatement (nut_oracle.c) and to generate golden vectors; the
+ * benchmark's reference arm times the reference's own CPU token loop through
+ * it.  Nothing here re-implements reference arithmetic: every number comes
+ * from the reference's own functions.
+ *
+ *   QuantizedMatrix::quantize            src/quant.cpp:154-197
+ *   matvec_quantized_threaded            src/quant.cpp:262-321
+ *   decode_quantized_token               src/quant_model.cpp:158-206
+ *   prefill_quantized                    src/quant_model.cpp:208-220
+ *   greedy loop of generate_tokens_cached src/generate.cpp:195-207 (driven
+ *     directly, without the eos stop, as the parity harness must do)
+ *   matvec_threaded / matmul_threaded    src/threading.cpp:163-198
+ *   load_llama2c_quantized_model         src/llama2.cpp:339-412
+ *
+ * Reading the private byte and scale arrays needs access to QuantizedMatrix
+ * internals, so this translation unit alone compiles quant.hpp with private
+ * members made public (layout unchanged).
+ */
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <limits>
+#include <map>
+#include <memory>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <vector>
+
+#define private public
+#include "quant.hpp"
+#undef private
+#include "generate.hpp"
+#include "kvcache.hpp"
+#include "llama2.hpp"
+#include "matmul.hpp"
+#include "ops.hpp"
+#include "quant_model.hpp"
+
+namespace {
+
+thread_local std::string g_error;
+
+template <typename F> int guarded(F &&body) {
+    try {
+        body();
+        return 0;
+    } catch (const std::invalid_argument &e) {
+        g_error = e.what();
+        return 1;
+    } catch (const std::out_of_range &e) {
+        g_error = e.what();
+        return 2;
+    } catch (const std::length_error &e) {
+        g_error = e.what();
+        return 3;
+    } catch (const std::range_error &e) {
+        g_error = e.what();
+        return 5;
+    } catch (const std::exception &e) {
+        g_error = e.what();
+        return 4;
+    }
+}
+
+QuantType to_type(int t) {
+    if (t == 0)
+        return QuantType::int8;
+    if (t == 1)
+        return QuantType::int4;
+    throw std::invalid_argument("ref harness: unknown quant type");
+}
+
+ModelConfig to_config(const int64_t *c) {
+    ModelConfig config;
+    config.layers = size_t(c[0]);
+    config.heads = size_t(c[1]);
+    config.dim = size_t(c[2]);
+    config.head_dim = size_t(c[3]);
+    config.ffn_dim = size_t(c[4]);
+    config.vocab_size = size_t(c[5]);
+    config.max_seq = size_t(c[6]);
+    config.eos_token = size_t(c[7]);
+    config.kv_heads = size_t(c[8]);
+    return config;
+}
+
+QuantizedMatrix from_bytes(int type, size_t rows, size_t cols,
+                           const uint8_t *data, const uint16_t *scales) {
+    QuantizedMatrix m(rows, cols, 32, to_type(type));
+    std::memcpy(m.data_.data(), data, m.data_.size());
+    std::memcpy(m.scales_.data(), scales, m.scales_.size() * 2);
+    return m;
+}
+
+struct RefModel {
+    std::unique_ptr<QuantizedModelWeights> weights;
+};
+
+/* The greedy token loop of generate_tokens_cached (src/generate.cpp:184-207)
+ * minus the eos stop: final rmsnorm -> fp32 lm_head (matvec_threaded) ->
+ * first-index argmax (std::max_element) -> decode_quantized_token. */
+void greedy(const QuantizedModelWeights &model, const std::vector<int> &prompt,
+            size_t steps, size_t threads, int *ids, float *logits_out,
+            float *prefill_hidden, double *prefill_s, double *decode_s) {
+    KVCache cache(model.config);
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<float> last = prefill_quantized(model, prompt, cache, threads);
+    const auto t1 = std::chrono::steady_clock::now();
+    if (prefill_hidden)
+        std::memcpy(prefill_hidden, last.data(), last.size() * 4);
+    std::vector<float> normalized(model.config.dim);
+    std::vector<float> logits(model.config.vocab_size);
+    for (size_t step = 0; step < steps; step++) {
+        rmsnorm(last.data(), model.final_norm.data(), normalized.data(),
+                model.config.dim, 1e-5f);
+        matvec_threaded(model.output_weights(), normalized.data(),
+                        logits.data(), threads);
+        const size_t token = size_t(
+            std::max_element(logits.begin(), logits.end()) - logits.begin());
+        if (logits_out)
+            std::memcpy(logits_out + step * logits.size(), logits.data(),
+                        logits.size() * 4);
+        ids[step] = int(token);
+        last = decode_quantized_token(model, int(token), cache, threads);
+    }
+    const auto t2 = std::chrono::steady_clock::now();
+    if (prefill_s)
+        *prefill_s = std::chrono::duration<double>(t1 - t0).count();
+    if (decode_s)
+        *decode_s = std::chrono::duration<double>(t2 - t1).count();
+}
+
+} // namespace
+
+extern "C" {
+
+const char *ref_last_error(void) { return g_error.c_str(); }
+
+int ref_quantize(const float *src, size_t rows, size_t cols, int type,
+                 uint8_t *data, size_t data_len, uint16_t *scales,
+                 size_t scales_len) {
+    return guarded([&] {
+        QuantizedMatrix m =
+            QuantizedMatrix::quantize(src, rows, cols, to_type(type));
+        if (m.data_.size() != data_len || m.scales_.size() != scales_len)
+            throw std::invalid_argument("ref harness: output size mismatch");
+        std::memcpy(data, m.data_.data(), data_len);
+        std::memcpy(scales, m.scales_.data(), scales_len * 2);
+    });
+}
+
+int ref_qmatrix_info(const float *src, size_t rows, size_t cols, int type,
+                     size_t *storage_bytes, float *values, float *bounds) {
+    return guarded([&] {
+        QuantizedMatrix m =
+            QuantizedMatrix::quantize(src, rows, cols, to_type(type));
+        *storage_bytes = m.storage_bytes();
+        for (size_t r = 0; r < rows; r++)
+            for (size_t c = 0; c < cols; c++) {
+                if (values)
+                    values[r * cols + c] = m.value(r, c);
+                if (bounds)
+                    bounds[r * cols + c] = m.error_bound(r, c);
+            }
+    });
+}
+
+int ref_qmatvec(int type, size_t rows, size_t cols, const uint8_t *data,
+                const uint16_t *scales, const float *x, float *y,
+                size_t threads) {
+    return guarded([&] {
+        QuantizedMatrix m = from_bytes(type, rows, cols, data, scales);
+        matvec_quantized_threaded(m, x, y, threads);
+    });
+}
+
+/* Times `reps` back-to-back quantised matvecs; returns seconds per call. */
+int ref_qmatvec_time(int type, size_t rows, size_t cols, const uint8_t *data,
+                     const uint16_t *scales, const float *x, float *y,
+                     size_t threads, size_t reps, double *seconds) {
+    return guarded([&] {
+        QuantizedMatrix m = from_bytes(type, rows, cols, data, scales);
+        matvec_quantized_threaded(m, x, y, threads);
+        const auto t0 = std::chrono::steady_clock::now();
+        for (size_t i = 0; i < reps; i++)
+            matvec_quantized_threaded(m, x, y, threads);
+        *seconds = std::chrono::duration<double>(
+                       std::chrono::steady_clock::now() - t0)
+                       .count() /
+                   double(reps);
+    });
+}
+
+int ref_rmsnorm(const float *x, const float *w, float *out, size_t n,
+                float eps) {
+    return guarded([&] { rmsnorm(x, w, out, n, eps); });
+}
+
+int ref_matvec_threaded(const float *w, size_t rows, size_t cols,
+                        const float *x, float *y, size_t threads) {
+    return guarded([&] {
+        Matrix m(rows, cols);
+        std::memcpy(m.data(), w, rows * cols * 4);
+        matvec_threaded(m, x, y, threads);
+    });
+}
+
+int ref_matmul_threaded(const float *a, const float *b, float *c, size_t m,
+                        size_t k, size_t n, size_t threads, size_t reps,
+                        double *seconds) {
+    return guarded([&] {
+        Matrix A(m, k), B(k, n), C(m, n);
+        std::memcpy(A.data(), a, m * k * 4);
+        std::memcpy(B.data(), b, k * n * 4);
+        matmul_threaded(A, B, C, threads);
+        const auto t0 = std::chrono::steady_clock::now();
+        for (size_t i = 0; i < reps; i++)
+            matmul_threaded(A, B, C, threads);
+        if (seconds)
+            *seconds = std::chrono::duration<double>(
+                           std::chrono::steady_clock::now() - t0)
+                           .count() /
+                       double(reps ? reps : 1);
+        std::memcpy(c, C.data(), m * n * 4);
+    });
+}
+
+int ref_matvec_time(const float *w, size_t rows, size_t cols, const float *x,
+                    float *y, size_t threads, size_t reps, double *seconds) {
+    return guarded([&] {
+        Matrix m(rows, cols);
+        std::memcpy(m.data(), w, rows * cols * 4);
+        matvec_threaded(m, x, y, threads);
+        const auto t0 = std::chrono::steady_clock::now();
+        for (size_t i = 0; i < reps; i++)
+            matvec_threaded(m, x, y, threads);
+        *seconds = std::chrono::duration<double>(
+                       std::chrono::steady_clock::now() - t0)
+                       .count() /
+                   double(reps);
+    });
+}
+
+int ref_model_new(const int64_t *config, int type, int tied, void **out) {
+    return guarded([&] {
+        auto model = std::make_unique<RefModel>();
+        model->weights = std::make_unique<QuantizedModelWeights>(
+            to_config(config), to_type(type), tied == 0);
+        model->weights->tied_embeddings = tied != 0;
+        *out = model.release();
+    });
+}
+
+void ref_model_free(void *model) { delete static_cast<RefModel *>(model); }
+
+int ref_model_set_embeddings(void *model, const float *embeddings) {
+    return guarded([&] {
+        auto &w = *static_cast<RefModel *>(model)->weights;
+        std::memcpy(w.embeddings.data(), embeddings, w.embeddings.size() * 4);
+    });
+}
+
+int ref_model_set_final(void *model, const float *final_norm,
+                        const float *lm_head) {
+    return guarded([&] {
+        auto &w = *static_cast<RefModel *>(model)->weights;
+        std::memcpy(w.final_norm.data(), final_norm, w.final_norm.size() * 4);
+        if (!w.tied_embeddings)
+            std::memcpy(w.lm_head.data(), lm_head, w.lm_head.size() * 4);
+    });
+}
+
+/* Adds a layer from fp32 [out][in] projections, quantised by the reference's
+ * own quantiser.  Order of `mats`: q, k, v, o, gate, up, down. */
+int ref_model_add_layer(void *model, const float *const *mats,
+                        const float *attention_norm, const float *ffn_norm) {
+    return guarded([&] {
+        auto &w = *static_cast<RefModel *>(model)->weights;
+        const ModelConfig &c = w.config;
+        const size_t shapes[7][2] = {
+            {c.dim, c.dim},     {c.kv_dim(), c.dim}, {c.kv_dim(), c.dim},
+            {c.dim, c.dim},     {c.ffn_dim, c.dim},  {c.ffn_dim, c.dim},
+            {c.dim, c.ffn_dim}};
+        std::vector<QuantizedMatrix> q;
+        for (int i = 0; i < 7; i++)
+            q.push_back(QuantizedMatrix::quantize(mats[i], shapes[i][0],
+                                                  shapes[i][1], w.quant_type));
+        w.layers.emplace_back(
+            std::move(q[0]), std::move(q[1]), std::move(q[2]), std::move(q[3]),
+            std::move(q[4]), std::move(q[5]), std::move(q[6]),
+            std::vector<float>(attention_norm, attention_norm + c.dim),
+            std::vector<float>(ffn_norm, ffn_norm + c.dim));
+    });
+}
+
+int ref_model_storage_bytes(void *model, size_t *bytes) {
+    return guarded([&] {
+        *bytes = static_cast<RefModel *>(model)->weights->storage_bytes();
+    });
+}
+
+/* Copies out the quantised bytes and fp16 scales of one projection
+ * (which: 0..6 = q k v o gate up down). */
+int ref_model_layer_bytes(void *model, size_t layer, int which, uint8_t *data,
+                          size_t data_len, uint16_t *scales,
+                          size_t scales_len) {
+    return guarded([&] {
+        auto &w = *static_cast<RefModel *>(model)->weights;
+        const QuantizedLayerWeights &l = w.layers.at(layer);
+        const QuantizedMatrix *mats[7] = {&l.query, &l.key,  &l.value,
+                                          &l.output, &l.gate, &l.up,
+                                          &l.down};
+        if (which < 0 || which > 6)
+            throw std::out_of_range("ref harness: projection index");
+        const QuantizedMatrix &m = *mats[which];
+        if (m.data_.size() != data_len || m.scales_.size() != scales_len)
+            throw std::invalid_argument("ref harness: output size mismatch");
+        std::memcpy(data, m.data_.data(), data_len);
+        std::memcpy(scales, m.scales_.data(), scales_len * 2);
+    });
+}
+
+int ref_generate(void *model, const int *prompt, size_t n, size_t steps,
+                 size_t threads, int *ids, float *logits,
+                 float *prefill_hidden, double *prefill_s, double *decode_s) {
+    return guarded([&] {
+        auto &w = *static_cast<RefModel *>(model)->weights;
+        greedy(w, std::vector<int>(prompt, prompt + n), steps, threads, ids,
+               logits, prefill_hidden, prefill_s, decode_s);
+    });
+}
+
+/* Per-token hidden states (pre final norm) of prefill, then `steps` greedy
+ * tokens: out_hidden holds (n + steps) rows of dim floats. */
+int ref_trace(void *model, const int *prompt, size_t n, size_t steps,
+              size_t threads, float *out_hidden) {
+    return guarded([&] {
+        auto &w = *static_cast<RefModel *>(model)->weights;
+        const ModelConfig &c = w.config;
+        KVCache cache(c);
+        std::vector<float> h;
+        for (size_t i = 0; i < n; i++) {
+            h = decode_quantized_token(w, prompt[i], cache, threads);
+            std::memcpy(out_hidden + i * c.dim, h.data(), c.dim * 4);
+        }
+        std::vector<float> normalized(c.dim), logits(c.vocab_size);
+        for (size_t s = 0; s < steps; s++) {
+            rmsnorm(h.data(), w.final_norm.data(), normalized.data(), c.dim,
+                    1e-5f);
+            matvec_threaded(w.output_weights(), normalized.data(),
+                            logits.data(), threads);
+            const int token = int(std::max_element(logits.begin(),
+                                                   logits.end()) -
+                                  logits.begin());
+            h = decode_quantized_token(w, token, cache, threads);
+            std::memcpy(out_hidden + (n + s) * c.dim, h.data(), c.dim * 4);
+        }
+    });
+}
+
+/* The reference's own end-to-end path on a llama2.c checkpoint:
+ * load_llama2c_quantized_model + generate_tokens_cached (greedy, eos stop). */
+int ref_llama2c_generate(const char *path, int type, const int *prompt,
+                         size_t n, size_t max_tokens, int *ids,
+                         size_t *n_out) {
+    return guarded([&] {
+        QuantizedModelWeights model =
+            load_llama2c_quantized_model(path, to_type(type));
+        SamplingConfig sampling;
+        sampling.max_tokens = max_tokens;
+        const std::vector<int> out = generate_tokens_cached(
+            model, std::vector<int>(prompt, prompt + n), sampling);
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = out.size();
+    });
+}
+
+} // extern "C"

@@ -1,0 +1,153 @@
+"""GPU parity of the token loop against the CPU oracle, through the C ABI.
+
+Tolerances: quantised bytes and scales bit-exact;
+per-step fp32 logits within max-abs 2e-3 and relative 1e-3
+(|gpu - oracle| <= 2e-3 + 1e-3 |oracle|); greedy ids identical.
+"""
+import numpy as np
+import pytest
+
+import nutllm_b200 as nb
+from nutllm_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_ATOL = 2e-3
+LOGIT_RTOL = 1e-3
+SEED = 1234
+
+
+def assert_logits_close(got, want):
+    err = np.abs(got - want)
+    bound = LOGIT_ATOL + LOGIT_RTOL * np.abs(want)
+    worst = float((err - bound).max())
+    assert worst <= 0.0, f"logits differ: max abs err {err.max():.3e}"
+
+
+def top2_margin(logits):
+    s = np.sort(logits, axis=-1)
+    return s[..., -1] - s[..., -2]
+
+
+QMATVEC_SHAPES = [(2048, 2048), (5632, 2048), (2048, 5632), (32000, 2048)]
+
+
+@pytest.mark.parametrize("qtype", [nb.INT4, nb.INT8], ids=["int4", "int8"])
+@pytest.mark.parametrize("shape", QMATVEC_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_qmatvec_matches_oracle(gpu, orc, qtype, shape):
+    rows, cols = shape
+    w = nb.synth_normal(SEED, 7, rows * cols, 0.02).reshape(rows, cols)
+    x = nb.synth_normal(SEED, 8, cols, 1.0)
+    q = nb.QuantizedMatrix.quantize(w, qtype)
+    dev = nb.DeviceQMatrix(q, gpu)
+    data, scales = dev.download()
+    assert np.array_equal(data, q.data) and np.array_equal(scales, q.scales)
+    got = dev.matvec(x)
+    want = orc.qmatvec(qtype, rows, cols, q.data, q.scales, x)
+    # bound: fp32 reassociation of the cols products of |q s x|
+    deq_abs = np.abs(_dequantize(q)) @ np.abs(x)
+    assert np.all(np.abs(got - want) <= 2e-6 * deq_abs + 1e-6)
+
+
+def _dequantize(q: nb.QuantizedMatrix) -> np.ndarray:
+    n = q.rows * q.cols
+    if q.qtype == nb.INT8:
+        vals = q.data.view(np.int8).astype(np.float32)
+    else:
+        lo = (q.data & 0x0F).astype(np.int8)
+        hi = (q.data >> 4).astype(np.int8)
+        v = np.empty(q.data.size * 2, np.int8)
+        v[0::2], v[1::2] = lo, hi
+        vals = np.where(v >= 8, v - 16, v)[:n].astype(np.float32)
+    scales = q.scales.view(np.float16).astype(np.float32)
+    return (vals * np.repeat(scales, 32)[:n]).reshape(q.rows, q.cols)
+
+
+def _run(name, orc, gpu, steps=None):
+    wl = syn.WORKLOADS[name]
+    c = wl.model_config()
+    w = syn.build_model(c, wl.qtype, SEED)
+    prompt = syn.prompt_ids(c, SEED, wl.prompt)
+    steps = wl.steps if steps is None else steps
+    om = orc.model(w)
+    ids_o, lg_o, hid_o = om.generate(prompt, steps)
+    model = nb.DeviceModel(w, gpu)
+    kv = nb.KVCache(model)
+    ids_g, lg_g, stats = nb.generate_greedy(model, kv, prompt, steps,
+                                            stop_at_eos=False, want_logits=True)
+    return dict(c=c, w=w, prompt=prompt, ids_o=ids_o, lg_o=lg_o, ids_g=ids_g,
+                lg_g=lg_g, stats=stats, model=model, kv=kv, om=om)
+
+
+def test_tiny_int8_greedy_ids_and_logits(gpu, orc):
+    r = _run("tiny-int8", orc, gpu)
+    assert r["model"].storage_bytes() == r["w"].storage_bytes()
+    assert np.array_equal(r["ids_g"], r["ids_o"])
+    assert_logits_close(r["lg_g"], r["lg_o"])
+    assert r["stats"].generated_tokens == 16
+
+
+def test_tiny_int8_decode_hidden_and_kv(gpu, orc):
+    wl = syn.WORKLOADS["tiny-int8"]
+    c = wl.model_config()
+    w = syn.build_model(c, wl.qtype, SEED)
+    prompt = syn.prompt_ids(c, SEED, wl.prompt)
+    om = orc.model(w)
+    model = nb.DeviceModel(w, gpu)
+    kv = nb.KVCache(model)
+    for i, t in enumerate(prompt):
+        hg = nb.decode_quantized_token(model, int(t), kv)
+        ho = om.decode(int(t))
+        assert kv.length() == i + 1
+        np.testing.assert_allclose(hg, ho, rtol=1e-4, atol=1e-5)
+    kvh = c.kv_heads or c.heads
+    n = c.head_dim
+    for layer in (0, c.layers - 1):
+        for head in (0, kvh - 1):
+            for pos in range(len(prompt)):
+                off = ((layer * kvh + head) * c.max_seq + pos) * n
+                np.testing.assert_allclose(kv.key(layer, head, pos),
+                                           om.keys[off:off + n], rtol=1e-4, atol=1e-5)
+                np.testing.assert_allclose(kv.value(layer, head, pos),
+                                           om.values[off:off + n], rtol=1e-4, atol=1e-5)
+    lg, best = nb.logits(model, kv)
+    lo, bo = om.logits(ho)
+    assert best == bo
+    assert_logits_close(lg, lo)
+
+
+def test_decode_errors_match_reference_classes(gpu):
+    wl = syn.WORKLOADS["tiny-int8"]
+    c = nb.Config(2, 6, 288, 48, 768, 512, 4, 1, 6)
+    w = syn.build_model(c, wl.qtype, SEED)
+    model = nb.DeviceModel(w, gpu)
+    kv = nb.KVCache(model)
+    with pytest.raises(IndexError, match="token out of range"):
+        nb.decode_quantized_token(model, 512, kv)
+    with pytest.raises(IndexError):
+        nb.decode_quantized_token(model, -1, kv)
+    with pytest.raises(ValueError, match="invalid prompt"):
+        nb.prefill_quantized(model, [], kv)
+    with pytest.raises(ValueError, match="invalid prompt"):
+        nb.prefill_quantized(model, [1] * 5, kv)
+    nb.prefill_quantized(model, [1, 2, 3, 4], kv)
+    assert kv.length() == 4
+    with pytest.raises(nb.LengthError, match="context is full"):
+        nb.decode_quantized_token(model, 1, kv)
+    with pytest.raises(ValueError, match="zero threads"):
+        nb.decode_quantized_token(model, 1, kv, thread_count=0)
+    kv.reset()
+    assert kv.length() == 0
+    with pytest.raises(nb.LengthError):
+        kv.set_length(5)
+
+
+@pytest.mark.slow
+def test_tinyllama_int4_greedy_ids_and_logits(gpu, orc):
+    r = _run("tinyllama-int4", orc, gpu)
+    margin = top2_margin(r["lg_o"])
+    assert_logits_close(r["lg_g"], r["lg_o"])
+    # ids must agree wherever the oracle's top-2 gap exceeds the tolerance
+    first_close = next((i for i, m in enumerate(margin) if m < 2 * LOGIT_ATOL),
+                       len(margin))
+    assert np.array_equal(r["ids_g"][:first_close], r["ids_o"][:first_close])
