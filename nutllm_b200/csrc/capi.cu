@@ -9,6 +9,7 @@
  */
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -18,7 +19,9 @@
 #include <cuda_runtime.h>
 
 #include "../../include/nutllm_cuda.h"
+#include "decode_mk.h"
 #include "kernels.h"
+#include "kernels_tc.h"
 
 namespace {
 
@@ -92,6 +95,20 @@ void validate_config(const nut_config &c) {
         raise(NUT_LENGTH_ERROR, "model config: dimensions exceed device limits");
 }
 
+void check_view(const nut_qmatrix_view &v, int64_t rows, int64_t cols, int type,
+                const char *name) {
+    if (v.data == nullptr || v.scales == nullptr)
+        raise(NUT_INVALID_ARGUMENT, std::string("model: null storage for ") + name);
+    if (v.rows != rows || v.cols != cols)
+        raise(NUT_INVALID_ARGUMENT,
+              std::string("quantized decode: shape mismatch for ") + name);
+    if (v.block_size != 32)
+        raise(NUT_INVALID_ARGUMENT, "quantized matrix: block size must be 32");
+    if (v.type != type)
+        raise(NUT_INVALID_ARGUMENT,
+              std::string("quantized decode: quant type mismatch for ") + name);
+}
+
 nut::DevQMatrix upload(const nut_qmatrix_view &v, int64_t rows, int64_t cols,
                        int type, const char *name) {
     if (v.data == nullptr || v.scales == nullptr)
@@ -129,12 +146,104 @@ nut::QSeg seg(const nut::DevQMatrix &m, float *out, int accumulate) {
     return nut::QSeg{m.data, m.scales, int(m.rows), out, accumulate};
 }
 
+/* Packs reference storage into fragment tiles on the device. */
+nut::TileMatrix upload_tiles(const nut_qmatrix_view &v) {
+    nut::TileMatrix t;
+    t.shape = nut::TileShape::of(v.rows, v.cols, v.type);
+    std::vector<uint8_t> data(t.shape.data_bytes());
+    std::vector<uint16_t> scales(t.shape.scale_count());
+    nut::pack_tiles(t.shape, v.data, v.scales, data.data(), scales.data());
+    t.data = dev_alloc<uint8_t>(data.size(), "alloc tiles");
+    t.scales = dev_alloc<uint16_t>(scales.size(), "alloc tile scales");
+    cuda_check(cudaMemcpy(t.data, data.data(), data.size(), cudaMemcpyHostToDevice),
+               "copy tiles");
+    cuda_check(cudaMemcpy(t.scales, scales.data(), scales.size() * 2,
+                          cudaMemcpyHostToDevice),
+               "copy tile scales");
+    return t;
+}
+
+void release(nut::TileMatrix &t) {
+    dev_free(t.data);
+    dev_free(t.scales);
+    t.data = nullptr;
+    t.scales = nullptr;
+}
+
+/* Stacks matrices with equal cols (reference storage, cols % 32 == 0, so
+ * no block spans two of them) and packs the result into fragment tiles. */
+nut::TileMatrix upload_stacked(std::initializer_list<const nut_qmatrix_view *> parts) {
+    const nut_qmatrix_view &first = **parts.begin();
+    int64_t rows = 0;
+    for (const nut_qmatrix_view *v : parts)
+        rows += v->rows;
+    nut_qmatrix_view all = first;
+    all.rows = rows;
+    const int64_t cols = first.cols;
+    std::vector<uint8_t> data;
+    std::vector<uint16_t> scales;
+    for (const nut_qmatrix_view *v : parts) {
+        const size_t n = size_t(v->rows * cols);
+        const size_t nd = first.type == NUT_QUANT_INT8 ? n : n / 2;
+        data.insert(data.end(), v->data, v->data + nd);
+        scales.insert(scales.end(), v->scales, v->scales + n / 32);
+    }
+    all.data = data.data();
+    all.scales = scales.data();
+    return upload_tiles(all);
+}
+
+/* Gate and up projections interleaved in groups of 8 rows, so one 16-row
+ * tile holds gate and up rows of the same 8 hidden units. */
+nut::TileMatrix upload_gate_up(const nut_qmatrix_view &gate, const nut_qmatrix_view &up) {
+    const int64_t ffn = gate.rows, cols = gate.cols;
+    const size_t row_bytes = size_t(gate.type == NUT_QUANT_INT8 ? cols : cols / 2);
+    const size_t row_scales = size_t(cols / 32);
+    std::vector<uint8_t> data(2 * size_t(ffn) * row_bytes);
+    std::vector<uint16_t> scales(2 * size_t(ffn) * row_scales);
+    for (int64_t r = 0; r < 2 * ffn; r++) {
+        const int64_t group = r / 16, within = r % 16;
+        const bool is_up = within >= 8;
+        const int64_t src = group * 8 + (within % 8);
+        const nut_qmatrix_view &v = is_up ? up : gate;
+        std::copy(v.data + src * row_bytes, v.data + (src + 1) * row_bytes,
+                  data.begin() + r * row_bytes);
+        std::copy(v.scales + src * row_scales, v.scales + (src + 1) * row_scales,
+                  scales.begin() + r * row_scales);
+    }
+    nut_qmatrix_view all = gate;
+    all.rows = 2 * ffn;
+    all.data = data.data();
+    all.scales = scales.data();
+    return upload_tiles(all);
+}
+
+/* Device-side error word -> status (bounded waits that gave up). */
+void check_device_error(int *error_dev, cudaStream_t stream) {
+    int code = 0;
+    cuda_check(cudaMemcpyAsync(&code, error_dev, sizeof code, cudaMemcpyDeviceToHost,
+                               stream),
+               "read error word");
+    cuda_check(cudaStreamSynchronize(stream), "synchronize");
+    if (code != 0) {
+        cudaMemsetAsync(error_dev, 0, sizeof(int), stream);
+        cudaStreamSynchronize(stream);
+        raise(NUT_DEVICE_TIMEOUT,
+              "device: bounded wait gave up (code " + std::to_string(code) + ")");
+    }
+}
+
 } // namespace
 
 struct nut_qmatrix {
     int device = 0;
-    nut::DevQMatrix m;
+    int64_t rows = 0, cols = 0;
+    int type = 0;
+    bool tiled = false;
+    nut::DevQMatrix m;  /* reference layout (blocks spanning rows) */
+    nut::TileMatrix t;  /* fragment tiles (cols % 32 == 0) */
     float *x = nullptr, *y = nullptr; /* staging for host-buffer calls */
+    int *error = nullptr;
     cudaStream_t stream = nullptr;
     ~nut_qmatrix() {
         if (stream) {
@@ -142,8 +251,24 @@ struct nut_qmatrix {
             cudaStreamDestroy(stream);
         }
         release(m);
+        release(t);
         dev_free(x);
         dev_free(y);
+        dev_free(error);
+    }
+    void launch(const float *xd, float *yd, cudaStream_t s) {
+        if (tiled) {
+            cuda_check(nut::launch_qmatvec_tc(t, xd, yd, error, nut::kDefaultWaitNs, s),
+                       "qmatvec launch");
+            return;
+        }
+        nut::QSegs q{};
+        q.seg[0] = seg(m, yd, 0);
+        q.count = 1;
+        q.cols = int(cols);
+        q.type = type;
+        nut::launch_qmatvec(q, xd, nullptr, s);
+        cuda_check(cudaGetLastError(), "qmatvec launch");
     }
 };
 
@@ -163,11 +288,21 @@ struct nut_model {
     std::vector<DevLayer> layers;
     uint64_t storage_bytes = 0;
     cudaStream_t stream = nullptr;
+    /* persistent-kernel image (block-aligned shapes) */
+    bool mk = false;
+    int sms = 0;
+    std::vector<nut::MkLayer> mk_layers;
+    nut::MkLayerPtrs *mk_ptrs = nullptr;
+    float *attn_norms = nullptr, *ffn_norms = nullptr; /* [layers][dim] */
     ~nut_model() {
         if (stream) {
             cudaStreamSynchronize(stream);
             cudaStreamDestroy(stream);
         }
+        for (auto &l : mk_layers) {
+            release(l.qkv), release(l.wo), release(l.gu), release(l.down);
+        }
+        dev_free(mk_ptrs), dev_free(attn_norms), dev_free(ffn_norms);
         for (auto &l : layers) {
             release(l.q), release(l.k), release(l.v), release(l.o);
             release(l.gate), release(l.up), release(l.down);
@@ -190,12 +325,24 @@ struct nut_kv {
     int32_t *ids = nullptr; /* [max_seq] generated ids */
     bool has_hidden = false;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    /* persistent-kernel state */
+    nut::Tagged *tagged = nullptr; /* hA | hB | qkv | gu */
+    size_t tagged_count = 0;
+    unsigned long long *mk_keys = nullptr; /* [max_seq] */
+    unsigned int *mk_done = nullptr;       /* [max_seq] */
+    int32_t *mk_prompt = nullptr;          /* [max_seq] */
+    int *mk_error = nullptr;
+    unsigned long long *mk_stamps = nullptr; /* [3] */
+    float *mk_logits = nullptr;
+    size_t mk_logits_cap = 0;
     ~nut_kv() {
         if (model)
             cudaStreamSynchronize(model->stream);
         dev_free(keys), dev_free(values), dev_free(hidden), dev_free(q);
         dev_free(k), dev_free(v), dev_free(ctx), dev_free(gate), dev_free(up);
         dev_free(logits), dev_free(argmax_key), dev_free(ids);
+        dev_free(tagged), dev_free(mk_keys), dev_free(mk_done), dev_free(mk_prompt);
+        dev_free(mk_error), dev_free(mk_stamps), dev_free(mk_logits);
         for (auto e : ev)
             if (e)
                 cudaEventDestroy(e);
@@ -284,6 +431,133 @@ void check_decode_args(nut_model *m, nut_kv *kv, int64_t token) {
 
 void sync(nut_model *m) { cuda_check(cudaStreamSynchronize(m->stream), "synchronize"); }
 
+/* One persistent-kernel launch: decode tokens[0..n_prompt) then greedy
+ * tokens up to n_tokens decode passes in total, starting at start_pos.
+ * Logits (and argmax ids) are produced after passes lfrom..lto.  Leaves
+ * the last hidden vector in kv->hidden. */
+void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
+            int64_t n_tokens, int64_t start_pos, int64_t lfrom, int64_t lto,
+            float *logits_host, int32_t *ids_host, nut_generation_stats *stats) {
+    const nut_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    const int64_t nlog = lto >= lfrom ? lto - lfrom + 1 : 0;
+    if (logits_host != nullptr && nlog > 0 &&
+        kv->mk_logits_cap < size_t(nlog) * size_t(c.vocab_size)) {
+        cuda_check(cudaStreamSynchronize(s), "synchronize");
+        dev_free(kv->mk_logits);
+        kv->mk_logits_cap = size_t(nlog) * size_t(c.vocab_size);
+        kv->mk_logits = dev_alloc<float>(kv->mk_logits_cap, "alloc logits");
+    }
+    cuda_check(cudaMemcpyAsync(kv->mk_prompt, tokens, size_t(n_prompt) * 4,
+                               cudaMemcpyHostToDevice, s),
+               "copy prompt");
+    cuda_check(cudaMemsetAsync(kv->tagged, 0, kv->tagged_count * sizeof(nut::Tagged), s),
+               "clear tags");
+    cuda_check(cudaMemsetAsync(kv->mk_keys, 0, size_t(n_tokens) * 8, s), "clear keys");
+    cuda_check(cudaMemsetAsync(kv->mk_done, 0, size_t(n_tokens) * 4, s), "clear counts");
+    cuda_check(cudaMemsetAsync(kv->mk_error, 0, sizeof(int), s), "clear error");
+    cuda_check(cudaMemsetAsync(kv->mk_stamps, 0, 3 * 8, s), "clear stamps");
+    const int dim = int(c.dim), kvd = int(m->kv_heads * c.head_dim), ffn = int(c.ffn_dim);
+    nut::MkParams p{};
+    p.layers = int(c.layers);
+    p.dim = dim;
+    p.kvd = kvd;
+    p.heads = int(c.heads);
+    p.kv_heads = int(m->kv_heads);
+    p.hd = int(c.head_dim);
+    p.ffn = ffn;
+    p.vocab = int(c.vocab_size);
+    p.max_seq = int(c.max_seq);
+    const nut::MkLayer &L0 = m->mk_layers[0];
+    p.nb_dim = int(L0.qkv.shape.blocks);
+    p.nb_ffn = int(L0.down.shape.blocks);
+    p.rt_qkv = int(L0.qkv.shape.row_tiles);
+    p.rt_wo = int(L0.wo.shape.row_tiles);
+    p.rt_gu = int(L0.gu.shape.row_tiles);
+    p.rt_down = int(L0.down.shape.row_tiles);
+    p.layer = m->mk_ptrs;
+    p.attn_norm = m->attn_norms;
+    p.ffn_norm = m->ffn_norms;
+    p.final_norm = m->final_norm;
+    p.lm_head = m->output_weights();
+    p.emb = m->embeddings;
+    p.rope_cos = m->rope_cos;
+    p.rope_sin = m->rope_sin;
+    p.kcache = kv->keys;
+    p.vcache = kv->values;
+    p.hA = kv->tagged;
+    p.hB = p.hA + dim;
+    p.qkv = p.hB + dim;
+    p.ctx = p.qkv + dim + 2 * kvd;
+    p.act = p.ctx + dim;
+    p.prompt = kv->mk_prompt;
+    p.n_prompt = int(n_prompt);
+    p.n_tokens = int(n_tokens);
+    p.start_pos = int(start_pos);
+    p.logits_from = nlog > 0 ? int(lfrom) : 1 << 30;
+    p.logits_to = nlog > 0 ? int(lto) : -1;
+    p.keys = kv->mk_keys;
+    p.done = kv->mk_done;
+    p.logits = logits_host != nullptr && nlog > 0 ? kv->mk_logits : nullptr;
+    p.error = kv->mk_error;
+    p.stamps = kv->mk_stamps;
+    p.limit_ns = nut::kDefaultWaitNs;
+    /* NUTLLM_TRACE_FILE: record per-CTA phase timestamps and append them
+     * to that file (tracing aid; off by default) */
+    const char *trace_file = std::getenv("NUTLLM_TRACE_FILE");
+    unsigned long long *trace = nullptr;
+    const int stride = int(n_tokens * (5 * c.layers + 1));
+    if (trace_file != nullptr) {
+        trace = dev_alloc<unsigned long long>(size_t(m->sms) * stride * 8, "alloc trace");
+        cuda_check(cudaMemsetAsync(trace, 0, size_t(m->sms) * stride * 64, s), "clear trace");
+        p.trace = trace;
+        p.trace_stride = stride;
+    }
+    cuda_check(nut::launch_decode_mk(p, m->type, m->sms, s), "persistent kernel launch");
+    if (trace != nullptr) {
+        std::vector<unsigned long long> host(size_t(m->sms) * stride * 8);
+        cuda_check(cudaMemcpyAsync(host.data(), trace, host.size() * 8, cudaMemcpyDeviceToHost,
+                                   s),
+                   "copy trace");
+        cuda_check(cudaStreamSynchronize(s), "synchronize");
+        dev_free(trace);
+        if (FILE *f = std::fopen(trace_file, "ab")) {
+            const int32_t hdr[4] = {m->sms, stride, int32_t(n_tokens), int32_t(c.layers)};
+            std::fwrite(hdr, sizeof hdr, 1, f);
+            std::fwrite(host.data(), 8, host.size(), f);
+            std::fclose(f);
+        }
+    }
+    /* last hidden vector: the value halves of hB */
+    cuda_check(cudaMemcpy2DAsync(kv->hidden, sizeof(float), p.hB, sizeof(nut::Tagged),
+                                 sizeof(float), size_t(dim), cudaMemcpyDeviceToDevice, s),
+               "unpack hidden");
+    std::vector<unsigned long long> keys(size_t(nlog > 0 ? nlog : 0));
+    if (ids_host != nullptr && nlog > 0)
+        cuda_check(cudaMemcpyAsync(keys.data(), kv->mk_keys + lfrom, size_t(nlog) * 8,
+                                   cudaMemcpyDeviceToHost, s),
+                   "copy ids");
+    if (p.logits != nullptr)
+        cuda_check(cudaMemcpyAsync(logits_host, kv->mk_logits,
+                                   size_t(nlog) * size_t(c.vocab_size) * 4,
+                                   cudaMemcpyDeviceToHost, s),
+                   "copy logits");
+    unsigned long long st[3] = {0, 0, 0};
+    cuda_check(cudaMemcpyAsync(st, kv->mk_stamps, sizeof st, cudaMemcpyDeviceToHost, s),
+               "copy stamps");
+    check_device_error(kv->mk_error, s);
+    for (size_t k = 0; k < keys.size(); k++)
+        ids_host[k] = int32_t(~uint32_t(keys[k] & 0xffffffffull));
+    kv->length = start_pos + n_tokens;
+    kv->has_hidden = true;
+    if (stats != nullptr) {
+        const double total = st[2] > st[0] ? double(st[2] - st[0]) * 1e-9 : 0.0;
+        const double pre = st[1] > st[0] ? double(st[1] - st[0]) * 1e-9 : total;
+        stats->prefill_seconds = pre;
+        stats->decode_seconds = total - pre;
+    }
+}
+
 } // namespace
 
 extern "C" {
@@ -309,10 +583,23 @@ nut_status nut_qmatrix_create(const nut_qmatrix_view *view, int device,
             raise(NUT_INVALID_ARGUMENT, "quantized matrix: unknown type");
         if (view->rows > (int64_t(1) << 30) || view->cols > (int64_t(1) << 24))
             raise(NUT_LENGTH_ERROR, "quantized matrix: dimensions exceed device limits");
+        if (view->data == nullptr || view->scales == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "quantized matrix: null storage");
+        if (view->block_size != 32)
+            raise(NUT_INVALID_ARGUMENT, "quantized matrix: block size must be 32");
         DeviceScope scope(device);
         auto q = std::make_unique<nut_qmatrix>();
         q->device = device;
-        q->m = upload(*view, view->rows, view->cols, view->type, "matrix");
+        q->rows = view->rows;
+        q->cols = view->cols;
+        q->type = view->type;
+        q->tiled = view->cols % 32 == 0;
+        if (q->tiled)
+            q->t = upload_tiles(*view);
+        else
+            q->m = upload(*view, view->rows, view->cols, view->type, "matrix");
+        q->error = dev_alloc<int>(1, "alloc error word");
+        cuda_check(cudaMemset(q->error, 0, sizeof(int)), "clear error word");
         q->x = dev_alloc<float>(size_t(view->cols), "alloc x");
         q->y = dev_alloc<float>(size_t(view->rows), "alloc y");
         cuda_check(cudaStreamCreateWithFlags(&q->stream, cudaStreamNonBlocking),
@@ -336,6 +623,19 @@ nut_status nut_qmatrix_download(const nut_qmatrix *matrix, uint8_t *data,
         if (matrix == nullptr || data == nullptr || scales == nullptr)
             raise(NUT_INVALID_ARGUMENT, "quantized matrix: null argument");
         DeviceScope scope(matrix->device);
+        if (matrix->tiled) {
+            const nut::TileShape &sh = matrix->t.shape;
+            std::vector<uint8_t> td(sh.data_bytes());
+            std::vector<uint16_t> ts(sh.scale_count());
+            cuda_check(cudaMemcpy(td.data(), matrix->t.data, td.size(),
+                                  cudaMemcpyDeviceToHost),
+                       "download tiles");
+            cuda_check(cudaMemcpy(ts.data(), matrix->t.scales, ts.size() * 2,
+                                  cudaMemcpyDeviceToHost),
+                       "download tile scales");
+            nut::unpack_tiles(sh, td.data(), ts.data(), data, scales);
+            return;
+        }
         cuda_check(cudaMemcpy(data, matrix->m.data, matrix->m.data_bytes(),
                               cudaMemcpyDeviceToHost),
                    "download weights");
@@ -351,14 +651,7 @@ nut_status nut_qmatvec_async(nut_qmatrix *matrix, const float *x_device,
         if (matrix == nullptr || x_device == nullptr || y_device == nullptr)
             raise(NUT_INVALID_ARGUMENT, "quantized matvec: null pointer");
         DeviceScope scope(matrix->device);
-        nut::QSegs s{};
-        s.seg[0] = seg(matrix->m, y_device, 0);
-        s.count = 1;
-        s.cols = int(matrix->m.cols);
-        s.type = matrix->m.type;
-        nut::launch_qmatvec(s, x_device, nullptr,
-                            static_cast<cudaStream_t>(stream));
-        cuda_check(cudaGetLastError(), "qmatvec launch");
+        matrix->launch(x_device, y_device, static_cast<cudaStream_t>(stream));
     });
 }
 
@@ -367,21 +660,15 @@ nut_status nut_qmatvec(nut_qmatrix *matrix, const float *x, float *y) {
         if (matrix == nullptr || x == nullptr || y == nullptr)
             raise(NUT_INVALID_ARGUMENT, "quantized matvec: null pointer");
         DeviceScope scope(matrix->device);
-        const size_t cols = size_t(matrix->m.cols), rows = size_t(matrix->m.rows);
+        const size_t cols = size_t(matrix->cols), rows = size_t(matrix->rows);
         cuda_check(cudaMemcpyAsync(matrix->x, x, cols * 4, cudaMemcpyHostToDevice,
                                    matrix->stream),
                    "copy x");
-        nut::QSegs s{};
-        s.seg[0] = seg(matrix->m, matrix->y, 0);
-        s.count = 1;
-        s.cols = int(cols);
-        s.type = matrix->m.type;
-        nut::launch_qmatvec(s, matrix->x, nullptr, matrix->stream);
-        cuda_check(cudaGetLastError(), "qmatvec launch");
+        matrix->launch(matrix->x, matrix->y, matrix->stream);
         cuda_check(cudaMemcpyAsync(y, matrix->y, rows * 4, cudaMemcpyDeviceToHost,
                                    matrix->stream),
                    "copy y");
-        cuda_check(cudaStreamSynchronize(matrix->stream), "synchronize");
+        check_device_error(matrix->error, matrix->stream);
     });
 }
 
@@ -425,7 +712,64 @@ nut_status nut_model_create(const nut_model_view *view, int device,
                                   cudaMemcpyHostToDevice),
                        "copy lm_head");
         }
-        for (int64_t l = 0; l < c.layers; l++) {
+        int max_smem = 0;
+        cuda_check(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device),
+                   "device attribute");
+        cuda_check(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                          device),
+                   "device attribute");
+        int coop = 0;
+        cuda_check(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device),
+                   "device attribute");
+        m->mk = coop != 0 &&
+                nut::mk_supported(int(c.dim), int(c.ffn_dim), int(kvd), int(c.head_dim),
+                                  int(c.heads), view->quant_type, max_smem);
+        if (m->mk) {
+            std::vector<nut::MkLayerPtrs> ptrs;
+            std::vector<float> an(size_t(c.layers) * dim), fn(size_t(c.layers) * dim);
+            for (int64_t l = 0; l < c.layers; l++) {
+                const nut_layer_view &lv = view->layers[l];
+                if (lv.attention_norm == nullptr || lv.ffn_norm == nullptr)
+                    raise(NUT_INVALID_ARGUMENT, "model: null norm weights");
+                const int t = view->quant_type;
+                check_view(lv.query, c.dim, c.dim, t, "query");
+                check_view(lv.key, kvd, c.dim, t, "key");
+                check_view(lv.value, kvd, c.dim, t, "value");
+                check_view(lv.output, c.dim, c.dim, t, "output");
+                check_view(lv.gate, c.ffn_dim, c.dim, t, "gate");
+                check_view(lv.up, c.ffn_dim, c.dim, t, "up");
+                check_view(lv.down, c.dim, c.ffn_dim, t, "down");
+                m->mk_layers.emplace_back();
+                nut::MkLayer &d = m->mk_layers.back();
+                d.qkv = upload_stacked({&lv.query, &lv.key, &lv.value});
+                d.wo = upload_tiles(lv.output);
+                d.gu = upload_gate_up(lv.gate, lv.up);
+                d.down = upload_tiles(lv.down);
+                ptrs.push_back({d.qkv.data, d.wo.data, d.gu.data, d.down.data,
+                                d.qkv.scales, d.wo.scales, d.gu.scales, d.down.scales});
+                for (const nut_qmatrix_view *q : {&lv.query, &lv.key, &lv.value, &lv.output,
+                                                  &lv.gate, &lv.up, &lv.down}) {
+                    const size_t n = size_t(q->rows * q->cols);
+                    bytes += (t == NUT_QUANT_INT8 ? n : (n + 1) / 2) + (n + 31) / 32 * 2;
+                }
+                std::copy(lv.attention_norm, lv.attention_norm + dim, an.begin() + l * dim);
+                std::copy(lv.ffn_norm, lv.ffn_norm + dim, fn.begin() + l * dim);
+                bytes += 2 * dim * 4;
+            }
+            m->mk_ptrs = dev_alloc<nut::MkLayerPtrs>(ptrs.size(), "alloc layer table");
+            cuda_check(cudaMemcpy(m->mk_ptrs, ptrs.data(), ptrs.size() * sizeof(ptrs[0]),
+                                  cudaMemcpyHostToDevice),
+                       "copy layer table");
+            m->attn_norms = dev_alloc<float>(an.size(), "alloc norms");
+            m->ffn_norms = dev_alloc<float>(fn.size(), "alloc norms");
+            cuda_check(cudaMemcpy(m->attn_norms, an.data(), an.size() * 4,
+                                  cudaMemcpyHostToDevice),
+                       "copy norms");
+            cuda_check(cudaMemcpy(m->ffn_norms, fn.data(), fn.size() * 4,
+                                  cudaMemcpyHostToDevice),
+                       "copy norms");
+        }
+        for (int64_t l = 0; !m->mk && l < c.layers; l++) {
             const nut_layer_view &lv = view->layers[l];
             if (lv.attention_norm == nullptr || lv.ffn_norm == nullptr)
                 raise(NUT_INVALID_ARGUMENT, "model: null norm weights");
@@ -520,6 +864,16 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
         kv->ids = dev_alloc<int32_t>(size_t(c.max_seq), "alloc ids");
         for (auto &e : kv->ev)
             cuda_check(cudaEventCreate(&e), "create event");
+        if (model->mk) {
+            kv->tagged_count = size_t(2 * c.dim) + size_t(c.dim) + 2 * kvd +
+                               size_t(c.dim) + size_t(c.ffn_dim);
+            kv->tagged = dev_alloc<nut::Tagged>(kv->tagged_count, "alloc tagged");
+            kv->mk_keys = dev_alloc<unsigned long long>(size_t(c.max_seq), "alloc keys");
+            kv->mk_done = dev_alloc<unsigned int>(size_t(c.max_seq), "alloc counts");
+            kv->mk_prompt = dev_alloc<int32_t>(size_t(c.max_seq), "alloc prompt");
+            kv->mk_error = dev_alloc<int>(1, "alloc error word");
+            kv->mk_stamps = dev_alloc<unsigned long long>(3, "alloc stamps");
+        }
         *out = kv.release();
     });
 }
@@ -598,7 +952,12 @@ nut_status nut_decode_token(nut_model *model, nut_kv *kv, int32_t token,
     return guarded([&] {
         check_decode_args(model, kv, token);
         DeviceScope scope(model->device);
-        enqueue_decode(model, kv, token, 0);
+        if (model->mk) {
+            const int32_t t = token;
+            run_mk(model, kv, &t, 1, 1, kv->length, 1, 0, nullptr, nullptr, nullptr);
+        } else {
+            enqueue_decode(model, kv, token, 0);
+        }
         if (hidden != nullptr) {
             cuda_check(cudaMemcpyAsync(hidden, kv->hidden, model->cfg.dim * 4,
                                        cudaMemcpyDeviceToHost, model->stream),
@@ -618,9 +977,16 @@ nut_status nut_prefill(nut_model *model, nut_kv *kv, const int32_t *tokens,
         kv->length = 0;
         kv->has_hidden = false;
         DeviceScope scope(model->device);
-        for (int64_t i = 0; i < n; i++) {
-            check_decode_args(model, kv, tokens[i]);
-            enqueue_decode(model, kv, tokens[i], 0);
+        for (int64_t i = 0; i < n; i++)
+            if (tokens[i] < 0 || tokens[i] >= model->cfg.vocab_size)
+                raise(NUT_OUT_OF_RANGE, "quantized decode: token out of range");
+        if (model->mk) {
+            run_mk(model, kv, tokens, n, n, 0, 1, 0, nullptr, nullptr, nullptr);
+        } else {
+            for (int64_t i = 0; i < n; i++) {
+                check_decode_args(model, kv, tokens[i]);
+                enqueue_decode(model, kv, tokens[i], 0);
+            }
         }
         if (hidden != nullptr)
             cuda_check(cudaMemcpyAsync(hidden, kv->hidden, model->cfg.dim * 4,
@@ -674,6 +1040,33 @@ nut_status nut_generate_greedy(nut_model *model, nut_kv *kv,
         cudaStream_t s = model->stream;
         kv->length = 0;
         kv->has_hidden = false;
+        if (model->mk) {
+            /* one launch: the prompt, then every greedy step (logits and
+             * argmax after passes n-1 .. n+steps-2; the last pass decodes
+             * the last chosen token, as the reference loop does) */
+            const int64_t steps = std::min<int64_t>(max_tokens, c.max_seq - n);
+            std::vector<int32_t> chosen(size_t(std::max<int64_t>(steps, 1)));
+            run_mk(model, kv, prompt, n, n + steps, 0, n - 1, n + steps - 2, logits,
+                   chosen.data(), stats);
+            int64_t produced = steps;
+            if (stop_at_eos) {
+                for (int64_t k = 0; k < steps; k++)
+                    if (chosen[size_t(k)] == c.eos_token) {
+                        produced = k;
+                        break;
+                    }
+                /* the reference decodes exactly the emitted tokens */
+                kv->length = n + produced;
+            }
+            std::copy(chosen.begin(), chosen.begin() + produced, ids);
+            if (n_generated != nullptr)
+                *n_generated = produced;
+            if (stats != nullptr) {
+                stats->prefill_tokens = n;
+                stats->generated_tokens = produced;
+            }
+            return;
+        }
         cuda_check(cudaEventRecord(kv->ev[0], s), "event");
         for (int64_t i = 0; i < n; i++)
             enqueue_decode(model, kv, prompt[i], 0);

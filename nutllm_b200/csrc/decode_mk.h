@@ -1,0 +1,65 @@
+#pragma once
+/* The persistent token-loop kernel (one launch per generation). */
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "kernels_tc.h"
+
+namespace nut {
+
+/* Weights of one layer in fragment tiles. */
+struct MkLayer {
+    TileMatrix qkv;  /* [dim + 2 kv_dim][dim]: query, key, value rows */
+    TileMatrix wo;   /* [dim][dim] */
+    TileMatrix gu;   /* [2 ffn][dim]: gate and up rows interleaved in groups
+                        of 8 (a 16-row tile = gate 8t..8t+7, up 8t..8t+7) */
+    TileMatrix down; /* [dim][ffn] */
+};
+
+/* Device-side view of a layer (pointers only). */
+struct MkLayerPtrs {
+    const uint8_t *qkv, *wo, *gu, *down;
+    const uint16_t *qkv_s, *wo_s, *gu_s, *down_s;
+};
+
+/* Cross-CTA tagged vector element: value bits in .x, tag in .y, written and
+ * read as one 64-bit access. */
+using Tagged = uint2;
+
+struct MkParams {
+    int layers, dim, kvd, heads, kv_heads, hd, ffn, vocab, max_seq;
+    int nb_dim, nb_ffn;                 /* padded blocks of K = dim / ffn */
+    int rt_qkv, rt_wo, rt_gu, rt_down;  /* row tiles per matrix */
+    const MkLayerPtrs *layer;           /* [layers] */
+    const float *attn_norm, *ffn_norm;  /* [layers][dim] */
+    const float *final_norm;            /* [dim] */
+    const float *lm_head;               /* [vocab][dim] (embeddings if tied) */
+    const float *emb;                   /* [vocab][dim] */
+    const float *rope_cos, *rope_sin;   /* [max_seq][hd / 2] */
+    float *kcache, *vcache;             /* [layers][kv_heads][max_seq][hd] */
+    Tagged *hA, *hB, *qkv, *ctx, *act;  /* tagged vectors */
+    const int *prompt;                  /* [n_prompt] */
+    int n_prompt, n_tokens, start_pos;
+    int logits_from, logits_to;         /* lm_head after tokens in [from, to] */
+    unsigned long long *keys;           /* [n_tokens] argmax keys */
+    unsigned int *done;                 /* [n_tokens] CTAs done with lm_head */
+    float *logits;                      /* [to - from + 1][vocab] or null */
+    int *error;
+    unsigned long long *stamps;         /* [3] start, prefill done, end (ns) */
+    unsigned long long *trace;          /* optional [ctas][trace_stride][4]:
+                                           phase id, start, inputs ready, end */
+    int trace_stride;
+    uint64_t limit_ns;
+    int att_chunk;                      /* positions per attention chunk */
+    int union_floats;                   /* floats in the digits/attention union */
+};
+
+/* Launches the kernel cooperatively on `stream`.  Returns the launch
+ * status; device-side failures land in *p.error. */
+cudaError_t launch_decode_mk(const MkParams &p, int type, int sms, cudaStream_t stream);
+
+/* Whether a model shape can run the persistent kernel on this device. */
+bool mk_supported(int dim, int ffn, int kvd, int head_dim, int heads, int type,
+                  int max_smem);
+
+} // namespace nut

@@ -49,6 +49,45 @@ def test_qmatvec_matches_oracle(gpu, orc, qtype, shape):
     assert np.all(np.abs(got - want) <= 2e-6 * deq_abs + 1e-6)
 
 
+ODD_SHAPES = [(5, 37), (1, 33), (7, 64), (17, 96), (33, 288), (3, 4)]
+
+
+@pytest.mark.parametrize("qtype", [nb.INT4, nb.INT8], ids=["int4", "int8"])
+@pytest.mark.parametrize("shape", ODD_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_qmatvec_edge_shapes(gpu, orc, qtype, shape):
+    """Row counts off the 16-row tile, block counts off the block pair, and
+    blocks spanning rows (cols % 32 != 0) all match the oracle."""
+    rows, cols = shape
+    w = nb.synth_normal(SEED, 9, rows * cols, 0.5).reshape(rows, cols)
+    x = nb.synth_normal(SEED, 10, cols, 1.0)
+    q = nb.QuantizedMatrix.quantize(w, qtype)
+    dev = nb.DeviceQMatrix(q, gpu)
+    data, scales = dev.download()
+    assert np.array_equal(data, q.data) and np.array_equal(scales, q.scales)
+    got = dev.matvec(x)
+    want = orc.qmatvec(qtype, rows, cols, q.data, q.scales, x)
+    deq_abs = np.abs(_dequantize(q)) @ np.abs(x)
+    assert np.all(np.abs(got - want) <= 2e-6 * deq_abs + 1e-6)
+
+
+def test_qmatvec_zero_and_extreme_blocks(gpu, orc):
+    """All-zero blocks (scale 2^-24) and blocks whose activations span many
+    binades quantise and multiply exactly like the oracle."""
+    rows, cols = 32, 128
+    w = nb.synth_normal(SEED, 11, rows * cols, 0.02).reshape(rows, cols)
+    w[:, 32:64] = 0.0
+    w[3, :] *= 1e4
+    x = nb.synth_normal(SEED, 12, cols, 1.0)
+    x[64:96] *= np.logspace(-30, 3, 32).astype(np.float32)
+    x[96:128] = 0.0
+    for qtype in (nb.INT4, nb.INT8):
+        q = nb.QuantizedMatrix.quantize(w, qtype)
+        got = nb.DeviceQMatrix(q, gpu).matvec(x)
+        want = orc.qmatvec(qtype, rows, cols, q.data, q.scales, x)
+        deq_abs = np.abs(_dequantize(q)) @ np.abs(x)
+        assert np.all(np.abs(got - want) <= 2e-6 * deq_abs + 1e-6)
+
+
 def _dequantize(q: nb.QuantizedMatrix) -> np.ndarray:
     n = q.rows * q.cols
     if q.qtype == nb.INT8:
