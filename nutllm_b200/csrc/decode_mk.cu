@@ -109,6 +109,7 @@ struct Shared {
 struct Trace {
     unsigned long long *rec = nullptr;
     __device__ __forceinline__ void open(const MkParams &p, int occ, int id) {
+        waited = 0;
         rec = p.trace != nullptr && occ < p.trace_stride
                   ? p.trace + (size_t(blockIdx.x) * p.trace_stride + occ) * 8
                   : nullptr;
@@ -122,6 +123,15 @@ struct Trace {
     __device__ __forceinline__ void mark(int slot) const {
         if (rec != nullptr && threadIdx.x == 0)
             rec[slot] = clock64();
+    }
+    /* slot 3 of consume phases: cycles warp 0 waited for weight stages */
+    long long waited = 0;
+    __device__ __forceinline__ long long *wait_acc() {
+        return rec != nullptr && threadIdx.x == 0 ? &waited : nullptr;
+    }
+    __device__ __forceinline__ void put_wait() const {
+        if (rec != nullptr && threadIdx.x == 0)
+            rec[3] = (unsigned long long)waited;
     }
 };
 
@@ -424,7 +434,7 @@ __device__ __forceinline__ float norm_scale(const Shared &s, int n) {
 /* ---------------------------------------------------------------- phases */
 
 template <int TYPE, int STAGES>
-__device__ bool phase_qkv(const Shared &s, const MkParams &p, const Trace &tr, Cursor &cur,
+__device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                           RowReduce &rr, int i, int l, int token, int pos) {
     int a, b;
     share(p.rt_qkv, a, b);
@@ -473,8 +483,10 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, const Trace &tr, C
         }
     };
     const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi);
+                                                 threadIdx.x >> 5, kBar, epi,
+                                                 tr.wait_acc());
     tr.mark(5);
+    tr.put_wait();
     return healthy(s) && ok;
 }
 
@@ -543,7 +555,7 @@ __device__ __forceinline__ float cmax(const Shared &s, float v) {
  * (attention_step, src/quant_model.cpp:68-105: scores q.k / sqrt(hd),
  * exp(score - max), weights / total, context); the context of head h is
  * published as tagged elements ctx[h hd .. h hd + hd). */
-__device__ bool phase_att(const Shared &s, const MkParams &p, const Trace &tr, int i, int l,
+__device__ bool phase_att(const Shared &s, const MkParams &p, Trace &tr, int i, int l,
                           int pos) {
     const int H = p.heads, hd = p.hd, ld = hd + 1, G = p.heads / p.kv_heads;
     const uint32_t tag_in = tag_of(p, i, l, 0), tag = tag_of(p, i, l, 1);
@@ -671,7 +683,7 @@ __device__ __forceinline__ void res_park(const Shared &s, const MkParams &p,
 }
 
 template <int TYPE, int STAGES>
-__device__ bool phase_wo(const Shared &s, const MkParams &p, const Trace &tr, Cursor &cur,
+__device__ bool phase_wo(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                          RowReduce &rr, int i, int l, int token) {
     int a, b;
     share(p.rt_wo, a, b);
@@ -708,13 +720,15 @@ __device__ bool phase_wo(const Shared &s, const MkParams &p, const Trace &tr, Cu
         st_relaxed(p.hA + row, h + y, tag);
     };
     const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi);
+                                                 threadIdx.x >> 5, kBar, epi,
+                                                 tr.wait_acc());
     tr.mark(5);
+    tr.put_wait();
     return healthy(s) && ok;
 }
 
 template <int TYPE, int STAGES>
-__device__ bool phase_gu(const Shared &s, const MkParams &p, const Trace &tr, Cursor &cur,
+__device__ bool phase_gu(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                          RowReduce &rr, int i, int l) {
     int a, b;
     share(p.rt_gu, a, b);
@@ -741,13 +755,15 @@ __device__ bool phase_gu(const Shared &s, const MkParams &p, const Trace &tr, Cu
             st_relaxed(p.act + (a + rt) * 8 + lane, y / (1.0f + expf(-y)) * up, tag);
     };
     const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi);
+                                                 threadIdx.x >> 5, kBar, epi,
+                                                 tr.wait_acc());
     tr.mark(5);
+    tr.put_wait();
     return healthy(s) && ok;
 }
 
 template <int TYPE, int STAGES>
-__device__ bool phase_down(const Shared &s, const MkParams &p, const Trace &tr, Cursor &cur,
+__device__ bool phase_down(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                            RowReduce &rr, int i, int l) {
     int a, b;
     share(p.rt_down, a, b);
@@ -779,8 +795,10 @@ __device__ bool phase_down(const Shared &s, const MkParams &p, const Trace &tr, 
         st_relaxed(p.hB + row, h + y, tag);
     };
     const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi);
+                                                 threadIdx.x >> 5, kBar, epi,
+                                                 tr.wait_acc());
     tr.mark(5);
+    tr.put_wait();
     return healthy(s) && ok;
 }
 
@@ -789,7 +807,7 @@ __device__ __forceinline__ int lm_rows_per_chunk(const MkParams &p) {
 }
 
 template <int STAGES>
-__device__ bool phase_lmhead(const Shared &s, const MkParams &p, const Trace &tr, Cursor &cur,
+__device__ bool phase_lmhead(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                              int i) {
     int a, b;
     share(p.vocab, a, b);

@@ -395,7 +395,8 @@ __device__ __forceinline__ void flush_rows(float (&sg)[kRowBatch], float (&sg8)[
 template <int TYPE, int WARPS, int STAGES, typename Epi>
 __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
                             const int8_t *dig, const float *fac, RowReduce &rr,
-                            int w, int barrier_id, Epi &&epi) {
+                            int w, int barrier_id, Epi &&epi,
+                            long long *wait_cycles = nullptr) {
     using G = TileGeom<TYPE>;
     const int lane = threadIdx.x & 31;
     float ya = 0.0f, ya8 = 0.0f, yb = 0.0f, yb8 = 0.0f;
@@ -411,11 +412,14 @@ __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
         const int n = min(G::kChunkTiles, run.tiles - t);
         if (!poisoned)
             poisoned = *reinterpret_cast<volatile int *>(ring.fatal) != 0;
+        const long long w0 = wait_cycles != nullptr ? clock64() : 0;
         if (!poisoned && !mbar_wait(&ring.full[cur.stage], cur.parity, ring.limit_ns)) {
             report(ring.error, kErrTimeoutFull);
             *reinterpret_cast<volatile int *>(ring.fatal) = 1;
             poisoned = true;
         }
+        if (wait_cycles != nullptr)
+            *wait_cycles += clock64() - w0;
         const uint8_t *sd = ring.data + size_t(cur.stage) * kStageBytes;
         const uint16_t *ss = ring.scales + size_t(cur.stage) * (kStageScaleBytes / 2);
         const int end = t + n;
