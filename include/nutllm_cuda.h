@@ -159,6 +159,36 @@ nut_status nut_generate_greedy(nut_model *model, nut_kv *kv,
                                int32_t *ids, int64_t *n_generated,
                                float *logits, nut_generation_stats *stats);
 
+/* ---- Greedy head without allocation ------------------------------------ */
+
+/* Largest batch of nut_greedy_head_static. */
+#define NUT_GREEDY_HEAD_MAX_BATCH 64
+
+/* Final rmsnorm + fp32 classifier + first-index argmax of `batch` hidden
+ * vectors, with every buffer in caller-provided DEVICE memory and no
+ * allocation of any kind.  It is for callers that cannot call cudaMalloc
+ * or cudaFree: code whose device memory is handed out by a host runtime's
+ * own arena, or that issues GPU work where allocating is not allowed, and
+ * which therefore cannot create the nut_model / nut_kv objects whose
+ * buffers the rest of this ABI owns.  The kernels' only scratch, one
+ * 64-bit argmax accumulator per batch row, is a fixed array of
+ * NUT_GREEDY_HEAD_MAX_BATCH entries in this library's device memory, which
+ * every GPU that loads the library keeps until the process exits; a larger
+ * batch fails with NUT_LENGTH_ERROR.  The first call on a device resolves
+ * the array's address (with that device current) and should come before
+ * any stream capture.  Every call shares the array and clears the rows it
+ * uses: calls whose work overlaps on the GPU race, so the caller must
+ * serialise them.
+ *   hidden [batch][dim], final_norm [dim], weights [vocab][dim] (fp32),
+ *   logits [batch][vocab] (may be NULL), argmax [batch] (int32);
+ *   enqueued on `stream` (a cudaStream_t, NULL = legacy default stream).
+ * No counterpart in the reference, whose greedy head runs on host vectors
+ * (src/generate.cpp:197-201); nut_logits is the model-handle form. */
+nut_status nut_greedy_head_static(const float *hidden, const float *final_norm,
+                                  const float *weights, int64_t batch, int64_t vocab,
+                                  int64_t dim, float *logits, int32_t *argmax,
+                                  void *stream);
+
 #ifdef __cplusplus
 }
 #endif

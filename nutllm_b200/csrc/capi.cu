@@ -27,6 +27,12 @@ namespace {
 
 thread_local std::string g_error;
 
+} // namespace
+
+void nut::set_last_error(const std::string &message) { g_error = message; }
+
+namespace {
+
 struct Failure {
     nut_status status;
     std::string message;

@@ -4,7 +4,12 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <string>
+
 namespace nut {
+
+/* Sets the calling thread's message returned by nut_last_error(). */
+void set_last_error(const std::string &message);
 
 /* One quantised matrix in the reference storage layout on the device. */
 struct DevQMatrix {
