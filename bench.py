@@ -6,13 +6,17 @@ weights N(0, 0.02), a 5-token prompt and 16 greedy decode steps, batch 1.
 One step = one generation (prefill of the prompt + 16 greedy tokens), the
 whole loop on the device.
 
-  value     decode tok/s of the device-resident loop (CUDA events on the
-            library's stream), prompt and weights already in HBM
+  value     decode tok/s of the device-resident loop, weights already in
+            HBM (each generation timed with CUDA events on the library's
+            stream; the prefill/decode split inside the one launch from the
+            kernel's device-timer stamps)
   e2e       generated tok/s through the C ABI call a user makes
             (nut_generate_greedy: prompt from host memory in, ids out)
-  roofline  the dominant kernel against the measured HBM copy bandwidth
+  roofline  the dominant kernel (the persistent token loop, one launch per
+            generation) against the measured HBM copy bandwidth
+  qmatvec   microbenchmark: the quantised matvec at the BASELINE shapes
   cpu_baseline  the reference's own CPU token loop (oracle/_ref) on this
-            host, on a bounded sample of the same workload
+            host, all threads, on the whole workload once
 
 `--impl reference` times the reference CPU implementation instead.
 Multi-GPU: batch-1 decode of a model that fits one GPU does not shard;
@@ -45,6 +49,8 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="tinyllama-int4")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-micro", action="store_true",
+                   help="skip the qmatvec microbenchmark")
     return p.parse_args()
 
 
@@ -128,6 +134,7 @@ def measured_peaks():
 
 
 def run_ours(args, rank, world, local):
+    import torch
     import nutllm_b200 as nb
     from nutllm_b200 import synthetic as syn
 
@@ -135,141 +142,185 @@ def run_ours(args, rank, world, local):
     c = wl.model_config()
     w = syn.build_model(c, wl.qtype, SEED)
     prompt = syn.prompt_ids(c, SEED, wl.prompt)
+    torch.cuda.set_device(local)
     model = nb.DeviceModel(w, local)
     kv = nb.KVCache(model)
+    # the library enqueues every generation on its model's own stream: the
+    # CUDA events that time it are recorded on that stream
+    lib_stream = torch.cuda.ExternalStream(model.stream, device=local)
 
     def step():
         ids, _, st = nb.generate_greedy(model, kv, prompt, wl.steps,
                                         stop_at_eos=False)
         return ids, st
 
-    for _ in range(max(args.warmup, 3)):
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
         ids, _ = step()
 
     barrier = _barrier(world)
+    events = []
+    dec_s, pre_s = 0.0, 0.0
     barrier()
-    dec_s, pre_s, wall = 0.0, 0.0, 0.0
+    torch.cuda.synchronize(local)
+    launches0 = nb.launch_count()
     with Clocks(local) as clocks:
         t0 = time.perf_counter()
         for _ in range(args.steps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(lib_stream)
             ids, st = step()
+            b.record(lib_stream)
+            events.append((a, b))
             dec_s += st.decode_seconds
             pre_s += st.prefill_seconds
+        torch.cuda.synchronize(local)
         wall = time.perf_counter() - t0
+    launches = nb.launch_count() - launches0
     barrier()
+    step_s = sum(a.elapsed_time(b) for a, b in events) * 1e-3
+    step_s = _max_over_ranks(step_s, world)
     dec_s = _max_over_ranks(dec_s, world)
     pre_s = _max_over_ranks(pre_s, world)
     wall = _max_over_ranks(wall, world)
 
-    decoded = wl.steps * args.steps * world
-    value = decoded / dec_s
+    value = wl.steps * args.steps * world / dec_s
     prefill_tps = wl.prompt * args.steps * world / pre_s
     e2e = wl.steps * args.steps * world / wall
 
-    roofline = qmatvec_roofline(nb, local) if rank == 0 else None
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(wl, c)
-    # kernels per generation step (v1: 7 per layer + embed per token,
-    # lm_head + argmax reset per generated token)
-    per_token = 7 * c.layers + 1
-    launches = args.steps * ((wl.prompt + wl.steps) * per_token + 2 * wl.steps)
-    if rank == 0:
-        line = {
-            "metric": "decode tok/s (TinyLlama-1.1B INT4, batch 1)",
-            "value": round(value, 2),
-            "unit": "tok/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": max(args.warmup, 3),
-            "ms_per_step": round(1e3 * (dec_s + pre_s) / args.steps, 4),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "int4xfp32",
-            "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
-            "config": {"workload": wl.name, "prompt": wl.prompt,
-                       "decode_steps": wl.steps, "batch": wl.batch,
-                       "parallelism": f"replicas{world}",
-                       "l2": "inputs larger than L2 (807 MB of weights per token)"},
-            "prefill_tok_s": round(prefill_tps, 2),
-            "e2e": {"value": round(e2e, 2),
-                    "unit": "generated tok/s via nut_generate_greedy (incl. prefill)",
-                    "h2d_bytes_per_step": int(prompt.nbytes),
-                    "d2h_bytes_per_step": int(wl.steps * 4)},
-            "gpu_launches": int(launches),
-            "roofline": roofline,
-            "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
-        }
-        print(json.dumps(line), flush=True)
-
-
-def qmatvec_roofline(nb, device):
-    """Dominant kernel: the quantised matvec at the gate/up shape, timed with
-    CUDA events on the stream it is launched on."""
-    import torch
-    rows, cols = 5632, 2048
-    w = nb.synth_normal(SEED, 7, rows * cols, 0.02).reshape(rows, cols)
-    q = nb.QuantizedMatrix.quantize(w, nb.INT4)
-    dev = nb.DeviceQMatrix(q, device)
-    torch.cuda.set_device(device)
-    x = torch.randn(cols, device=f"cuda:{device}")
-    y = torch.empty(rows, device=f"cuda:{device}")
-    s = torch.cuda.current_stream()
-    for _ in range(10):
-        dev.matvec_async(x.data_ptr(), y.data_ptr(), s.cuda_stream)
-    reps = 200
-    # read (not write) a buffer larger than L2 between launches, so the
-    # timed kernel finds the weights in HBM and no dirty lines to evict
-    flush = torch.ones(512 << 20, dtype=torch.uint8, device=x.device)
-    times = []
-    for _ in range(reps):
-        flush.sum()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(s)
-        dev.matvec_async(x.data_ptr(), y.data_ptr(), s.cuda_stream)
-        b.record(s)
-        b.synchronize()
-        times.append(a.elapsed_time(b) * 1e-3)
-    t = statistics.median(times)
-    bytes_ = rows * cols // 2 + 2 * (rows * cols // 32) + 4 * cols + 4 * rows
+    if rank != 0:
+        return
+    per_launch = syn.algorithmic_generation_bytes(c, wl.qtype, wl.prompt, wl.steps)
+    launch_s = step_s / args.steps
     peak, src = measured_peaks()
-    ach = bytes_ / t / 1e9
-    return {"kernel": "qmatvec_kernel<int4> 5632x2048", "bound": "hbm",
-            "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(ach / peak, 4), "peak_source": src,
-            "bytes_per_launch": bytes_, "us_per_launch": round(t * 1e6, 3),
-            "traffic": None}
+    ach = per_launch / launch_s / 1e9
+    roofline = {
+        "kernel": "decode_mk_kernel (persistent token loop, one launch per "
+                  "generation: %d passes, %d classifier reads)"
+                  % (wl.prompt + wl.steps, wl.steps),
+        "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+        "unit": "GB/s", "frac": round(ach / peak, 4), "peak_source": src,
+        "algorithmic_bytes_per_launch": per_launch,
+        "ms_per_launch": round(launch_s * 1e3, 4),
+        "traffic": NCU_TRAFFIC.get(wl.name),
+    }
+    micro = None if args.no_micro else qmatvec_micro(nb, local, peak)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(wl, c)
+    line = {
+        "metric": "decode tok/s (TinyLlama-1.1B INT4, batch 1)",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": warmup,
+        "ms_per_step": round(1e3 * step_s / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4xfp32",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
+        "config": {"workload": wl.name, "prompt": wl.prompt,
+                   "decode_steps": wl.steps, "batch": wl.batch,
+                   "parallelism": f"replicas{world}",
+                   "l2": "inputs larger than L2 (807.6 MB of weights and "
+                         "classifier per token)",
+                   "timing": "step: CUDA events on the library stream; "
+                             "prefill/decode split: in-kernel device timer"},
+        "prefill_tok_s": round(prefill_tps, 2),
+        "e2e": {"value": round(e2e, 2),
+                "unit": "generated tok/s via nut_generate_greedy (incl. prefill)",
+                "h2d_bytes_per_step": int(prompt.nbytes),
+                "d2h_bytes_per_step": int(wl.steps * 4)},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "qmatvec": micro,
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
+# capture summarised in profiles/
+NCU_TRAFFIC: dict = {}
+
+QMATVEC_SHAPES = [(2048, 2048), (5632, 2048), (2048, 5632), (32000, 2048)]
+
+
+def qmatvec_micro(nb, device, peak):
+    """Kernel microbenchmark (a): the quantised matvec at every BASELINE
+    shape, INT4 and INT8, x ~ N(0, 1).  Each measurement replays a CUDA
+    graph of back-to-back launches over enough copies of the matrix to
+    exceed twice the L2, so every launch reads its weights from HBM and no
+    host launch gap is timed.  GB/s = algorithmic bytes (weights, fp16
+    scales, x, y) per launch / device time per launch."""
+    import torch
+    torch.cuda.set_device(device)
+    dev = f"cuda:{device}"
+    out = []
+    s = torch.cuda.Stream(device=dev)
+    for qtype, tname in ((nb.INT4, "int4"), (nb.INT8, "int8")):
+        for rows, cols in QMATVEC_SHAPES:
+            w = nb.synth_normal(SEED, 7, rows * cols, 0.02).reshape(rows, cols)
+            q = nb.QuantizedMatrix.quantize(w, qtype)
+            wbytes = (rows * cols // (2 if qtype == nb.INT4 else 1)
+                      + 2 * (rows * cols // 32))
+            copies = max(2, -(-(256 << 20) // wbytes))
+            mats = [nb.DeviceQMatrix(q, device) for _ in range(copies)]
+            x = torch.from_numpy(nb.synth_normal(SEED, 8, cols, 1.0)).to(dev)
+            ys = [torch.empty(rows, device=dev) for _ in range(copies)]
+            with torch.cuda.stream(s):
+                for m, y in zip(mats, ys):  # warm-up (also sets attributes)
+                    m.matvec_async(x.data_ptr(), y.data_ptr(), s.cuda_stream)
+            s.synchronize()
+            reps = max(1, 512 // copies)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(reps):
+                    for m, y in zip(mats, ys):
+                        m.matvec_async(x.data_ptr(), y.data_ptr(),
+                                       torch.cuda.current_stream().cuda_stream)
+            times = []
+            for _ in range(4):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(s):
+                    a.record(s)
+                    g.replay()
+                    b.record(s)
+                b.synchronize()
+                times.append(a.elapsed_time(b) * 1e-3 / (reps * copies))
+            t = min(times[1:])
+            bytes_ = wbytes + 4 * cols + 4 * rows
+            ach = bytes_ / t / 1e9
+            out.append({"type": tname, "rows": rows, "cols": cols,
+                        "us": round(t * 1e6, 3), "GB/s": round(ach, 1),
+                        "frac": round(ach / peak, 4)})
+            del g, mats, ys
+    return out
 
 
 def cpu_baseline(wl, c):
-    """The reference's own CPU loop on a bounded sample (prompt + 2 greedy
-    tokens) of the same workload, all host threads."""
+    """The reference's own CPU loop (oracle/_ref) on this host, all host
+    threads, on the whole workload: the prompt and every greedy step."""
     import oracle
+    from nutllm_b200 import synthetic as syn
     threads = os.cpu_count() or 1
-    sample_steps = 2
-    try:
-        if oracle.reference_available():
-            r = oracle.Reference()
-            rm = r.model(c, wl.qtype, SEED)
-            from nutllm_b200 import synthetic as syn
-            prompt = syn.prompt_ids(c, SEED, wl.prompt)
-            _, _, _, ps, ds = rm.generate(prompt, sample_steps, threads,
-                                          want_logits=False)
-            kind = "reference"
-        else:
-            return {"value": None, "unit": "tok/s", "cores": threads,
-                    "kind": "port", "sample": "reference build missing"}
-    except Exception as e:  # pragma: no cover - reported, not fatal
-        return {"value": None, "unit": "tok/s", "cores": threads,
-                "kind": "reference", "sample": f"failed: {e}"}
-    return {"value": round(sample_steps / ds, 3), "unit": "decode tok/s",
-            "cores": threads, "kind": kind,
+    if not oracle.reference_available():
+        return {"value": None, "unit": "decode tok/s", "cores": threads,
+                "kind": "reference", "sample": "oracle/_ref not built"}
+    r = oracle.Reference()
+    rm = r.model(c, wl.qtype, SEED)
+    prompt = syn.prompt_ids(c, SEED, wl.prompt)
+    _, _, _, ps, ds = rm.generate(prompt, wl.steps, threads, want_logits=False)
+    return {"value": round(wl.steps / ds, 3), "unit": "decode tok/s",
+            "cores": threads, "kind": "reference",
             "prefill_tok_s": round(wl.prompt / ps, 3),
-            "sample": f"{wl.prompt}-token prompt + {sample_steps} greedy "
-                      f"decode steps of {wl.name}, {threads} threads"}
+            "sample": f"the whole workload once: {wl.prompt}-token prompt + "
+                      f"{wl.steps} greedy decode steps of {wl.name}"}
 
 
 # ------------------------------------------------------------- reference
@@ -291,7 +342,7 @@ def run_reference(args, rank, world):
     r = oracle.Reference()
     rm = r.model(c, wl.qtype, SEED)
     prompt = syn.prompt_ids(c, SEED, wl.prompt)
-    sample_steps = min(wl.steps, 4)
+    sample_steps = wl.steps
     for _ in range(min(args.warmup, 1)):
         rm.generate(prompt, 1, threads, want_logits=False)
     dec, pre = 0.0, 0.0

@@ -115,6 +115,17 @@ nut_status nut_model_destroy(nut_model *model);
 /* QuantizedModelWeights::storage_bytes (src/quant_model.cpp:140-156). */
 nut_status nut_model_storage_bytes(const nut_model *model, uint64_t *bytes);
 
+/* The CUDA stream (a cudaStream_t) on which every call with this model
+ * enqueues its work, for callers that time or order that work with their
+ * own CUDA events.  No counterpart in the reference (its loop is host
+ * code). */
+nut_status nut_model_stream(const nut_model *model, void **stream);
+
+/* Total kernels this library has launched in this process (all devices),
+ * for callers that account for launches per step.  No counterpart in the
+ * reference. */
+nut_status nut_launch_count(uint64_t *count);
+
 /* ---- KV cache and decode state (include/kvcache.hpp:8-31) ------------ */
 
 /* KVCache(config) (src/kvcache.cpp:173-177): fp32 keys and values of

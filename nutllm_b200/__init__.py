@@ -149,6 +149,8 @@ def cuda_lib() -> C.CDLL:
                                            C.POINTER(_P)])
         _declare(lib, "nut_model_destroy", [_P])
         _declare(lib, "nut_model_storage_bytes", [_P, C.POINTER(C.c_uint64)])
+        _declare(lib, "nut_model_stream", [_P, C.POINTER(_P)])
+        _declare(lib, "nut_launch_count", [C.POINTER(C.c_uint64)])
         _declare(lib, "nut_kv_create", [_P, C.POINTER(_P)])
         _declare(lib, "nut_kv_destroy", [_P])
         _declare(lib, "nut_kv_reset", [_P])
@@ -214,6 +216,13 @@ def storage_sizes(rows: int, cols: int, qtype: int) -> tuple[int, int]:
     n = rows * cols
     return (n if qtype == INT8 else (n + 1) // 2), (n + 31) // 32
 
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process so far."""
+    out = C.c_uint64()
+    _check(cuda_lib().nut_launch_count(C.byref(out)))
+    return out.value
 
 def quantize(weights: np.ndarray, qtype: int) -> tuple[np.ndarray, np.ndarray]:
     """QuantizedMatrix::quantize (reference src/quant.cpp:154-197): returns
@@ -408,6 +417,13 @@ class DeviceModel:
         out = C.c_uint64(0)
         _check(cuda_lib().nut_model_storage_bytes(self.handle, C.byref(out)))
         return out.value
+
+    @property
+    def stream(self) -> int:
+        """The cudaStream_t (as an integer) all work on this model runs on."""
+        out = _P()
+        _check(cuda_lib().nut_model_stream(self.handle, C.byref(out)))
+        return int(out.value or 0)
 
     def close(self) -> None:
         if getattr(self, "handle", None):

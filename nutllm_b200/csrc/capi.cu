@@ -7,6 +7,7 @@
  * the same order, as the reference's decode_quantized_token
  * (src/quant_model.cpp:161-172) and prefill_quantized (:212-213).
  */
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -30,6 +31,12 @@ thread_local std::string g_error;
 } // namespace
 
 void nut::set_last_error(const std::string &message) { g_error = message; }
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}
+
+void nut::count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 namespace {
 
@@ -842,6 +849,23 @@ nut_status nut_model_storage_bytes(const nut_model *model, uint64_t *bytes) {
             raise(NUT_INVALID_ARGUMENT, "model: null argument");
         *bytes = model->storage_bytes;
     });
+}
+
+nut_status nut_model_stream(const nut_model *model, void **stream) {
+    return guarded([&] {
+        if (model == nullptr || stream == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "model: null argument");
+        *stream = static_cast<void *>(model->stream);
+    });
+}
+
+nut_status nut_launch_count(uint64_t *count) {
+    if (count == nullptr) {
+        g_error = "launch count: null argument";
+        return NUT_INVALID_ARGUMENT;
+    }
+    *count = g_launches.load(std::memory_order_relaxed);
+    return NUT_OK;
 }
 
 nut_status nut_kv_create(nut_model *model, nut_kv **out) {

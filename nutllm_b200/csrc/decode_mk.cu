@@ -33,6 +33,7 @@
 #include <cstdio>
 
 #include "decode_mk.h"
+#include "kernels.h"
 #include "stream.cuh"
 
 namespace nut {
@@ -1066,6 +1067,7 @@ cudaError_t launch_t(MkParams p, int sms, size_t smem, cudaStream_t stream) {
     if (e != cudaSuccess)
         return e;
     void *args[] = {&p};
+    nut::count_launches(1);
     return cudaLaunchCooperativeKernel(reinterpret_cast<void *>(kernel), dim3(sms),
                                        dim3(THREADS), args, smem, stream);
 }

@@ -376,10 +376,12 @@ void launch_qmatvec(const QSegs &segs, const float *src, const float *norm,
         cudaFuncSetAttribute(qmatvec_kernel<1>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         qmatvec_kernel<1><<<grid, kMatvecThreads, smem, stream>>>(segs, src, norm);
+        count_launches(1);
     } else {
         cudaFuncSetAttribute(qmatvec_kernel<0>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         qmatvec_kernel<0><<<grid, kMatvecThreads, smem, stream>>>(segs, src, norm);
+        count_launches(1);
     }
 }
 
@@ -388,6 +390,7 @@ void launch_embed(const float *embeddings, int dim, int vocab, int token,
                   float *hidden, cudaStream_t stream) {
     embed_kernel<<<1, 256, 0, stream>>>(embeddings, dim, vocab, token,
                                         argmax_key, id_slot, hidden);
+    count_launches(1);
 }
 
 void launch_rope_store(float *q, const float *k, const float *v, float *kcache,
@@ -402,6 +405,7 @@ void launch_rope_store(float *q, const float *k, const float *v, float *kcache,
                                                 rope_cos, rope_sin, position,
                                                 layer, heads, kv_heads,
                                                 head_dim, max_seq);
+    count_launches(1);
 }
 
 void launch_attention(const float *q, const float *kcache, const float *vcache,
@@ -414,10 +418,12 @@ void launch_attention(const float *q, const float *kcache, const float *vcache,
     attention_kernel<<<heads, 128, smem, stream>>>(q, kcache, vcache, ctx,
                                                    position, layer, heads,
                                                    kv_heads, head_dim, max_seq);
+    count_launches(1);
 }
 
 void launch_swiglu(float *gate, const float *up, int n, cudaStream_t stream) {
     swiglu_kernel<<<(n + 255) / 256, 256, 0, stream>>>(gate, up, n);
+    count_launches(1);
 }
 
 void launch_lmhead(const float *hidden, const float *final_norm,
@@ -430,6 +436,7 @@ void launch_lmhead(const float *hidden, const float *final_norm,
     grid = grid < 4 * sm_count() ? grid : 4 * sm_count();
     lmhead_kernel<<<grid, 256, smem, stream>>>(hidden, final_norm, weights,
                                                vocab, dim, logits, argmax_key);
+    count_launches(1);
 }
 
 } // namespace nut

@@ -173,6 +173,7 @@ extern "C" nut_status nut_greedy_head_static(const float *hidden, const float *f
     head_kernel<<<dim3(per_row, rows), 256, smem, s>>>(hidden, final_norm, weights, int(vocab),
                                                         int(dim), logits, keys);
     keys_to_index<<<(rows + 255) / 256, 256, 0, s>>>(keys, rows, argmax);
+    nut::count_launches(3);
     e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(NUT_RUNTIME_ERROR, std::string("cuda: greedy head launch: ") +

@@ -11,6 +11,10 @@ namespace nut {
 /* Sets the calling thread's message returned by nut_last_error(). */
 void set_last_error(const std::string &message);
 
+/* Adds n to the process-wide count of kernels this library has launched
+ * (read through nut_launch_count). */
+void count_launches(unsigned n);
+
 /* One quantised matrix in the reference storage layout on the device. */
 struct DevQMatrix {
     uint8_t *data = nullptr;

@@ -8,6 +8,7 @@
  * digits once and then multiply every streamed tile pair. */
 #include <cstdio>
 
+#include "kernels.h"
 #include "kernels_tc.h"
 #include "stream.cuh"
 
@@ -138,6 +139,7 @@ cudaError_t launch_qmatvec_tc(const TileMatrix &m, const float *x, float *y,
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(smem));
         kernel<<<grid, kThreads, smem, stream>>>(p);
+        nut::count_launches(1);
     };
     if (m.shape.type == 1)
         stages == 10 ? go(qmatvec_tc_kernel<1, 10>) : go(qmatvec_tc_kernel<1, 6>);

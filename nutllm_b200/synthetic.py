@@ -93,15 +93,34 @@ def build_model(c: Config, qtype: int, seed: int, tied: bool = False) -> ModelWe
                         tied_embeddings=tied)
 
 
-def algorithmic_decode_bytes(c: Config, qtype: int, context: int) -> int:
-    """HBM bytes one batch-1 decode token must move: every quantised weight
-    and scale once, the embedding row, the norms, the fp32 classifier, the
-    KV history read (context positions, K and V) and the new K/V written."""
-    n = 0
-    for rows, cols in projection_shapes(c):
-        n += rows * cols
-    weights = (n if qtype == INT8 else n // 2) + 2 * (n // 32)
-    per_layer_kv = 2 * c.kv_dim * 4
-    return int(c.layers * 0 + weights + c.vocab_size * c.dim * 4 + c.dim * 4
-               + (2 * c.layers + 1) * c.dim * 4
-               + c.layers * per_layer_kv * (context + 1))
+def quantised_layer_bytes(c: Config, qtype: int) -> int:
+    """Storage of one layer's seven quantised projections: the weights
+    (1 or 1/2 byte each) and one fp16 scale per block of 32."""
+    n = sum(rows * cols for rows, cols in projection_shapes(c))
+    return (n if qtype == INT8 else n // 2) + 2 * (n // 32)
+
+
+def algorithmic_decode_bytes(c: Config, qtype: int, pos: int,
+                             logits: bool = True) -> int:
+    """HBM bytes one batch-1 decode pass at position `pos` must move: every
+    quantised weight and scale once, the embedding row, the two norm vectors
+    per layer, the KV history of positions 0..pos (K and V, fp32, written
+    once and read once), and, when the pass produces logits, the final norm
+    and the fp32 classifier."""
+    b = (c.layers * quantised_layer_bytes(c, qtype) + c.dim * 4
+         + 2 * c.layers * c.dim * 4 + c.layers * 2 * c.kv_dim * 4 * (pos + 1))
+    if logits:
+        b += c.vocab_size * c.dim * 4 + c.dim * 4
+    return int(b)
+
+
+def algorithmic_generation_bytes(c: Config, qtype: int, n_prompt: int,
+                                 steps: int) -> int:
+    """Bytes of one greedy generation run as a single device loop: passes at
+    positions 0 .. n_prompt+steps-1, logits after passes n_prompt-1 ..
+    n_prompt+steps-2 (the last pass decodes the last chosen token)."""
+    total = 0
+    for pos in range(n_prompt + steps):
+        total += algorithmic_decode_bytes(
+            c, qtype, pos, n_prompt - 1 <= pos <= n_prompt + steps - 2)
+    return total
