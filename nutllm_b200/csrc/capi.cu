@@ -160,9 +160,9 @@ nut::QSeg seg(const nut::DevQMatrix &m, float *out, int accumulate) {
 }
 
 /* Packs reference storage into fragment tiles on the device. */
-nut::TileMatrix upload_tiles(const nut_qmatrix_view &v) {
+nut::TileMatrix upload_tiles(const nut_qmatrix_view &v, int order = nut::kRowMajor) {
     nut::TileMatrix t;
-    t.shape = nut::TileShape::of(v.rows, v.cols, v.type);
+    t.shape = nut::TileShape::of(v.rows, v.cols, v.type, order);
     std::vector<uint8_t> data(t.shape.data_bytes());
     std::vector<uint16_t> scales(t.shape.scale_count());
     nut::pack_tiles(t.shape, v.data, v.scales, data.data(), scales.data());
@@ -339,7 +339,9 @@ struct nut_kv {
     bool has_hidden = false;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     /* persistent-kernel state */
-    nut::Tagged *tagged = nullptr; /* hA | hB | qkv | gu */
+    nut::Tagged *tagged = nullptr; /* q | k | v of the current token */
+    float *mk_acc = nullptr;       /* [kAccSlots][dim] residual accumulators */
+    unsigned int *mk_cnt = nullptr; /* [kAccSlots] step counters */
     size_t tagged_count = 0;
     unsigned long long *mk_keys = nullptr; /* [max_seq] */
     unsigned int *mk_done = nullptr;       /* [max_seq] */
@@ -355,6 +357,7 @@ struct nut_kv {
         dev_free(k), dev_free(v), dev_free(ctx), dev_free(gate), dev_free(up);
         dev_free(logits), dev_free(argmax_key), dev_free(ids);
         dev_free(tagged), dev_free(mk_keys), dev_free(mk_done), dev_free(mk_prompt);
+        dev_free(mk_acc), dev_free(mk_cnt);
         dev_free(mk_error), dev_free(mk_stamps), dev_free(mk_logits);
         for (auto e : ev)
             if (e)
@@ -464,6 +467,9 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
     cuda_check(cudaMemcpyAsync(kv->mk_prompt, tokens, size_t(n_prompt) * 4,
                                cudaMemcpyHostToDevice, s),
                "copy prompt");
+    cuda_check(cudaMemsetAsync(kv->mk_acc, 0, size_t(nut::kAccSlots) * c.dim * 4, s),
+               "clear accumulators");
+    cuda_check(cudaMemsetAsync(kv->mk_cnt, 0, size_t(nut::kAccSlots) * 4, s), "clear counters");
     cuda_check(cudaMemsetAsync(kv->tagged, 0, kv->tagged_count * sizeof(nut::Tagged), s),
                "clear tags");
     cuda_check(cudaMemsetAsync(kv->mk_keys, 0, size_t(n_tokens) * 8, s), "clear keys");
@@ -498,11 +504,16 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
     p.rope_sin = m->rope_sin;
     p.kcache = kv->keys;
     p.vcache = kv->values;
-    p.hA = kv->tagged;
-    p.hB = p.hA + dim;
-    p.qkv = p.hB + dim;
-    p.ctx = p.qkv + dim + 2 * kvd;
-    p.act = p.ctx + dim;
+    p.qkv = kv->tagged;
+    p.hacc = kv->mk_acc;
+    p.hidden_out = kv->hidden;
+    p.cnt = kv->mk_cnt;
+    p.wo_pairs = int(L0.wo.shape.blocks / 2);
+    p.cpp = std::max(1, std::min(m->sms / p.wo_pairs, p.rt_wo));
+    p.count_aw = p.wo_pairs * p.cpp;
+    p.nbf = int(c.ffn_dim / 32);
+    p.count_gd = std::min(p.nbf, m->sms);
+    p.rt_down_pairs = int(L0.down.shape.row_tiles / 2);
     p.prompt = kv->mk_prompt;
     p.n_prompt = int(n_prompt);
     p.n_tokens = int(n_tokens);
@@ -519,7 +530,7 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
      * to that file (tracing aid; off by default) */
     const char *trace_file = std::getenv("NUTLLM_TRACE_FILE");
     unsigned long long *trace = nullptr;
-    const int stride = int(n_tokens * (5 * c.layers + 1));
+    const int stride = int(n_tokens * (3 * c.layers + 1));
     if (trace_file != nullptr) {
         trace = dev_alloc<unsigned long long>(size_t(m->sms) * stride * 8, "alloc trace");
         cuda_check(cudaMemsetAsync(trace, 0, size_t(m->sms) * stride * 64, s), "clear trace");
@@ -541,10 +552,6 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
             std::fclose(f);
         }
     }
-    /* last hidden vector: the value halves of hB */
-    cuda_check(cudaMemcpy2DAsync(kv->hidden, sizeof(float), p.hB, sizeof(nut::Tagged),
-                                 sizeof(float), size_t(dim), cudaMemcpyDeviceToDevice, s),
-               "unpack hidden");
     std::vector<unsigned long long> keys(size_t(nlog > 0 ? nlog : 0));
     if (ids_host != nullptr && nlog > 0)
         cuda_check(cudaMemcpyAsync(keys.data(), kv->mk_keys + lfrom, size_t(nlog) * 8,
@@ -736,7 +743,7 @@ nut_status nut_model_create(const nut_model_view *view, int device,
                    "device attribute");
         m->mk = coop != 0 &&
                 nut::mk_supported(int(c.dim), int(c.ffn_dim), int(kvd), int(c.head_dim),
-                                  int(c.heads), view->quant_type, max_smem);
+                                  int(c.heads), view->quant_type, max_smem, m->sms);
         if (m->mk) {
             std::vector<nut::MkLayerPtrs> ptrs;
             std::vector<float> an(size_t(c.layers) * dim), fn(size_t(c.layers) * dim);
@@ -755,9 +762,9 @@ nut_status nut_model_create(const nut_model_view *view, int device,
                 m->mk_layers.emplace_back();
                 nut::MkLayer &d = m->mk_layers.back();
                 d.qkv = upload_stacked({&lv.query, &lv.key, &lv.value});
-                d.wo = upload_tiles(lv.output);
+                d.wo = upload_tiles(lv.output, nut::kPairColumn);
                 d.gu = upload_gate_up(lv.gate, lv.up);
-                d.down = upload_tiles(lv.down);
+                d.down = upload_tiles(lv.down, nut::kBlockColumn);
                 ptrs.push_back({d.qkv.data, d.wo.data, d.gu.data, d.down.data,
                                 d.qkv.scales, d.wo.scales, d.gu.scales, d.down.scales});
                 for (const nut_qmatrix_view *q : {&lv.query, &lv.key, &lv.value, &lv.output,
@@ -895,8 +902,9 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
         for (auto &e : kv->ev)
             cuda_check(cudaEventCreate(&e), "create event");
         if (model->mk) {
-            kv->tagged_count = size_t(2 * c.dim) + size_t(c.dim) + 2 * kvd +
-                               size_t(c.dim) + size_t(c.ffn_dim);
+            kv->tagged_count = size_t(c.dim) + 2 * kvd;
+            kv->mk_acc = dev_alloc<float>(size_t(nut::kAccSlots) * c.dim, "alloc accumulators");
+            kv->mk_cnt = dev_alloc<unsigned int>(nut::kAccSlots, "alloc step counters");
             kv->tagged = dev_alloc<nut::Tagged>(kv->tagged_count, "alloc tagged");
             kv->mk_keys = dev_alloc<unsigned long long>(size_t(c.max_seq), "alloc keys");
             kv->mk_done = dev_alloc<unsigned int>(size_t(c.max_seq), "alloc counts");

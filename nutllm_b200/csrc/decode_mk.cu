@@ -3,25 +3,42 @@
  *
  * Per token i at position pos (reference decode_quantized_token,
  * src/quant_model.cpp:158-206, then the greedy head of generate_tokens_cached,
- * src/generate.cpp:197-205), for each layer l:
- *   QKV   x = rmsnorm(h) -> [q;k;v] = Wqkv x, RoPE on q and k
- *         (src/quant_model.cpp:26-37), k and v appended to the KV cache
- *   WO    GQA attention over positions 0..pos (src/quant_model.cpp:68-105),
- *         hA = h + Wo ctx
- *   GU    x = rmsnorm(hA) -> [gate;up] = Wgu x
- *   DOWN  a = silu(gate) * up, hB = hA + Wdown a
+ * src/generate.cpp:197-205), for each layer l, three steps:
+ *   QKV    x = rmsnorm(h) -> [q;k;v] = Wqkv x, RoPE on q and k
+ *          (src/quant_model.cpp:26-37), k and v appended to the KV cache;
+ *          CTAs own row tiles; q|k|v are published as tagged elements
+ *   ATTWO  hA = h + Wo ctx, split by K: CTA (P, r) owns columns
+ *          64 P .. 64 P + 63 of Wo (one pair of blocks) for the r-th share of
+ *          its row tiles; it computes the GQA attention (src/quant_model.cpp:
+ *          68-105) of the heads those columns cover and adds Wo[:, cols] ctx
+ *          into an fp32 accumulator
+ *   GUDOWN hB = hA + Wdown silu(Wgate x) * Wup x, x = rmsnorm(hA), split by
+ *          FFN block: a CTA owns 32-unit blocks, computes their gate and up
+ *          rows, the SwiGLU in shared memory, and adds Wdown[:, block] act
+ *          into an fp32 accumulator
  * and, when the token's logits are needed, LMHEAD: x = rmsnorm(hB),
  * logits = W_cls x (fp32), argmax (first index of the maximum).
  *
- * Each CTA owns an even share of the row tiles of every matrix and of the
- * classifier rows, so its weights form a fixed sequence of contiguous runs
- * that its producer warp streams through the shared-memory ring without
- * ever waiting for activations: weight traffic runs ahead across phase and
- * token boundaries, limited only by the ring.  Activations cross CTAs
- * through tagged vectors: every element is written once per phase as one
- * 64-bit (value, tag) store, the tag naming the token, layer and phase, and
- * a consumer waits until every element it needs carries the expected tag.
- * That replaces grid-wide barriers with point-to-point data readiness.
+ * Each CTA's weights form a fixed sequence of contiguous tile runs that its
+ * producer warp streams through the shared-memory ring without ever waiting
+ * for activations: weight traffic runs ahead across step and token
+ * boundaries, limited only by the ring.
+ *
+ * Activations cross CTAs in two ways.  q|k|v travel as tagged vectors:
+ * every element is written once per layer as one 64-bit (value, tag) store
+ * and a consumer waits until each element it needs carries the expected
+ * tag.  The residual stream travels through a ring of kAccSlots fp32
+ * accumulators: the contributors of a step add their partial rows with
+ * red.add, fence, and count themselves in the slot's counter; readers wait
+ * (acquire) for the counter to reach the step's target and read the slot
+ * through L2.  Step s (two per layer) uses slot s mod kAccSlots, whose
+ * counter only grows, so step s's target is (s / kAccSlots + 1) times its
+ * contributor count.  During step s every contributor zeroes its share of
+ * slot s + 1 before counting itself, which orders the zeroing before every
+ * red.add of step s + 1; the slot's previous readers (step s + 1 -
+ * kAccSlots) finished long before, since each step waits for the last.
+ * Float red.add makes the summation order of a step's partials vary from
+ * run to run (parity is by tolerance, as for any reordered sum).
  * Key and value rows of the current position travel in the tagged q|k|v
  * vector; their cache stores precede a release store of the tag, and the
  * attention's acquire loads of those tags make every earlier cache store
@@ -76,18 +93,34 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
 
-/* Phases per layer: 0 QKV, 1 ATT, 2 WO, 3 GU, 4 DOWN. */
-__device__ __forceinline__ uint32_t tag_of(const MkParams &p, int i, int l, int phase) {
-    return 1u + uint32_t((i * p.layers + l) * 5 + phase);
+/* Tag of the q|k|v elements of token i, layer l. */
+__device__ __forceinline__ uint32_t qkv_tag(const MkParams &p, int i, int l) {
+    return 1u + uint32_t(i * p.layers + l);
 }
 
-/* Row-tile (or row) range of this CTA in an even split of `total`
- * (total * gridDim.x < 2^31 for every supported shape; 32-bit arithmetic
- * avoids the emulated 64-bit division). */
+/* Accumulator steps: 2 per layer, kind 0 = hA (after ATTWO), 1 = hB (after
+ * GUDOWN). */
+__device__ __forceinline__ int step_of(const MkParams &p, int i, int l, int kind) {
+    return 2 * (i * p.layers + l) + kind;
+}
+__device__ __forceinline__ float *slot_of(const MkParams &p, int step) {
+    return p.hacc + size_t(step % kAccSlots) * p.dim;
+}
+__device__ __forceinline__ unsigned target_of(const MkParams &p, int step) {
+    return unsigned(step / kAccSlots + 1) * unsigned((step & 1) ? p.count_gd : p.count_aw);
+}
+
+/* Range of part i in an even split of `total` into n parts
+ * (total * n < 2^31 for every supported shape; 32-bit arithmetic avoids
+ * the emulated 64-bit division). */
+__device__ __forceinline__ void share_of(int total, int i, int n, int &a, int &b) {
+    const unsigned t = unsigned(total), c = unsigned(n), k = unsigned(i);
+    a = int(t * k / c);
+    b = int(t * (k + 1) / c);
+}
+/* This CTA's range in an even split over the grid. */
 __device__ __forceinline__ void share(int total, int &a, int &b) {
-    const unsigned t = unsigned(total), c = gridDim.x, i = blockIdx.x;
-    a = int(t * i / c);
-    b = int(t * (i + 1) / c);
+    share_of(total, int(blockIdx.x), int(gridDim.x), a, b);
 }
 
 struct Shared {
@@ -100,7 +133,8 @@ struct Shared {
     float *wsum;       /* [W] */
     unsigned long long *bestk; /* [W] */
     int *flag;         /* [0] fatal, [1] token */
-    float *res;        /* [kResRows] residual inputs of this CTA's rows */
+    float *yacc;       /* [dim] this CTA's partial rows of a split-K step */
+    float *actv;       /* [kMaxFfnBlocks * 32] SwiGLU outputs of owned blocks */
 };
 
 /* Optional phase trace (thread 0 of each CTA): one record of 8 words per
@@ -163,8 +197,10 @@ __device__ Shared carve(uint8_t *base, const MkParams &p) {
     off = align16(off + W * 8);
     s.flag = reinterpret_cast<int *>(base + off);
     off = align16(off + 16);
-    s.res = reinterpret_cast<float *>(base + off);
-    off = align16(off + 64 * 4);
+    s.yacc = reinterpret_cast<float *>(base + off);
+    off = align16(off + size_t(p.dim + 32) * 4);
+    s.actv = reinterpret_cast<float *>(base + off);
+    off = align16(off + kMaxFfnBlocks * 32 * 4);
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + off);
     s.ring = Ring{data, scales, bars, bars + STAGES, STAGES, p.limit_ns, p.error, s.flag};
     return s;
@@ -216,63 +252,68 @@ __device__ __forceinline__ bool wait_tag(const Tagged *src, uint32_t tag,
     return true;
 }
 
-constexpr int kPollBatch = 8; /* element loads in flight per thread */
+constexpr int kPollBatch = 8; /* elements per thread of a staged vector */
+constexpr int kResRegs = 2;   /* residual rows per thread held in registers */
 
-/* Loads up to kPollBatch tagged elements k0, k0 + NT, ... (< n) of src
- * into v[] with all loads issued before any tag is checked; retries (with
- * a short sleep) until every tag matches.  False on timeout. */
-template <bool ACQ>
-__device__ __forceinline__ bool wait_batch(const Tagged *src, int n, int k0,
-                                           uint32_t tag, uint64_t limit,
-                                           float (&v)[kPollBatch]) {
-    uint64_t x[kPollBatch];
-    uint64_t t0 = 0;
-    for (bool first = true;; first = false) {
-#pragma unroll
-        for (int j = 0; j < kPollBatch; j++) {
-            const int k = k0 + j * NT;
-            x[j] = k < n ? (ACQ ? ld_acquire(src + k) : ld_relaxed(src + k))
-                         : (uint64_t(tag) << 32);
+/* Collective: waits until accumulator step `step` is complete (its counter
+ * reached the step's target; thread 0 polls with acquire loads and the
+ * barrier passes the ordering on).  The slot is then read with L2 loads
+ * (__ldcg): lines of an older use of the slot may still sit in L1. */
+__device__ bool wait_step(const Shared &s, const MkParams &p, int step) {
+    if (threadIdx.x == 0) {
+        const unsigned *c = p.cnt + step % kAccSlots;
+        const unsigned want = target_of(p, step);
+        if (ld_acquire_u32(c) < want) {
+            const uint64_t t0 = global_ns();
+            while (ld_acquire_u32(c) < want) {
+                if (global_ns() - t0 > p.limit_ns) {
+                    fatal(s, p, kErrTimeoutInput);
+                    break;
+                }
+                __nanosleep(32);
+            }
         }
-        bool ready = true;
-#pragma unroll
-        for (int j = 0; j < kPollBatch; j++)
-            ready = ready && uint32_t(x[j] >> 32) == tag;
-        if (ready)
-            break;
-        const uint64_t now = global_ns();
-        if (first)
-            t0 = now;
-        else if (now - t0 > limit)
-            return false;
-        __nanosleep(128);
     }
-#pragma unroll
-    for (int j = 0; j < kPollBatch; j++)
-        v[j] = __uint_as_float(uint32_t(x[j]));
-    return true;
+    return healthy(s);
 }
 
-/* Collective: stages n tagged elements into dst; thread t handles elements
- * t, t + NT, ... */
-template <bool ACQ>
-__device__ bool poll(const Shared &s, const MkParams &p, const Tagged *src, int n,
-                     uint32_t tag, float *dst) {
-    for (int k0 = threadIdx.x; k0 < n; k0 += kPollBatch * NT) {
-        float v[kPollBatch];
-        /* acquire = relaxed loads of every tag, then one fence */
-        if (!wait_batch<false>(src, n, k0, tag, p.limit_ns, v)) {
-            fatal(s, p, kErrTimeoutInput);
-            break;
-        }
+/* Collective: stages n (<= kPollBatch * NT) elements of a complete
+ * accumulator slot into dst with the same thread mapping as NormW. */
+__device__ void stage_slot(const float *src, int n, float *dst) {
 #pragma unroll
-        for (int j = 0; j < kPollBatch; j++)
-            if (k0 + j * NT < n)
-                dst[k0 + j * NT] = v[j];
+    for (int j = 0; j < kPollBatch; j++) {
+        const int k = threadIdx.x + j * NT;
+        if (k < n)
+            dst[k] = __ldcg(src + k);
     }
-    if (ACQ)
-        __threadfence();
-    return healthy(s);
+}
+
+__device__ __forceinline__ void red_add4(float *dst, float4 v) {
+    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(dst),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+/* Collective end of a contributor's share of accumulator step `step`:
+ * adds yacc[0, nrows) into rows row0.. of the step's slot, zeroes this
+ * contributor's share (index `me` of `count`) of the next step's slot, and
+ * counts itself in once every thread's stores are fenced. */
+__device__ void finish_step(const Shared &s, const MkParams &p, int step, int row0, int nrows,
+                            int me, int count) {
+    cbar();
+    float *dst = slot_of(p, step) + row0;
+    const float4 *y4 = reinterpret_cast<const float4 *>(s.yacc);
+    for (int k = threadIdx.x; k < nrows / 4; k += NT)
+        red_add4(dst + 4 * k, y4[k]);
+    int z0, z1;
+    share_of(p.dim / 4, me, count, z0, z1);
+    float4 *next = reinterpret_cast<float4 *>(slot_of(p, step + 1));
+    for (int k = z0 + int(threadIdx.x); k < z1; k += NT)
+        next[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    __threadfence();
+    cbar();
+    if (threadIdx.x == 0)
+        atomicAdd(p.cnt + step % kAccSlots, 1u);
 }
 
 /* Norm weights of this thread's elements (k = tid + j NT), loaded before
@@ -336,7 +377,10 @@ __device__ __forceinline__ float rope(float y, int lane, float c, float sn) {
    is applied to each row in the epilogue, from per-warp partial sums that
    the first row-tile barrier publishes. */
 
-constexpr int kSliceBlocks = 4; /* blocks staged per round (per lane: one element each) */
+/* Blocks staged per round (per lane: one element each): every load of the
+ * slice is issued before any is used, so the slice costs one L2 round trip
+ * (one round for K <= 2 * W * 5 blocks, i.e. dim <= 4800). */
+constexpr int kSliceBlocks = 10;
 
 /* Element of the warp's k-th owned block: block index, or -1 past the end. */
 __device__ __forceinline__ int slice_block(int w, int nb, int k) {
@@ -344,13 +388,13 @@ __device__ __forceinline__ int slice_block(int w, int nb, int k) {
     return 2 * p < nb ? 2 * p + (k & 1) : -1;
 }
 
-/* Stages the warp's slice of an input vector of K elements (tagged, or a
- * plain fp32 row when `plain` is set), multiplies it by `norm` (if any),
- * writes its digits and block factors and returns the lane's sum of
- * squares of the raw inputs.  False on timeout. */
+/* Stages the warp's slice of an fp32 input vector of K elements (an
+ * embedding row or a complete accumulator slot, read through L2), multiplies
+ * it by `norm` (if any), writes its digits and block factors and returns
+ * the lane's sum of squares of the raw inputs.  All loads are issued before
+ * any is used and the block peaks are reduced together. */
 template <int TYPE>
-__device__ bool warp_slice(const Shared &s, const MkParams &p, const Tagged *src,
-                           const float *plain, int K, int nb, uint32_t tag,
+__device__ void warp_slice(const Shared &s, const float *src, int K, int nb,
                            const float *norm, float &ss) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float a_unit_inv = TYPE == 1 ? 1.0f / 16.0f : 1.0f;
@@ -358,56 +402,28 @@ __device__ bool warp_slice(const Shared &s, const MkParams &p, const Tagged *src
     for (int k0 = 0;; k0 += kSliceBlocks) {
         if (slice_block(w, nb, k0) < 0)
             break;
-        float nw[kSliceBlocks];
-        uint64_t x[kSliceBlocks];
+        float nw[kSliceBlocks], x[kSliceBlocks];
 #pragma unroll
         for (int k = 0; k < kSliceBlocks; k++) {
             const int b = slice_block(w, nb, k0 + k), e = b * 32 + lane;
             const bool in = b >= 0 && e < K;
             nw[k] = norm != nullptr && in ? __ldg(norm + e) : 1.0f;
-            if (plain != nullptr)
-                x[k] = (uint64_t(tag) << 32) | __float_as_uint(in ? plain[e] : 0.0f);
-            else
-                x[k] = in ? ld_relaxed(src + e) : (uint64_t(tag) << 32);
+            x[k] = in ? __ldcg(src + e) : 0.0f;
         }
-        if (plain == nullptr) {
-            uint64_t t0 = 0;
-            for (bool first = true;; first = false) {
-                bool ready = true;
+        uint32_t mb[kSliceBlocks];
 #pragma unroll
-                for (int k = 0; k < kSliceBlocks; k++)
-                    ready = ready && uint32_t(x[k] >> 32) == tag;
-                if (__all_sync(0xffffffffu, ready))
-                    break;
-                const uint64_t now = global_ns();
-                if (first)
-                    t0 = now;
-                else if (now - t0 > p.limit_ns) {
-                    fatal(s, p, kErrTimeoutInput);
-                    return false;
-                }
-                __nanosleep(128);
-#pragma unroll
-                for (int k = 0; k < kSliceBlocks; k++) {
-                    const int b = slice_block(w, nb, k0 + k), e = b * 32 + lane;
-                    if (b >= 0 && e < K && uint32_t(x[k] >> 32) != tag)
-                        x[k] = ld_relaxed(src + e);
-                }
-            }
+        for (int k = 0; k < kSliceBlocks; k++) {
+            ss = fmaf(x[k], x[k], ss);
+            x[k] *= nw[k];
+            mb[k] = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(x[k])));
         }
 #pragma unroll
         for (int k = 0; k < kSliceBlocks; k++) {
             const int b = slice_block(w, nb, k0 + k);
-            if (b < 0)
-                break;
-            const float v = __uint_as_float(uint32_t(x[k]));
-            ss = fmaf(v, v, ss);
-            const float u = v * nw[k];
-            s.xvec[b * 32 + lane] = u;
-            digit_block(s.xvec, nb * 32, b, s.dig, s.fac, a_unit_inv);
+            if (b >= 0)
+                digit_from(x[k], mb[k], b, s.dig, s.fac, a_unit_inv);
         }
     }
-    return true;
 }
 
 /* Publishes the warp's sum of squares for the epilogue's norm scale. */
@@ -441,27 +457,49 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor 
     share(p.rt_qkv, a, b);
     if (a == b)
         return true;
+    /* The input is hB of layer l - 1.  Layer 0 reads the embedding row, but
+     * still waits for the previous token's last step: the q|k|v vector is
+     * single-buffered, and that step completes only after every attention
+     * of the previous token has read it. */
+    const int prev = l > 0 ? step_of(p, i, l - 1, 1)
+                           : (i > 0 ? step_of(p, i - 1, p.layers - 1, 1) : -1);
+    if (prev >= 0 && !wait_step(s, p, prev))
+        return false;
+    const float *src = l == 0 ? p.emb + size_t(token) * p.dim
+                              : slot_of(p, step_of(p, i, l - 1, 1));
+    const int half = p.hd / 2;
+    /* this position's RoPE row, staged for the epilogues (the first row-tile
+     * barrier publishes it) */
+    float *rope_cs = s.yacc, *rope_sn = s.yacc + half;
+    float rc = 0.0f, rsn = 0.0f; /* loaded here, stored after the slice */
+    if (int(threadIdx.x) < half) {
+        rc = __ldg(p.rope_cos + size_t(pos) * half + threadIdx.x);
+        rsn = __ldg(p.rope_sin + size_t(pos) * half + threadIdx.x);
+    }
     float ss;
-    if (!warp_slice<TYPE>(s, p, p.hB, l == 0 ? p.emb + size_t(token) * p.dim : nullptr, p.dim,
-                          p.nb_dim, l == 0 ? 0u : tag_of(p, i, l - 1, 4),
-                          p.attn_norm + size_t(l) * p.dim, ss))
-        ss = 0.0f;
+    warp_slice<TYPE>(s, src, p.dim, p.nb_dim, p.attn_norm + size_t(l) * p.dim, ss);
     slice_ss(s, ss);
+    if (int(threadIdx.x) < half) {
+        rope_cs[threadIdx.x] = rc;
+        rope_sn[threadIdx.x] = rsn;
+    }
     tr.mark(2);
     constexpr int TB = TileGeom<TYPE>::kTileBytes;
     const MkLayerPtrs &L = p.layer[l];
     const TileRun run{L.qkv + size_t(a) * p.nb_dim * TB, L.qkv_s + size_t(a) * p.nb_dim * 16,
                       (b - a) * p.nb_dim, p.nb_dim};
-    const uint32_t tag = tag_of(p, i, l, 0);
-    const int lane = threadIdx.x & 31, half = p.hd / 2;
-    const float *cs = p.rope_cos + size_t(pos) * half;
-    const float *sn = p.rope_sin + size_t(pos) * half;
+    const uint32_t tag = qkv_tag(p, i, l);
+    const int lane = threadIdx.x & 31;
+    const float *cs = rope_cs, *sn = rope_sn;
     /* The cache rows of this token are read only by later tokens: the
      * fence ahead of each token's key/value tags orders the rows written
      * by the same lane one token earlier, and the readers acquire those
      * tags (load, then fence) before fetching history. */
+    float nsc = -1.0f; /* the rmsnorm scale, computed at the first epilogue */
     auto epi = [&](int rt, float y) {
-        y *= norm_scale(s, p.dim);
+        if (nsc < 0.0f)
+            nsc = norm_scale(s, p.dim);
+        y *= nsc;
         const int row0 = (a + rt) * 16, row = row0 + (lane & 15);
         if (row0 < p.dim) {                       /* query */
             const int j = (row % p.hd) >> 1;
@@ -491,29 +529,24 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor 
     return healthy(s) && ok;
 }
 
-/* Query heads owned by this CTA: head h belongs to CTA floor(h C / H),
- * i.e. this CTA owns h in [ceil(c H / C), ceil((c + 1) H / C)). */
-__device__ __forceinline__ void owned_heads(int heads, int &h0, int &h1) {
-    const unsigned H = unsigned(heads), C = gridDim.x, c = blockIdx.x;
-    h0 = int((c * H + C - 1) / C);
-    h1 = int(((c + 1) * H + C - 1) / C);
-}
-
 /* Per-head attention scratch inside the union region. */
 struct HeadScratch {
     float *q;        /* [hd] */
+    float *wm, *wl;  /* [W] per-warp maximum and exp sum of a chunk */
+    float *part;     /* [W][hd] per-warp partial contexts of a chunk */
+    float *cur;      /* [2 hd] current k and v while pos is past the chunk */
+    float *w;        /* [CH] exp weights */
     float *Kt, *Vt;  /* [CH][hd + 1] (padded rows: conflict-free) */
-    float *w;        /* [CH] scores, then exp weights */
-    float *part;     /* [NT] partial context sums */
-    float *stat;     /* [2]: running max, running sum */
     int CH;
     __device__ HeadScratch(const Shared &s, const MkParams &p) {
         const int hd = p.hd, ld = hd + 1;
         q = s.uni;
-        stat = q + hd;
-        part = stat + 2;
-        w = part + NT;
-        const int used = hd + 2 + NT;
+        wm = q + hd;
+        wl = wm + W;
+        part = wl + W;
+        cur = part + W * hd;
+        w = cur + 2 * hd;
+        const int used = hd + 2 * W + W * hd + 2 * hd;
         CH = (p.union_floats - used) / (2 * ld + 1);
         if (CH > NT)
             CH = NT;
@@ -538,85 +571,61 @@ __device__ __forceinline__ void head_fetch(const HeadScratch &t, const MkParams 
     }
 }
 
-/* Block-wide max / sum over the consumer threads (all threads get it). */
-__device__ __forceinline__ float cmax(const Shared &s, float v) {
-    v = warp_max(v);
-    if ((threadIdx.x & 31) == 0)
-        s.wsum[threadIdx.x >> 5] = v;
-    cbar();
-    float t = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < W; w++)
-        t = fmaxf(t, s.wsum[w]);
-    cbar();
-    return t;
-}
-
-/* ATT: the heads this CTA owns, each over positions 0..pos in chunks
- * (attention_step, src/quant_model.cpp:68-105: scores q.k / sqrt(hd),
- * exp(score - max), weights / total, context); the context of head h is
- * published as tagged elements ctx[h hd .. h hd + hd). */
-__device__ bool phase_att(const Shared &s, const MkParams &p, Trace &tr, int i, int l,
-                          int pos) {
-    const int H = p.heads, hd = p.hd, ld = hd + 1, G = p.heads / p.kv_heads;
-    const uint32_t tag_in = tag_of(p, i, l, 0), tag = tag_of(p, i, l, 1);
+/* Attention of query head h at position pos (attention_step,
+ * src/quant_model.cpp:68-105: scores q.k / sqrt(hd), exp(score - max),
+ * weights / total, context) over positions 0..pos in chunks of CH, with
+ * the current q, k and v taken from the tagged q|k|v vector (tag tag_in):
+ * the head's context vector into out[0, hd).  Within a chunk warp w takes
+ * positions 32 w .. 32 w + 31 (one per lane): scores, the warp's maximum
+ * and exp sum by shuffles, and its partial context (each lane owning dims
+ * lane, lane + 32, ...); threads d < hd then merge the warps' partials into
+ * a running (maximum, sum, context) carried across chunks.  Collective. */
+__device__ bool head_context(const Shared &s, const MkParams &p, int l, int h, int pos,
+                             uint32_t tag_in, float *out) {
+    const int hd = p.hd, ld = hd + 1, G = p.heads / p.kv_heads;
     const float scale = 1.0f / sqrtf(float(hd));
     const HeadScratch t(s, p);
-    const int slices = NT / hd; /* position slices in the context sum */
-    int h_first, h_last;
-    owned_heads(H, h_first, h_last);
-    for (int h = h_first; h < h_last; h++) {
-        const int g = h / G;
-        /* history does not depend on this token: fetch it first */
-        head_fetch(t, p, l, g, 0, min(t.CH, pos + 1), pos);
-        /* q of head h and the current k, v of kv head g */
-        bool ok = true;
-        if (threadIdx.x < 3 * hd) {
-            const int part = threadIdx.x / hd, d = threadIdx.x - part * hd;
-            const int row = part == 0 ? h * hd + d
-                                      : p.dim + (part - 1) * p.kvd + g * hd + d;
-            float v;
-            ok = wait_tag<false>(p.qkv + row, tag_in, p.limit_ns, v);
-            if (ok) {
-                if (part == 0)
-                    t.q[d] = v;
-                else if (pos < t.CH)
-                    (part == 1 ? t.Kt : t.Vt)[pos * ld + d] = v;
-                else
-                    t.part[d + (part - 1) * hd] = v; /* kept for its chunk */
-            } else {
-                fatal(s, p, kErrTimeoutInput);
+    const int g = h / G, lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+    /* history does not depend on this token: fetch it first */
+    head_fetch(t, p, l, g, 0, min(t.CH, pos + 1), pos);
+    /* q of head h and the current k, v of kv head g */
+    if (threadIdx.x < 3 * hd) {
+        const int part = threadIdx.x / hd, d = threadIdx.x - part * hd;
+        const int row = part == 0 ? h * hd + d : p.dim + (part - 1) * p.kvd + g * hd + d;
+        float v;
+        if (wait_tag<false>(p.qkv + row, tag_in, p.limit_ns, v)) {
+            if (part == 0)
+                t.q[d] = v;
+            else if (pos < t.CH)
+                (part == 1 ? t.Kt : t.Vt)[pos * ld + d] = v;
+            else
+                t.cur[d + (part - 1) * hd] = v; /* kept for its chunk */
+        } else {
+            fatal(s, p, kErrTimeoutInput);
+        }
+    }
+    __threadfence(); /* acquire: the tags order the older cache rows */
+    if (!healthy(s)) {
+        cp_async_wait_all();
+        return false;
+    }
+    float m = -INFINITY, total = 0.0f, acc = 0.0f; /* running state of dim threadIdx.x */
+    for (int p0 = 0; p0 <= pos; p0 += t.CH) {
+        const int n = min(t.CH, pos + 1 - p0);
+        if (p0 > 0) {
+            head_fetch(t, p, l, g, p0, n, pos);
+            if (pos >= p0 && pos < p0 + n && threadIdx.x < hd) {
+                t.Kt[(pos - p0) * ld + threadIdx.x] = t.cur[threadIdx.x];
+                t.Vt[(pos - p0) * ld + threadIdx.x] = t.cur[hd + threadIdx.x];
             }
         }
-        __threadfence(); /* acquire: the tags order the older cache rows */
-        if (!healthy(s)) {
-            cp_async_wait_all();
-            return false;
-        }
-        if (threadIdx.x == 0)
-            tr.mark(2);
-        float m = -INFINITY, total = 0.0f, acc = 0.0f; /* acc: ctx[d] of slice */
-        const int d_own = threadIdx.x % hd, sl = threadIdx.x / hd;
-        float kcur = 0.0f, vcur = 0.0f;
-        if (pos >= t.CH && threadIdx.x < hd) {
-            kcur = t.part[threadIdx.x];
-            vcur = t.part[hd + threadIdx.x];
-        }
+        cp_async_wait_all();
         cbar();
-        for (int p0 = 0; p0 <= pos; p0 += t.CH) {
-            const int n = min(t.CH, pos + 1 - p0);
-            if (p0 > 0) {
-                head_fetch(t, p, l, g, p0, n, pos);
-                if (pos >= p0 && pos < p0 + n && threadIdx.x < hd) {
-                    t.Kt[(pos - p0) * ld + threadIdx.x] = kcur;
-                    t.Vt[(pos - p0) * ld + threadIdx.x] = vcur;
-                }
-            }
-            cp_async_wait_all();
-            cbar();
+        const int j0 = 32 * wi, j = j0 + lane;
+        if (j0 < n) {
             float sc = -INFINITY;
-            if (threadIdx.x < n) {
-                const float *kj = t.Kt + threadIdx.x * ld;
+            if (j < n) {
+                const float *kj = t.Kt + j * ld;
                 float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
                 int d = 0;
                 for (; d + 4 <= hd; d += 4) {
@@ -629,177 +638,203 @@ __device__ bool phase_att(const Shared &s, const MkParams &p, Trace &tr, int i, 
                     a0 = fmaf(t.q[d], kj[d], a0);
                 sc = ((a0 + a1) + (a2 + a3)) * scale;
             }
-            const float m_new = fmaxf(m, cmax(s, sc));
-            const float e = threadIdx.x < n ? expf(sc - m_new) : 0.0f;
-            if (threadIdx.x < n)
-                t.w[threadIdx.x] = e;
-            const float alpha = expf(m - m_new);
-            total = total * alpha + csum(s, e); /* csum's barriers publish w */
-            m = m_new;
-            acc *= alpha;
-            if (sl < slices)
-                for (int j = sl; j < n; j += slices)
-                    acc = fmaf(t.w[j], t.Vt[j * ld + d_own], acc);
-            cbar();
+            const float mw = warp_max(sc);
+            const float e = j < n ? expf(sc - mw) : 0.0f;
+            const float lw = warp_sum(e);
+            if (j < n)
+                t.w[j] = e;
+            __syncwarp();
+            const int jn = min(32, n - j0);
+            for (int d = lane; d < hd; d += 32) {
+                const float *vj = t.Vt + j0 * ld + d;
+                const float *ew = t.w + j0;
+                float c = 0.0f;
+                for (int k = 0; k < jn; k++)
+                    c = fmaf(ew[k], vj[k * ld], c);
+                t.part[wi * hd + d] = c;
+            }
+            if (lane == 0) {
+                t.wm[wi] = mw;
+                t.wl[wi] = lw;
+            }
         }
-        tr.mark(3);
-        if (sl < slices)
-            t.part[threadIdx.x] = acc;
         cbar();
-        tr.mark(4);
         if (threadIdx.x < hd) {
-            float c = 0.0f;
-            for (int k = 0; k < slices; k++)
-                c += t.part[k * hd + threadIdx.x];
-            st_relaxed(p.ctx + h * hd + threadIdx.x, c / total, tag);
+            const int nw = (n + 31) / 32;
+            float mc = m;
+            for (int k = 0; k < nw; k++)
+                mc = fmaxf(mc, t.wm[k]);
+            const float f0 = expf(m - mc);
+            float tn = total * f0, an = acc * f0;
+            for (int k = 0; k < nw; k++) {
+                const float f = expf(t.wm[k] - mc);
+                tn = fmaf(t.wl[k], f, tn);
+                an = fmaf(t.part[k * hd + threadIdx.x], f, an);
+            }
+            m = mc;
+            total = tn;
+            acc = an;
         }
-        cbar();
-        tr.mark(5);
+        cbar(); /* tiles and partials are reused by the next chunk */
     }
+    if (threadIdx.x < hd)
+        out[threadIdx.x] = acc / total;
+    cbar();
     return true;
 }
 
-/* Residual inputs of this CTA's rows, loaded without waiting before the
- * phase input is polled (their tags are normally complete by then) and
- * parked in `res` (at most kResRows rows; later rows are read in the
- * epilogue). */
-constexpr int kResRows = 64;
-
-__device__ __forceinline__ uint64_t res_issue(const Tagged *src, int row0, int nrows) {
-    return threadIdx.x < nrows && threadIdx.x < kResRows
-               ? ld_relaxed(src + row0 + threadIdx.x)
-               : 0ull;
-}
-
-__device__ __forceinline__ void res_park(const Shared &s, const MkParams &p,
-                                         const Tagged *src, int row0, int nrows,
-                                         uint32_t tag, uint64_t x) {
-    if (threadIdx.x < nrows && threadIdx.x < kResRows) {
-        float v = __uint_as_float(uint32_t(x));
-        if (uint32_t(x >> 32) != tag &&
-            !wait_tag<false>(src + row0 + threadIdx.x, tag, p.limit_ns, v))
-            fatal(s, p, kErrTimeoutInput);
-        s.res[threadIdx.x] = v;
-    }
-}
-
+/* ATTWO (hA = h + Wo ctx), split by K: CTA c < count_aw owns the block pair
+ * P = c / cpp (ctx columns 64 P .. 64 P + 63) for share c mod cpp of Wo's
+ * row tiles.  It computes the attention of every head those columns cover
+ * (a head may be computed by several CTAs), multiplies its Wo tiles, adds
+ * the residual rows when P == 0, and adds its rows into step 2 (i L + l). */
 template <int TYPE, int STAGES>
-__device__ bool phase_wo(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
-                         RowReduce &rr, int i, int l, int token) {
-    int a, b;
-    share(p.rt_wo, a, b);
-    if (a == b)
+__device__ bool phase_attwo(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
+                            int i, int l, int token, int pos) {
+    const int c = blockIdx.x;
+    if (c >= p.count_aw)
         return true;
-    const int row0 = a * 16, nrows = (b - a) * 16;
-    const uint32_t tag = tag_of(p, i, l, 2), tag_in = l > 0 ? tag_of(p, i, l - 1, 4) : 0;
-    const uint64_t pre = l > 0 ? res_issue(p.hB, row0, nrows) : 0ull;
-    if (l == 0 && threadIdx.x < nrows && threadIdx.x < kResRows)
-        s.res[threadIdx.x] = p.emb[size_t(token) * p.dim + row0 + threadIdx.x];
-    float ss;
-    warp_slice<TYPE>(s, p, p.ctx, nullptr, p.dim, p.nb_dim, tag_of(p, i, l, 1), nullptr, ss);
-    if (l > 0)
-        res_park(s, p, p.hB, row0, nrows, tag_in, pre);
+    const int P = c / p.cpp, part = c - P * p.cpp;
+    int a, b;
+    share_of(p.rt_wo, part, p.cpp, a, b);
+    const int st = step_of(p, i, l, 0);
+    const uint32_t tag_in = qkv_tag(p, i, l);
+    /* P == 0 adds the residual rows: the embedding row at layer 0, else hB of
+     * layer l - 1.  Their loads are issued first and land during the
+     * attention; rows past kResRegs * NT (only when cpp is small) are read
+     * at the end. */
+    const int nrows = (b - a) * 16;
+    const float *res = nullptr;
+    float resv[kResRegs];
+    if (P == 0) {
+        if (l > 0 && !wait_step(s, p, st - 1))
+            return false;
+        res = (l == 0 ? p.emb + size_t(token) * p.dim : slot_of(p, st - 1)) + a * 16;
+#pragma unroll
+        for (int j = 0; j < kResRegs; j++) {
+            const int r = int(threadIdx.x) + j * NT;
+            resv[j] = r < nrows ? __ldcg(res + r) : 0.0f;
+        }
+    }
+    float *xs = s.xvec, *hc = s.xvec + 64;
+    const int e0 = 64 * P;
+    if (threadIdx.x < 64)
+        xs[threadIdx.x] = 0.0f;
+    const int h0 = e0 / p.hd, h1 = min(p.heads - 1, (e0 + 63) / p.hd);
+    for (int h = h0; h <= h1; h++) {
+        if (!head_context(s, p, l, h, pos, tag_in, hc))
+            return false;
+        if (threadIdx.x < 64) {
+            const int e = e0 + threadIdx.x;
+            if (e < p.dim && e / p.hd == h)
+                xs[threadIdx.x] = hc[e - h * p.hd];
+        }
+        cbar();
+    }
     tr.mark(2);
+    const int w = threadIdx.x >> 5;
+    if (w < 2)
+        digit_block(xs, 64, w, s.dig, s.fac, TYPE == 1 ? 1.0f / 16.0f : 1.0f);
+    cbar();
+    tr.mark(4);
     constexpr int TB = TileGeom<TYPE>::kTileBytes;
     const MkLayerPtrs &L = p.layer[l];
-    const TileRun run{L.wo + size_t(a) * p.nb_dim * TB, L.wo_s + size_t(a) * p.nb_dim * 16,
-                      (b - a) * p.nb_dim, p.nb_dim};
-    const int lane = threadIdx.x & 31;
-    auto epi = [&](int rt, float y) {
-        const int k = rt * 16 + lane, row = row0 + k;
-        if (lane >= 16)
-            return;
-        float h;
-        if (k < kResRows)
-            h = s.res[k];
-        else if (l == 0)
-            h = p.emb[size_t(token) * p.dim + row];
-        else if (!wait_tag<false>(p.hB + row, tag_in, p.limit_ns, h)) {
-            fatal(s, p, kErrTimeoutInput);
-            return;
-        }
-        st_relaxed(p.hA + row, h + y, tag);
-    };
-    const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi,
-                                                 tr.wait_acc());
+    const size_t t0 = (size_t(P) * p.rt_wo + a) * 2;
+    const TileRun run{L.wo + t0 * TB, L.wo_s + t0 * 16, (b - a) * 2, 2};
+    const bool ok = consume_cols<TYPE, W, STAGES, true>(s.ring, run, cur, s.dig, s.fac, 1,
+                                                        s.yacc, w, tr.wait_acc());
     tr.mark(5);
     tr.put_wait();
+    if (P == 0) {
+        cbar(); /* every row of yacc written */
+#pragma unroll
+        for (int j = 0; j < kResRegs; j++) {
+            const int r = int(threadIdx.x) + j * NT;
+            if (r < nrows)
+                s.yacc[r] += resv[j];
+        }
+        for (int r = int(threadIdx.x) + kResRegs * NT; r < nrows; r += NT)
+            s.yacc[r] += __ldcg(res + r);
+    }
+    finish_step(s, p, st, a * 16, nrows, c, p.count_aw);
     return healthy(s) && ok;
 }
 
+/* GUDOWN (hB = hA + Wdown silu(gate) * up), split by FFN block: CTA
+ * c < count_gd owns blocks [j0, j1) (32 hidden units each): the gate and up
+ * rows of those units (row tiles 4 j0 .. 4 j1 of the interleaved matrix),
+ * SwiGLU into shared memory (src/quant_model.cpp:197-198), then columns
+ * 32 j0 .. 32 j1 of Wdown, plus its share of the residual rows, added into
+ * step 2 (i L + l) + 1. */
 template <int TYPE, int STAGES>
-__device__ bool phase_gu(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
-                         RowReduce &rr, int i, int l) {
-    int a, b;
-    share(p.rt_gu, a, b);
-    if (a == b)
+__device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
+                             RowReduce &rr, int i, int l) {
+    const int c = blockIdx.x;
+    if (c >= p.count_gd)
         return true;
+    int j0, j1;
+    share_of(p.nbf, c, p.count_gd, j0, j1);
+    const int st = step_of(p, i, l, 1);
+    if (!wait_step(s, p, st - 1))
+        return false;
+    const float *hA = slot_of(p, st - 1);
+    /* this CTA's share of the residual rows, loaded alongside the slice */
+    int r0, r1;
+    share_of(p.dim / 16, c, p.count_gd, r0, r1);
+    float resv[kResRegs];
+#pragma unroll
+    for (int j = 0; j < kResRegs; j++) {
+        const int r = r0 * 16 + int(threadIdx.x) + j * NT;
+        resv[j] = r < r1 * 16 ? __ldcg(hA + r) : 0.0f;
+    }
     float ss;
-    if (!warp_slice<TYPE>(s, p, p.hA, nullptr, p.dim, p.nb_dim, tag_of(p, i, l, 2),
-                          p.ffn_norm + size_t(l) * p.dim, ss))
-        ss = 0.0f;
+    warp_slice<TYPE>(s, hA, p.dim, p.nb_dim, p.ffn_norm + size_t(l) * p.dim, ss);
     slice_ss(s, ss);
+    for (int r = threadIdx.x; r < p.dim + 32; r += NT)
+        s.yacc[r] = 0.0f;
+    cbar(); /* zeroing and the residual rows use different thread mappings */
+#pragma unroll
+    for (int j = 0; j < kResRegs; j++) {
+        const int r = r0 * 16 + int(threadIdx.x) + j * NT;
+        if (r < r1 * 16)
+            s.yacc[r] = resv[j];
+    }
+    for (int r = r0 * 16 + int(threadIdx.x) + kResRegs * NT; r < r1 * 16; r += NT)
+        s.yacc[r] = __ldcg(hA + r);
     tr.mark(2);
     constexpr int TB = TileGeom<TYPE>::kTileBytes;
     const MkLayerPtrs &L = p.layer[l];
+    const int a = 4 * j0, b = 4 * j1;
     const TileRun run{L.gu + size_t(a) * p.nb_dim * TB, L.gu_s + size_t(a) * p.nb_dim * 16,
                       (b - a) * p.nb_dim, p.nb_dim};
-    const uint32_t tag = tag_of(p, i, l, 3);
-    const int lane = threadIdx.x & 31;
-    /* tile rt: lanes 0-7 gate rows, lanes 8-15 up rows of units 8 R .. 8 R + 7;
-     * a = silu(gate) * up (src/quant_model.cpp:197-198) */
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    /* tile rt: lanes 0-7 gate rows, lanes 8-15 up rows of units 8 rt .. 8 rt + 7
+     * of the owned blocks */
+    float nsc = -1.0f; /* the rmsnorm scale, computed at the first epilogue */
     auto epi = [&](int rt, float y) {
-        y *= norm_scale(s, p.dim);
+        if (nsc < 0.0f)
+            nsc = norm_scale(s, p.dim);
+        y *= nsc;
         const float up = __shfl_down_sync(0xffffffffu, y, 8);
         if (lane < 8)
-            st_relaxed(p.act + (a + rt) * 8 + lane, y / (1.0f + expf(-y)) * up, tag);
+            s.actv[rt * 8 + lane] = y / (1.0f + expf(-y)) * up;
     };
-    const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi,
-                                                 tr.wait_acc());
+    bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr, w, kBar, epi,
+                                           tr.wait_acc());
+    cbar(); /* every SwiGLU output written; the GU digits are free */
+    const int nblk = j1 - j0;
+    for (int k = w; k < nblk; k += W)
+        digit_block(s.actv, nblk * 32, k, s.dig, s.fac, TYPE == 1 ? 1.0f / 16.0f : 1.0f);
+    cbar();
+    tr.mark(4);
+    const size_t t0 = size_t(j0) * size_t(2 * p.rt_down_pairs);
+    const TileRun down{L.down + t0 * TB, L.down_s + t0 * 16, nblk * 2 * p.rt_down_pairs, 1};
+    ok = consume_cols<TYPE, W, STAGES, false>(s.ring, down, cur, s.dig, s.fac,
+                                              p.rt_down_pairs, s.yacc, w, tr.wait_acc()) &&
+         ok;
     tr.mark(5);
     tr.put_wait();
-    return healthy(s) && ok;
-}
-
-template <int TYPE, int STAGES>
-__device__ bool phase_down(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
-                           RowReduce &rr, int i, int l) {
-    int a, b;
-    share(p.rt_down, a, b);
-    if (a == b)
-        return true;
-    const int row0 = a * 16, nrows = (b - a) * 16;
-    const uint32_t tag = tag_of(p, i, l, 4), tag_in = tag_of(p, i, l, 2);
-    const uint64_t pre = res_issue(p.hA, row0, nrows);
-    float ss;
-    warp_slice<TYPE>(s, p, p.act, nullptr, p.ffn, p.nb_ffn, tag_of(p, i, l, 3), nullptr, ss);
-    res_park(s, p, p.hA, row0, nrows, tag_in, pre);
-    tr.mark(2);
-    constexpr int TB = TileGeom<TYPE>::kTileBytes;
-    const MkLayerPtrs &L = p.layer[l];
-    const TileRun run{L.down + size_t(a) * p.nb_ffn * TB,
-                      L.down_s + size_t(a) * p.nb_ffn * 16, (b - a) * p.nb_ffn, p.nb_ffn};
-    const int lane = threadIdx.x & 31;
-    auto epi = [&](int rt, float y) {
-        const int k = rt * 16 + lane, row = row0 + k;
-        if (lane >= 16)
-            return;
-        float h;
-        if (k < kResRows)
-            h = s.res[k];
-        else if (!wait_tag<false>(p.hA + row, tag_in, p.limit_ns, h)) {
-            fatal(s, p, kErrTimeoutInput);
-            return;
-        }
-        st_relaxed(p.hB + row, h + y, tag);
-    };
-    const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
-                                                 threadIdx.x >> 5, kBar, epi,
-                                                 tr.wait_acc());
-    tr.mark(5);
-    tr.put_wait();
+    finish_step(s, p, st, 0, p.dim, c, p.count_gd);
     return healthy(s) && ok;
 }
 
@@ -817,8 +852,10 @@ __device__ bool phase_lmhead(const Shared &s, const MkParams &p, Trace &tr, Curs
     if (a < b) {
         NormW nw;
         nw.load(p.final_norm, p.dim);
-        if (!poll<false>(s, p, p.hB, p.dim, tag_of(p, i, p.layers - 1, 4), s.xvec))
+        const int last = step_of(p, i, p.layers - 1, 1);
+        if (!wait_step(s, p, last))
             return false;
+        stage_slot(slot_of(p, last), p.dim, s.xvec);
         if (i == p.n_prompt - 1 && blockIdx.x == 0 && threadIdx.x == 0)
             p.stamps[1] = global_ns(); /* every layer of the prompt is done */
         tr.mark(2);
@@ -914,6 +951,7 @@ __device__ __forceinline__ bool wants_logits(const MkParams &p, int i) {
 template <int TYPE, int STAGES>
 __device__ void producer(const Shared &s, const MkParams &p) {
     constexpr int TB = TileGeom<TYPE>::kTileBytes;
+    const int c = blockIdx.x;
     Cursor cur;
     for (int i = 0; i < p.n_tokens; i++) {
         for (int l = 0; l < p.layers; l++) {
@@ -925,25 +963,28 @@ __device__ void producer(const Shared &s, const MkParams &p) {
                     TileRun{L.qkv + size_t(a) * p.nb_dim * TB, L.qkv_s + size_t(a) * p.nb_dim * 16,
                             (b - a) * p.nb_dim, p.nb_dim}, cur))
                 return;
-            share(p.rt_wo, a, b);
-            if (a < b &&
-                !produce_run_c<TYPE, STAGES>(s.ring,
-                    TileRun{L.wo + size_t(a) * p.nb_dim * TB, L.wo_s + size_t(a) * p.nb_dim * 16,
-                            (b - a) * p.nb_dim, p.nb_dim}, cur))
-                return;
-            share(p.rt_gu, a, b);
-            if (a < b &&
-                !produce_run_c<TYPE, STAGES>(s.ring,
-                    TileRun{L.gu + size_t(a) * p.nb_dim * TB, L.gu_s + size_t(a) * p.nb_dim * 16,
-                            (b - a) * p.nb_dim, p.nb_dim}, cur))
-                return;
-            share(p.rt_down, a, b);
-            if (a < b &&
-                !produce_run_c<TYPE, STAGES>(s.ring,
-                    TileRun{L.down + size_t(a) * p.nb_ffn * TB,
-                            L.down_s + size_t(a) * p.nb_ffn * 16, (b - a) * p.nb_ffn, p.nb_ffn},
-                    cur))
-                return;
+            if (c < p.count_aw) {
+                const int P = c / p.cpp;
+                share_of(p.rt_wo, c - P * p.cpp, p.cpp, a, b);
+                const size_t t0 = (size_t(P) * p.rt_wo + a) * 2;
+                if (!produce_run_c<TYPE, STAGES>(s.ring,
+                        TileRun{L.wo + t0 * TB, L.wo_s + t0 * 16, (b - a) * 2, 2}, cur))
+                    return;
+            }
+            if (c < p.count_gd) {
+                int j0, j1;
+                share_of(p.nbf, c, p.count_gd, j0, j1);
+                if (!produce_run_c<TYPE, STAGES>(s.ring,
+                        TileRun{L.gu + size_t(4 * j0) * p.nb_dim * TB,
+                                L.gu_s + size_t(4 * j0) * p.nb_dim * 16,
+                                4 * (j1 - j0) * p.nb_dim, p.nb_dim}, cur))
+                    return;
+                const size_t t0 = size_t(j0) * size_t(2 * p.rt_down_pairs);
+                if (!produce_run_c<TYPE, STAGES>(s.ring,
+                        TileRun{L.down + t0 * TB, L.down_s + t0 * 16,
+                                (j1 - j0) * 2 * p.rt_down_pairs, 1}, cur))
+                    return;
+            }
         }
         if (wants_logits(p, i)) {
             int a, b;
@@ -989,13 +1030,16 @@ __global__ void __launch_bounds__(THREADS, 1) decode_mk_kernel(const MkParams p)
     RowReduce rr{s.red, 0};
     Cursor cur;
     int occ = 0;
+    bool alive = true;
     for (int i = 0; i < p.n_tokens; i++) {
         const int pos = p.start_pos + i;
         int token = 0;
         if (i < p.n_prompt)
             token = p.prompt[i];
-        else if (!next_token(s, p, i, token))
+        else if (!next_token(s, p, i, token)) {
+            alive = false;
             break;
+        }
         bool ok = true;
         Trace tr;
         for (int l = 0; l < p.layers && ok; l++) {
@@ -1005,22 +1049,12 @@ __global__ void __launch_bounds__(THREADS, 1) decode_mk_kernel(const MkParams p)
             if (!ok)
                 break;
             tr.open(p, occ++, 1);
-            ok = phase_att(s, p, tr, i, l, pos);
+            ok = phase_attwo<TYPE, STAGES>(s, p, tr, cur, i, l, token, pos);
             tr.mark(7);
             if (!ok)
                 break;
             tr.open(p, occ++, 2);
-            ok = phase_wo<TYPE, STAGES>(s, p, tr, cur, rr, i, l, token);
-            tr.mark(7);
-            if (!ok)
-                break;
-            tr.open(p, occ++, 3);
-            ok = phase_gu<TYPE, STAGES>(s, p, tr, cur, rr, i, l);
-            tr.mark(7);
-            if (!ok)
-                break;
-            tr.open(p, occ++, 4);
-            ok = phase_down<TYPE, STAGES>(s, p, tr, cur, rr, i, l);
+            ok = phase_gudown<TYPE, STAGES>(s, p, tr, cur, rr, i, l);
             tr.mark(7);
         }
         if (ok && wants_logits(p, i)) {
@@ -1028,8 +1062,17 @@ __global__ void __launch_bounds__(THREADS, 1) decode_mk_kernel(const MkParams p)
             ok = phase_lmhead<STAGES>(s, p, tr, cur, i);
             tr.mark(7);
         }
-        if (!ok)
+        if (!ok) {
+            alive = false;
             break;
+        }
+    }
+    /* the last hidden vector (hB of the last layer of the last token) */
+    if (alive && blockIdx.x == 0) {
+        const int last = step_of(p, p.n_tokens - 1, p.layers - 1, 1);
+        if (wait_step(s, p, last))
+            for (int k = threadIdx.x; k < p.dim; k += NT)
+                p.hidden_out[k] = __ldcg(slot_of(p, last) + k);
     }
     if (threadIdx.x == 0)
         atomicMax(p.stamps + 2, static_cast<unsigned long long>(global_ns()));
@@ -1044,19 +1087,20 @@ size_t fixed_smem(int stages, int dim, int ffn) {
 }
 
 /* Mirrors carve(): every piece after the union is 16-byte aligned. */
-size_t tail_smem(int stages) {
+size_t tail_smem(int stages, int dim) {
     auto align16 = [](size_t o) { return (o + 15) & ~size_t(15); };
     size_t off = align16(2 * kRowBatch * W * 16 * 4);
     off = align16(off + W * 4);
     off = align16(off + W * 8);
     off = align16(off + 16);
-    off = align16(off + 64 * 4);
+    off = align16(off + size_t(dim + 32) * 4);
+    off = align16(off + kMaxFfnBlocks * 32 * 4);
     return off + size_t(stages) * 16 + 64; /* barriers, and slack */
 }
 
 /* Per-head attention scratch floats for a chunk of `ch` positions. */
 size_t att_floats(int hd, int ch) {
-    return size_t(hd) + 2 + NT + size_t(ch) * (2 * size_t(hd + 1) + 1);
+    return size_t(hd) * (3 + W) + 2 * W + size_t(ch) * (2 * size_t(hd + 1) + 1);
 }
 
 template <int TYPE, int STAGES>
@@ -1078,7 +1122,7 @@ cudaError_t launch_t(MkParams p, int sms, size_t smem, cudaStream_t stream) {
 bool plan(int dim, int ffn, int hd, int nbmax, int max_smem, int &stages,
           size_t &union_bytes, int &chunk) {
     for (int st : {8, 6, 4}) {
-        const size_t fixed = fixed_smem(st, dim, ffn) + tail_smem(st);
+        const size_t fixed = fixed_smem(st, dim, ffn) + tail_smem(st, dim);
         if (fixed >= size_t(max_smem))
             continue;
         const size_t avail = (size_t(max_smem) - fixed) & ~size_t(15);
@@ -1086,7 +1130,7 @@ bool plan(int dim, int ffn, int hd, int nbmax, int max_smem, int &stages,
             continue;
         stages = st;
         union_bytes = avail;
-        chunk = int((avail / 4 - (size_t(hd) + 2 + NT)) / (2 * size_t(hd + 1) + 1));
+        chunk = int((avail / 4 - (size_t(hd) * (3 + W) + 2 * W)) / (2 * size_t(hd + 1) + 1));
         return true;
     }
     return false;
@@ -1095,12 +1139,21 @@ bool plan(int dim, int ffn, int hd, int nbmax, int max_smem, int &stages,
 } // namespace
 
 bool mk_supported(int dim, int ffn, int kvd, int head_dim, int heads, int type,
-                  int max_smem) {
+                  int max_smem, int sms) {
     (void)type;
     /* row tiles never straddle the q / k / v boundaries (dim and kv_dim
-     * multiples of 16), every classifier row fits one stage */
+     * multiples of 16), every classifier row fits one stage, the staging
+     * vector holds a context pair and one head, and no CTA owns more FFN
+     * blocks than kMaxFfnBlocks */
     if (dim % 32 != 0 || ffn % 32 != 0 || kvd % 16 != 0 || dim * 4 > kStageBytes ||
-        head_dim % 2 != 0 || head_dim > 256 || heads % (kvd / head_dim) != 0)
+        head_dim % 2 != 0 || head_dim > 256 || heads % (kvd / head_dim) != 0 ||
+        dim < 64 + head_dim || sms <= 0)
+        return false;
+    const int nbf = ffn / 32, cgd = nbf < sms ? nbf : sms;
+    if ((nbf + cgd - 1) / cgd > kMaxFfnBlocks)
+        return false;
+    /* every Wo block pair needs its own CTA (the step counts them all) */
+    if ((dim / 32 + 1) / 2 > sms)
         return false;
     const int nb_dim = ((dim / 32) + 1) / 2 * 2, nb_ffn = ((ffn / 32) + 1) / 2 * 2;
     int stages, chunk;
@@ -1121,7 +1174,7 @@ cudaError_t launch_decode_mk(const MkParams &pin, int type, int sms, cudaStream_
         return cudaErrorInvalidConfiguration;
     p.att_chunk = chunk;
     p.union_floats = int(ub / 4);
-    const size_t smem = fixed_smem(stages, p.dim, p.ffn) + ub + tail_smem(stages);
+    const size_t smem = fixed_smem(stages, p.dim, p.ffn) + ub + tail_smem(stages, p.dim);
     if (type == 1) {
         if (stages == 8)
             return launch_t<1, 8>(p, sms, smem, stream);

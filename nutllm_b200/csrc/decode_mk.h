@@ -9,12 +9,19 @@ namespace nut {
 
 /* Weights of one layer in fragment tiles. */
 struct MkLayer {
-    TileMatrix qkv;  /* [dim + 2 kv_dim][dim]: query, key, value rows */
-    TileMatrix wo;   /* [dim][dim] */
+    TileMatrix qkv;  /* [dim + 2 kv_dim][dim]: query, key, value rows,
+                        row-major tiles */
+    TileMatrix wo;   /* [dim][dim], pair-column tiles (split by K pairs) */
     TileMatrix gu;   /* [2 ffn][dim]: gate and up rows interleaved in groups
-                        of 8 (a 16-row tile = gate 8t..8t+7, up 8t..8t+7) */
-    TileMatrix down; /* [dim][ffn] */
+                        of 8 (a 16-row tile = gate 8t..8t+7, up 8t..8t+7),
+                        row-major tiles */
+    TileMatrix down; /* [dim][ffn], block-column tiles (split by K blocks) */
 };
+
+/* Accumulator slots of the split-K reductions (a ring; see decode_mk.cu). */
+constexpr int kAccSlots = 8;
+/* Most FFN blocks (32 hidden units) one CTA may own. */
+constexpr int kMaxFfnBlocks = 4;
 
 /* Device-side view of a layer (pointers only). */
 struct MkLayerPtrs {
@@ -37,7 +44,15 @@ struct MkParams {
     const float *emb;                   /* [vocab][dim] */
     const float *rope_cos, *rope_sin;   /* [max_seq][hd / 2] */
     float *kcache, *vcache;             /* [layers][kv_heads][max_seq][hd] */
-    Tagged *hA, *hB, *qkv, *ctx, *act;  /* tagged vectors */
+    Tagged *qkv;                        /* tagged q | k | v of the current token */
+    float *hacc;                        /* [kAccSlots][dim] residual stream
+                                           accumulators (fp32, red.add) */
+    float *hidden_out;                  /* [dim] last hidden vector */
+    unsigned int *cnt;                  /* [kAccSlots] contributions counted */
+    int wo_pairs, cpp;                  /* K pairs of Wo; CTAs per pair */
+    int count_aw;                       /* CTAs of the attention + Wo step */
+    int nbf, count_gd;                  /* FFN blocks; CTAs of the FFN step */
+    int rt_down_pairs;                  /* row-tile pairs per Wdown block */
     const int *prompt;                  /* [n_prompt] */
     int n_prompt, n_tokens, start_pos;
     int logits_from, logits_to;         /* lm_head after tokens in [from, to] */
@@ -46,8 +61,7 @@ struct MkParams {
     float *logits;                      /* [to - from + 1][vocab] or null */
     int *error;
     unsigned long long *stamps;         /* [3] start, prefill done, end (ns) */
-    unsigned long long *trace;          /* optional [ctas][trace_stride][4]:
-                                           phase id, start, inputs ready, end */
+    unsigned long long *trace;          /* optional [ctas][trace_stride][8] */
     int trace_stride;
     uint64_t limit_ns;
     int att_chunk;                      /* positions per attention chunk */
@@ -60,6 +74,6 @@ cudaError_t launch_decode_mk(const MkParams &p, int type, int sms, cudaStream_t 
 
 /* Whether a model shape can run the persistent kernel on this device. */
 bool mk_supported(int dim, int ffn, int kvd, int head_dim, int heads, int type,
-                  int max_smem);
+                  int max_smem, int sms);
 
 } // namespace nut

@@ -212,12 +212,11 @@ __device__ __forceinline__ bool produce_bytes(const Ring &ring, const uint8_t *s
  * Called by all `warps` consumer warps (warp index w); the block peak is
  * one redux.sync over the magnitudes' bit patterns (order-preserving for
  * non-negative floats). */
-__device__ __forceinline__ void digit_block(const float *x, int K, int b, int8_t *dig,
-                                            float *fac, float a_unit_inv) {
+/* Digits of block b from the lane's value v and the block's peak bits
+ * (the redux of |v| over the warp), for callers that batch the reduxes. */
+__device__ __forceinline__ void digit_from(float v, uint32_t mbits, int b, int8_t *dig,
+                                           float *fac, float a_unit_inv) {
     const int lane = threadIdx.x & 31;
-    const int k = b * 32 + lane;
-    const float v = k < K ? x[k] : 0.0f;
-    const uint32_t mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
     const float m = __uint_as_float(mbits);
     int d1 = 0, d2 = 0, d3 = 0, d4 = 0;
     float f_hi = 0.0f, f_lo = 0.0f;
@@ -244,6 +243,14 @@ __device__ __forceinline__ void digit_block(const float *x, int K, int b, int8_t
         fac[2 * b] = f_hi;
         fac[2 * b + 1] = f_lo;
     }
+}
+
+__device__ __forceinline__ void digit_block(const float *x, int K, int b, int8_t *dig,
+                                            float *fac, float a_unit_inv) {
+    const int k = b * 32 + (threadIdx.x & 31);
+    const float v = k < K ? x[k] : 0.0f;
+    digit_from(v, __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))), b, dig, fac,
+               a_unit_inv);
 }
 
 __device__ __forceinline__ void make_digits(const float *x, int K, int nb, int w,
@@ -425,9 +432,12 @@ __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
         const int end = t + n;
         while (rt_base < end) {
             const int lo = max(t, rt_base), hi = min(end, rt_base + nb);
-            /* pairs of this row tile inside [lo, hi) owned by warp w */
+            /* pairs of this row tile inside [lo, hi) owned by warp w: pair
+             * q of the run (q = rt_base / 2 + p) belongs to warp q mod WARPS,
+             * so the remainder pairs of consecutive row tiles land on
+             * different warps */
             const int p_lo = (lo - rt_base) >> 1, p_hi = (hi - rt_base) >> 1;
-            int p = p_lo + ((w - p_lo % WARPS) + WARPS) % WARPS;
+            int p = p_lo + ((w - ((rt_base >> 1) + p_lo) % WARPS) + WARPS) % WARPS;
             if (poisoned)
                 p = p_hi;
             for (; p + WARPS < p_hi; p += 2 * WARPS) {
@@ -466,6 +476,113 @@ __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
             if (k >= nslot)
                 sg[k] = sg8[k] = 0.0f;
         flush_rows<WARPS>(sg, sg8, nslot, batch_first, rr, w, barrier_id, epi);
+    }
+    return !poisoned;
+}
+
+/* ---- consuming a column-split run ------------------------------------
+
+   Runs of the pair-column and block-column tile orders: the CTA owns a
+   K slice of one or two blocks per row tile, so a row tile's product is
+   finished inside one pair and needs no reduction across warps.  Pair q of
+   the run is tiles (2q, 2q+1):
+     SAME_ROW (pair-column): both tiles are row tile q, blocks 0 and 1 of
+       `dig`; the B operand carries block 0's digits in columns 0-3 and
+       block 1's in 4-7, and the four lanes c of a row group sum to row
+       tile q's rows.  yacc[16 q + r] = result.
+     !SAME_ROW (block-column): pair q covers row tiles 2 lq and 2 lq + 1
+       (lq = q mod pairs_per_block) of block k = q / pairs_per_block; both
+       halves of B carry block k's digits, lanes c = 0, 1 sum row tile 2 lq
+       and lanes c = 2, 3 row tile 2 lq + 1.  yacc[16 (2 lq + h) + r] +=
+       result (blocks accumulate).
+   Warp (SAME_ROW ? q : lq) mod WARPS handles pair q, so every yacc row has
+   a single writer.  Returns false on timeout. */
+template <int TYPE, bool SAME_ROW>
+__device__ __forceinline__ void pair_cols(const uint8_t *stage_data,
+                                          const uint16_t *stage_scales, int tile,
+                                          int blk0, int blk1, const int8_t *dig,
+                                          const float *fac, float &yg, float &yg8) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3, half = c >> 1;
+    uint32_t a0[4], a1[4];
+    load_a<TYPE>(stage_data, tile, a0);
+    load_a<TYPE>(stage_data, tile + 1, a1);
+    const int8_t *src = dig + (g < 4 ? blk0 : blk1) * 128 + (g & 3) * 32 + 4 * c;
+    const uint32_t bx0 = *reinterpret_cast<const uint32_t *>(src);
+    const uint32_t bx1 = *reinterpret_cast<const uint32_t *>(src + 16);
+    int d0[4], d1[4];
+    mma_s8_seeded(d0, a0, bx0, bx1);
+    mma_s8_seeded(d1, a1, bx0, bx1);
+    const int e0 = half ? d1[0] : d0[0], e1 = half ? d1[1] : d0[1];
+    const int e2 = half ? d1[2] : d0[2], e3 = half ? d1[3] : d0[3];
+    const float f0 = __int_as_float(e0) - kMagicF, f1 = __int_as_float(e1) - kMagicF;
+    const float f2 = __int_as_float(e2) - kMagicF, f3 = __int_as_float(e3) - kMagicF;
+    const float tg = fmaf(f0, 128.0f, f1), tg8 = fmaf(f2, 128.0f, f3);
+    const float F = fac[2 * (half ? blk1 : blk0) + (c & 1)];
+    const uint16_t *sc = stage_scales + (tile + half) * 16;
+    yg = tg * (half_bits_to_float(sc[g]) * F);
+    yg8 = tg8 * (half_bits_to_float(sc[g + 8]) * F);
+}
+
+template <int TYPE, int WARPS, int STAGES, bool SAME_ROW>
+__device__ bool consume_cols(const Ring &ring, const TileRun &run, Cursor &cur,
+                             const int8_t *dig, const float *fac, int pairs_per_block,
+                             float *yacc, int w, long long *wait_cycles = nullptr) {
+    using G = TileGeom<TYPE>;
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    bool poisoned = false;
+    for (int t = 0; t < run.tiles; t += G::kChunkTiles) {
+        const int n = min(G::kChunkTiles, run.tiles - t);
+        if (!poisoned)
+            poisoned = *reinterpret_cast<volatile int *>(ring.fatal) != 0;
+        const long long w0 = wait_cycles != nullptr ? clock64() : 0;
+        if (!poisoned && !mbar_wait(&ring.full[cur.stage], cur.parity, ring.limit_ns)) {
+            report(ring.error, kErrTimeoutFull);
+            *reinterpret_cast<volatile int *>(ring.fatal) = 1;
+            poisoned = true;
+        }
+        if (wait_cycles != nullptr)
+            *wait_cycles += clock64() - w0;
+        const uint8_t *sd = ring.data + size_t(cur.stage) * kStageBytes;
+        const uint16_t *ss = ring.scales + size_t(cur.stage) * (kStageScaleBytes / 2);
+        const int q0 = t >> 1, q1 = (t + n) >> 1;
+        if (!poisoned) {
+            if (SAME_ROW) {
+                for (int q = q0 + ((w - q0 % WARPS) + WARPS) % WARPS; q < q1; q += WARPS) {
+                    float y, y8;
+                    pair_cols<TYPE, true>(sd, ss, 2 * q - t, 0, 1, dig, fac, y, y8);
+                    y += __shfl_xor_sync(0xffffffffu, y, 1);
+                    y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+                    y += __shfl_xor_sync(0xffffffffu, y, 2);
+                    y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+                    if (c == 0) {
+                        yacc[16 * q + g] = y;
+                        yacc[16 * q + g + 8] = y8;
+                    }
+                }
+            } else {
+                for (int k = q0 / pairs_per_block; k * pairs_per_block < q1; k++) {
+                    const int base = k * pairs_per_block;
+                    const int lo = max(q0 - base, 0), hi = min(q1 - base, pairs_per_block);
+                    for (int lq = lo + ((w - lo % WARPS) + WARPS) % WARPS; lq < hi;
+                         lq += WARPS) {
+                        float y, y8;
+                        pair_cols<TYPE, false>(sd, ss, 2 * (base + lq) - t, k, k, dig, fac,
+                                               y, y8);
+                        y += __shfl_xor_sync(0xffffffffu, y, 1);
+                        y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+                        if ((c & 1) == 0) {
+                            const int row = 16 * (2 * lq + (c >> 1)) + g;
+                            yacc[row] += y;
+                            yacc[row + 8] += y8;
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && !poisoned)
+            mbar_arrive(&ring.empty[cur.stage]);
+        cur.template next<STAGES>();
     }
     return !poisoned;
 }

@@ -46,7 +46,7 @@ void pack_tiles(const TileShape &s, const uint8_t *data, const uint16_t *scales,
     const int64_t src_blocks = s.cols / 32;
     for (int64_t rt = 0; rt < s.row_tiles; rt++)
         for (int64_t b = 0; b < s.blocks; b++) {
-            const size_t t = size_t(rt * s.blocks + b);
+            const size_t t = s.tile_index(rt, b);
             uint8_t *out = tile_data + t * tb;
             const int64_t r0 = rt * 16, k0 = b * 32;
             for (int lane = 0; lane < 32; lane++) {
@@ -84,7 +84,7 @@ void unpack_tiles(const TileShape &s, const uint8_t *tile_data,
         std::memset(data, 0, size_t((s.rows * s.cols + 1) / 2));
     for (int64_t rt = 0; rt < s.row_tiles; rt++)
         for (int64_t b = 0; b < s.blocks; b++) {
-            const size_t t = size_t(rt * s.blocks + b);
+            const size_t t = s.tile_index(rt, b);
             const uint8_t *in = tile_data + t * tb;
             const int64_t r0 = rt * 16, k0 = b * 32;
             for (int lane = 0; lane < 32; lane++) {

@@ -18,7 +18,17 @@
  *     The kernel widens them with two masks to bytes 16*q (exact signed
  *     int8): a0 = (word0 << 4) & 0xF0F0F0F0, a1 = word0 & 0xF0F0F0F0, ...
  *
- * Scales are stored beside the data as [row tile][block][16] fp16 bits.
+ * Three tile orders serve the three ways a matrix is split across CTAs:
+ *   row-major    [row tile][block]            a CTA owns whole row tiles
+ *   pair-column  [block / 2][row tile][2]     a CTA owns one block pair
+ *                (K columns 64 P .. 64 P + 63) of a range of row tiles
+ *   block-column [block][row tile]            a CTA owns whole K blocks;
+ *                row tiles are padded to an even count so consecutive
+ *                tiles pair up
+ * In every order a CTA's share is one contiguous run of tiles.
+ *
+ * Scales are stored beside the data in the same tile order, 16 fp16 bits
+ * per tile.
  * Rows are padded to a multiple of 16 and blocks to an even count with
  * zero weights and zero scales, which contribute exactly nothing.  The
  * packing is a byte permutation of the reference storage; unpack() inverts
@@ -30,21 +40,35 @@
 
 namespace nut {
 
+enum TileOrder : int { kRowMajor = 0, kPairColumn = 1, kBlockColumn = 2 };
+
 struct TileShape {
     int64_t rows = 0, cols = 0;
     int type = 0;          /* 0 INT8, 1 INT4 */
-    int64_t row_tiles = 0; /* ceil(rows / 16) */
+    int64_t row_tiles = 0; /* ceil(rows / 16) (even for kBlockColumn) */
     int64_t blocks = 0;    /* ceil(cols / 32) rounded up to even */
+    int order = kRowMajor;
 
-    static TileShape of(int64_t rows, int64_t cols, int type) {
+    static TileShape of(int64_t rows, int64_t cols, int type, int order = kRowMajor) {
         TileShape s;
         s.rows = rows;
         s.cols = cols;
         s.type = type;
+        s.order = order;
         s.row_tiles = (rows + 15) / 16;
+        if (order == kBlockColumn)
+            s.row_tiles = (s.row_tiles + 1) / 2 * 2;
         const int64_t b = (cols + 31) / 32;
         s.blocks = (b + 1) / 2 * 2;
         return s;
+    }
+    /* Position of tile (row tile rt, block b) in the stored sequence. */
+    size_t tile_index(int64_t rt, int64_t b) const {
+        if (order == kPairColumn)
+            return size_t(((b >> 1) * row_tiles + rt) * 2 + (b & 1));
+        if (order == kBlockColumn)
+            return size_t(b * row_tiles + rt);
+        return size_t(rt * blocks + b);
     }
     size_t tile_bytes() const { return type == 0 ? 512 : 256; }
     size_t tiles() const { return size_t(row_tiles * blocks); }
