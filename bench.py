@@ -40,6 +40,28 @@ sys.path.insert(0, ROOT)
 
 SEED = 1234
 
+LABELS = {
+    "tinyllama-int4": "TinyLlama-1.1B INT4",
+    "tinyllama-int8-long": "TinyLlama-1.1B INT8, 512-token prompt + 256 steps",
+    "tiny-int8": "tiny dim-288 INT8",
+}
+
+
+def metric_of(wl):
+    return f"decode tok/s ({LABELS.get(wl.name, wl.name)}, batch 1)"
+
+
+def dtype_of(wl, nb):
+    return "int4xfp32" if wl.qtype == nb.INT4 else "int8xfp32"
+
+
+def cpu_sample(wl):
+    """(prompt tokens, greedy steps) the reference CPU runs per sample: the
+    whole workload when it takes seconds, a bounded prefix otherwise."""
+    if wl.prompt + wl.steps > 64:
+        return 64, 8
+    return wl.prompt, wl.steps
+
 
 def parse():
     p = argparse.ArgumentParser()
@@ -210,7 +232,7 @@ def run_ours(args, rank, world, local):
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, c)
     line = {
-        "metric": "decode tok/s (TinyLlama-1.1B INT4, batch 1)",
+        "metric": metric_of(wl),
         "value": round(value, 2),
         "unit": "tok/s",
         "n_gpus": world,
@@ -220,13 +242,14 @@ def run_ours(args, rank, world, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "int4xfp32",
+        "dtype": dtype_of(wl, nb),
         "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
         "config": {"workload": wl.name, "prompt": wl.prompt,
                    "decode_steps": wl.steps, "batch": wl.batch,
                    "parallelism": f"replicas{world}",
-                   "l2": "inputs larger than L2 (807.6 MB of weights and "
-                         "classifier per token)",
+                   "l2": "inputs larger than L2 (%.1f MB of weights and "
+                         "classifier per token)"
+                         % (syn.algorithmic_decode_bytes(c, wl.qtype, 0) / 1e6),
                    "timing": "step: CUDA events on the library stream; "
                              "prefill/decode split: in-kernel device timer"},
         "prefill_tok_s": round(prefill_tps, 2),
@@ -305,22 +328,26 @@ def qmatvec_micro(nb, device, peak):
 
 def cpu_baseline(wl, c):
     """The reference's own CPU loop (oracle/_ref) on this host, all host
-    threads, on the whole workload: the prompt and every greedy step."""
+    threads, on the workload (or a bounded prefix of it, see cpu_sample)."""
     import oracle
     from nutllm_b200 import synthetic as syn
     threads = os.cpu_count() or 1
     if not oracle.reference_available():
         return {"value": None, "unit": "decode tok/s", "cores": threads,
                 "kind": "reference", "sample": "oracle/_ref not built"}
+    n_prompt, n_steps = cpu_sample(wl)
     r = oracle.Reference()
     rm = r.model(c, wl.qtype, SEED)
-    prompt = syn.prompt_ids(c, SEED, wl.prompt)
-    _, _, _, ps, ds = rm.generate(prompt, wl.steps, threads, want_logits=False)
-    return {"value": round(wl.steps / ds, 3), "unit": "decode tok/s",
+    prompt = syn.prompt_ids(c, SEED, n_prompt)
+    _, _, _, ps, ds = rm.generate(prompt, n_steps, threads, want_logits=False)
+    whole = (n_prompt, n_steps) == (wl.prompt, wl.steps)
+    return {"value": round(n_steps / ds, 3), "unit": "decode tok/s",
             "cores": threads, "kind": "reference",
-            "prefill_tok_s": round(wl.prompt / ps, 3),
-            "sample": f"the whole workload once: {wl.prompt}-token prompt + "
-                      f"{wl.steps} greedy decode steps of {wl.name}"}
+            "prefill_tok_s": round(n_prompt / ps, 3),
+            "sample": ("the whole workload once: " if whole else
+                       "a bounded prefix of the workload: ") +
+                      f"{n_prompt}-token prompt + {n_steps} greedy decode "
+                      f"steps of {wl.name}"}
 
 
 # ------------------------------------------------------------- reference
@@ -341,8 +368,8 @@ def run_reference(args, rank, world):
     threads = os.cpu_count() or 1
     r = oracle.Reference()
     rm = r.model(c, wl.qtype, SEED)
-    prompt = syn.prompt_ids(c, SEED, wl.prompt)
-    sample_steps = wl.steps
+    n_prompt, sample_steps = cpu_sample(wl)
+    prompt = syn.prompt_ids(c, SEED, n_prompt)
     for _ in range(min(args.warmup, 1)):
         rm.generate(prompt, 1, threads, want_logits=False)
     dec, pre = 0.0, 0.0
@@ -354,19 +381,19 @@ def run_reference(args, rank, world):
     value = sample_steps * args.steps / dec
     print(json.dumps({
         "impl": "reference",
-        "metric": "decode tok/s (TinyLlama-1.1B INT4, batch 1)",
+        "metric": metric_of(wl),
         "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * (dec + pre) / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4xfp32", "data": "synthetic",
+        "dtype": "int4xfp32" if wl.qtype == 1 else "int8xfp32", "data": "synthetic",
         "config": {"workload": wl.name, "prompt": wl.prompt,
-                   "decode_steps": sample_steps, "batch": 1},
-        "prefill_tok_s": round(wl.prompt * args.steps / pre, 3),
+                   "decode_steps": wl.steps, "batch": 1},
+        "prefill_tok_s": round(n_prompt * args.steps / pre, 3),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s",
                          "cores": threads, "kind": "reference",
-                         "sample": f"{wl.prompt}-token prompt + {sample_steps} "
-                                   f"greedy steps per step"},
+                         "sample": f"{n_prompt}-token prompt + {sample_steps} "
+                                   f"greedy steps of {wl.name} per step"},
         "e2e": {"value": round(value, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)

@@ -102,11 +102,11 @@ def _dequantize(q: nb.QuantizedMatrix) -> np.ndarray:
     return (vals * np.repeat(scales, 32)[:n]).reshape(q.rows, q.cols)
 
 
-def _run(name, orc, gpu, steps=None):
+def _run(name, orc, gpu, steps=None, prompt_len=None):
     wl = syn.WORKLOADS[name]
     c = wl.model_config()
     w = syn.build_model(c, wl.qtype, SEED)
-    prompt = syn.prompt_ids(c, SEED, wl.prompt)
+    prompt = syn.prompt_ids(c, SEED, wl.prompt if prompt_len is None else prompt_len)
     steps = wl.steps if steps is None else steps
     om = orc.model(w)
     ids_o, lg_o, hid_o = om.generate(prompt, steps)
@@ -187,6 +187,19 @@ def test_tinyllama_int4_greedy_ids_and_logits(gpu, orc):
     margin = top2_margin(r["lg_o"])
     assert_logits_close(r["lg_g"], r["lg_o"])
     # ids must agree wherever the oracle's top-2 gap exceeds the tolerance
+    first_close = next((i for i, m in enumerate(margin) if m < 2 * LOGIT_ATOL),
+                       len(margin))
+    assert np.array_equal(r["ids_g"][:first_close], r["ids_o"][:first_close])
+
+
+@pytest.mark.slow
+def test_tinyllama_int8_long_context(gpu, orc):
+    """BASELINE config 3's shape (TinyLlama INT8) at a 200-token prompt: the
+    attention spans several position chunks per head and the KV history is
+    read back across many tokens."""
+    r = _run("tinyllama-int8-long", orc, gpu, steps=8, prompt_len=200)
+    margin = top2_margin(r["lg_o"])
+    assert_logits_close(r["lg_g"], r["lg_o"])
     first_close = next((i for i, m in enumerate(margin) if m < 2 * LOGIT_ATOL),
                        len(margin))
     assert np.array_equal(r["ids_g"][:first_close], r["ids_o"][:first_close])
