@@ -104,6 +104,21 @@ nut_status nut_qmatvec(nut_qmatrix *matrix, const float *x, float *y);
 nut_status nut_qmatvec_async(nut_qmatrix *matrix, const float *x_device,
                              float *y_device, void *stream);
 
+/* Prefill form of the quantised product on DEVICE buffers, enqueued on
+ * `stream`: Y[tokens][rows] = X[tokens][cols] Q^T.  Runs on the 5th-gen
+ * tensor cores with bf16 operands (Q dequantised once, q * scale rounded to
+ * bf16, and cached with the matrix; X rounded to bf16 per call) and fp32
+ * accumulation, so |Y - exact| <= 2^-7 sum_k |x_k q_k s_k| per element.
+ * The reference has no batched quantised product: prefill_quantized
+ * (src/quant_model.cpp:208-220) runs matvec_quantized_threaded per token;
+ * this entry point is that loop over a batch of tokens.  Device-side
+ * timeouts are reported by the next nut_qmatrix_error call. */
+nut_status nut_qmatrix_gemm(nut_qmatrix *matrix, const float *x_device, int64_t tokens,
+                            float *y_device, void *stream);
+/* Synchronises the matrix's work and reports a device-side timeout of an
+ * earlier asynchronous call (NUT_DEVICE_TIMEOUT), clearing it. */
+nut_status nut_qmatrix_error(nut_qmatrix *matrix);
+
 /* ---- Model weights (include/quant_model.hpp:31-46) ------------------- */
 
 /* Copies a QuantizedModelWeights image to `device` (layout private to the

@@ -145,6 +145,8 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_qmatrix_download", [_P, _P, _P])
         _declare(lib, "nut_qmatvec", [_P, _P, _P])
         _declare(lib, "nut_qmatvec_async", [_P, _P, _P, _P])
+        _declare(lib, "nut_qmatrix_gemm", [_P, _P, _I64, _P, _P])
+        _declare(lib, "nut_qmatrix_error", [_P])
         _declare(lib, "nut_model_create", [C.POINTER(ModelView), C.c_int,
                                            C.POINTER(_P)])
         _declare(lib, "nut_model_destroy", [_P])
@@ -380,6 +382,16 @@ class DeviceQMatrix:
     def matvec_async(self, x_dev: int, y_dev: int, stream: int = 0) -> None:
         _check(cuda_lib().nut_qmatvec_async(self.handle, x_dev, y_dev,
                                             stream or None))
+
+    def gemm_async(self, x_dev: int, tokens: int, y_dev: int, stream: int = 0) -> None:
+        """Y[tokens][rows] = X[tokens][cols] Q^T on the tensor cores (bf16
+        operands, fp32 accumulation), device buffers."""
+        _check(cuda_lib().nut_qmatrix_gemm(self.handle, x_dev, int(tokens), y_dev,
+                                           stream or None))
+
+    def check(self) -> None:
+        """Raises DeviceTimeout if an earlier asynchronous call gave up."""
+        _check(cuda_lib().nut_qmatrix_error(self.handle))
 
     def download(self) -> tuple[np.ndarray, np.ndarray]:
         nd, ns = storage_sizes(self.rows, self.cols, self.qtype)

@@ -258,6 +258,11 @@ struct nut_qmatrix {
     float *x = nullptr, *y = nullptr; /* staging for host-buffer calls */
     int *error = nullptr;
     cudaStream_t stream = nullptr;
+    /* prefill GEMM state: the dequantised bf16 copy of the matrix
+     * [row_tiles * 16][blocks * 32] (made on first use) and the bf16
+     * activation buffer */
+    uint16_t *wbf = nullptr, *xbf = nullptr;
+    size_t xbf_cap = 0;
     ~nut_qmatrix() {
         if (stream) {
             cudaStreamSynchronize(stream);
@@ -268,6 +273,8 @@ struct nut_qmatrix {
         dev_free(x);
         dev_free(y);
         dev_free(error);
+        dev_free(wbf);
+        dev_free(xbf);
     }
     void launch(const float *xd, float *yd, cudaStream_t s) {
         if (tiled) {
@@ -672,6 +679,50 @@ nut_status nut_qmatvec_async(nut_qmatrix *matrix, const float *x_device,
             raise(NUT_INVALID_ARGUMENT, "quantized matvec: null pointer");
         DeviceScope scope(matrix->device);
         matrix->launch(x_device, y_device, static_cast<cudaStream_t>(stream));
+    });
+}
+
+nut_status nut_qmatrix_gemm(nut_qmatrix *matrix, const float *x_device, int64_t tokens,
+                            float *y_device, void *stream) {
+    return guarded([&] {
+        if (matrix == nullptr || x_device == nullptr || y_device == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "quantized gemm: null pointer");
+        if (tokens <= 0 || tokens > (int64_t(1) << 24))
+            raise(NUT_INVALID_ARGUMENT, "quantized gemm: invalid token count");
+        if (!matrix->tiled)
+            raise(NUT_INVALID_ARGUMENT,
+                  "quantized gemm: columns must be a multiple of the block size");
+        DeviceScope scope(matrix->device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const nut::TileShape &sh = matrix->t.shape;
+        const int64_t kp = sh.blocks * 32, n_alloc = sh.row_tiles * 16;
+        if (matrix->wbf == nullptr) {
+            matrix->wbf = dev_alloc<uint16_t>(size_t(n_alloc * kp), "alloc bf16 weights");
+            cuda_check(nut::dequant_tiles_bf16(matrix->t, matrix->wbf, s), "dequantize");
+        }
+        const size_t need = size_t(tokens * kp);
+        if (matrix->xbf_cap < need) {
+            cuda_check(cudaStreamSynchronize(s), "synchronize");
+            dev_free(matrix->xbf);
+            matrix->xbf = dev_alloc<uint16_t>(need, "alloc bf16 activations");
+            matrix->xbf_cap = need;
+        }
+        cuda_check(nut::round_bf16(x_device, int(tokens), int(matrix->cols), int(kp),
+                                   matrix->xbf, s),
+                   "round activations");
+        cuda_check(nut::gemm_bf16(matrix->xbf, int(tokens), matrix->wbf, int(matrix->rows),
+                                  int(n_alloc), int(kp), y_device, int(matrix->rows),
+                                  matrix->error, nut::kDefaultWaitNs, s),
+                   "gemm launch");
+    });
+}
+
+nut_status nut_qmatrix_error(nut_qmatrix *matrix) {
+    return guarded([&] {
+        if (matrix == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "quantized matrix: null handle");
+        DeviceScope scope(matrix->device);
+        check_device_error(matrix->error, matrix->stream);
     });
 }
 

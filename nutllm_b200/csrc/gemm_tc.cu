@@ -1,0 +1,418 @@
+/* Prefill GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+ *
+ * Y[M][N] = X[M][K] W[N][K]^T for the quantised linear layers when many
+ * tokens are processed at once (prefill_quantized, src/quant_model.cpp:
+ * 208-220, feeds every prompt token through the same projections; a batch
+ * of M tokens turns the N x K matrix-vector products into one dense
+ * contraction).  Operands are bf16: W is the quantised matrix dequantised
+ * once (q * scale rounded to bf16) and cached beside the fragment tiles; X
+ * is rounded to bf16 per call.  Accumulation is fp32 in tensor memory.
+ *
+ * One CTA computes one 128 x BN output tile:
+ *   warp 4 (one lane)  TMA producer: A tile 128 x 64 and B tile BN x 64
+ *                      (bf16, 128-byte swizzle) per stage of a ring
+ *   warp 5             allocates BN TMEM columns; one lane issues four
+ *                      tcgen05.mma (K = 16 each) per stage and commits
+ *                      each stage back to its "empty" barrier
+ *   warps 0-3          epilogue: wait for the last commit, tcgen05.ld
+ *                      their 32-lane quadrant of the accumulator, store
+ *                      fp32 rows of Y
+ * Every wait is bounded; a timed-out role records an error and stops, and
+ * the producer waits (bounded) for the copies it issued before the CTA
+ * frees its tensor memory and exits.
+ */
+#include <cstdint>
+#include <cstdio>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "kernels_tc.h"
+#include "stream.cuh"
+
+namespace nut {
+namespace {
+
+constexpr int kBM = 128;  /* UMMA M */
+constexpr int kBK = 64;   /* bf16 elements per 128-byte swizzle row */
+constexpr int kEpiWarps = 4;
+constexpr int kThreadsG = (kEpiWarps + 2) * 32;
+
+enum : int { kGemmErrFull = 11, kGemmErrEmpty = 12, kGemmErrAccum = 13 };
+
+/* ---- tcgen05 / TMA wrappers ---- */
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     smem_u32(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t addr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(addr), "r"(cols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+
+/* D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, fp32 accumulation. */
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+/* Arrives on `bar` once every tcgen05.mma issued so far by this thread has
+ * completed. */
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+/* 16 consecutive fp32 accumulator columns of this thread's TMEM lane. */
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+        v[j] = __uint_as_float(r[j]);
+}
+
+/* Shared-memory matrix descriptor of a K-major tile with 128-byte rows in
+ * the 128-byte swizzle: 8-row core groups 1024 bytes apart (stride byte
+ * offset 64 x 16 B), leading byte offset 1 (unused by this mode), version
+ * 1, swizzle mode 2.  The tile base must be 1024-byte aligned. */
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= uint64_t((addr >> 4) & 0x3FFFu);
+    d |= uint64_t(1) << 16;          /* leading byte offset (16 B units) */
+    d |= uint64_t(64) << 32;         /* stride byte offset: 1024 B */
+    d |= uint64_t(1) << 46;          /* descriptor version */
+    d |= uint64_t(2) << 61;          /* 128-byte swizzle */
+    return d;
+}
+
+/* Instruction descriptor: dense, fp32 accumulator, bf16 A and B, both
+ * K-major, shape M x N. */
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4)                      /* accumulator format F32 */
+           | (1u << 7)                    /* A format BF16 */
+           | (1u << 10)                   /* B format BF16 */
+           | (uint32_t(N >> 3) << 17)     /* N / 8 */
+           | (uint32_t(M >> 4) << 24);    /* M / 16 */
+}
+
+struct GemmArgs {
+    int M, N, K;       /* K a multiple of 64 */
+    float *Y;          /* [M][ldy] */
+    int ldy;
+    int *error;
+    uint64_t limit_ns;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+    static constexpr int kA = kBM * kBK * 2;  /* 16 KB */
+    static constexpr int kB = BN * kBK * 2;
+    static constexpr int kStage = kA + kB;
+    static constexpr size_t kBytes = size_t(STAGES) * kStage + 1024 /* align */ + 256;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreadsG, 1)
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const GemmArgs g) {
+    using S = GemmSmem<BN, STAGES>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *tiles = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStage);
+    uint64_t *empty = full + STAGES;
+    uint64_t *accum = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+    const int kb_count = g.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kEpiWarps + 1)
+        tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kEpiWarps) {
+        /* TMA producer */
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < kb_count; kb++) {
+                const int s = kb % STAGES;
+                const uint32_t par = uint32_t((kb / STAGES) & 1);
+                if (kb >= STAGES &&
+                    (*abort_flag || !mbar_wait(&empty[s], par ^ 1u, g.limit_ns))) {
+                    atomicCAS(g.error, 0, kGemmErrEmpty);
+                    *abort_flag = 1;
+                    break;
+                }
+                uint8_t *a = tiles + s * S::kStage;
+                mbar_expect_tx(&full[s], uint32_t(S::kStage));
+                tma_load_2d(a, &tmA, kb * kBK, m0, &full[s]);
+                tma_load_2d(a + S::kA, &tmB, kb * kBK, n0, &full[s]);
+                issued = kb + 1;
+            }
+            /* every issued copy has landed before the CTA can exit */
+            for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
+                mbar_wait(&full[kb % STAGES], uint32_t((kb / STAGES) & 1), g.limit_ns);
+        }
+    } else if (warp == kEpiWarps + 1) {
+        /* MMA issuer */
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+            for (int kb = 0; kb < kb_count; kb++) {
+                const int s = kb % STAGES;
+                const uint32_t par = uint32_t((kb / STAGES) & 1);
+                if (*abort_flag || !mbar_wait(&full[s], par, g.limit_ns)) {
+                    atomicCAS(g.error, 0, kGemmErrFull);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(tiles + s * S::kStage), b = a + S::kA;
+#pragma unroll
+                for (int k = 0; k < kBK / 16; k++)
+                    umma_bf16(tmem, smem_desc_sw128(a + k * 32), smem_desc_sw128(b + k * 32),
+                              idesc, (kb | k) != 0);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(accum);
+        }
+        __syncwarp();
+    } else {
+        /* epilogue: warp w owns TMEM lanes (rows) 32 w .. 32 w + 31 */
+        bool ok = mbar_wait(accum, 0u, g.limit_ns);
+        if (!ok)
+            atomicCAS(g.error, 0, kGemmErrAccum);
+        ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+        tc_fence_after();
+        const int row = m0 + warp * 32 + lane;
+        if (ok) {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float v[16];
+                tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c), v);
+                if (row < g.M) {
+                    float *y = g.Y + size_t(row) * g.ldy + n0 + c;
+                    if (n0 + c + 16 <= g.N && (g.ldy % 4) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(y + j) =
+                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+                        for (int j = 0; j < 16; j++)
+                            if (n0 + c + j < g.N)
+                                y[j] = v[j];
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+/* ---- dequantisation and activation rounding ---- */
+
+/* Fragment tiles (row-major order) -> bf16 [row_tiles * 16][blocks * 32]
+ * (q * scale exact in fp32, rounded to nearest bf16).  One thread per
+ * (tile, lane). */
+template <int TYPE>
+__global__ void dequant_tiles_kernel(const uint8_t *tiles, const uint16_t *scales, int row_tiles,
+                                     int blocks, __nv_bfloat16 *out) {
+    const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t ntiles = int64_t(row_tiles) * blocks;
+    if (gid >= ntiles * 32)
+        return;
+    const int lane = int(gid & 31);
+    const int64_t t = gid >> 5;
+    const int rt = int(t / blocks), b = int(t % blocks);
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t a[4];
+    if (TYPE == 0) {
+        const uint4 p = *reinterpret_cast<const uint4 *>(tiles + t * 512 + 16 * lane);
+        a[0] = p.x, a[1] = p.y, a[2] = p.z, a[3] = p.w;
+    } else {
+        const uint2 p = *reinterpret_cast<const uint2 *>(tiles + t * 256 + 8 * lane);
+        a[0] = (p.x << 4) & 0xF0F0F0F0u, a[1] = p.x & 0xF0F0F0F0u;
+        a[2] = (p.y << 4) & 0xF0F0F0F0u, a[3] = p.y & 0xF0F0F0F0u;
+    }
+    const float unit = TYPE == 1 ? 1.0f / 16.0f : 1.0f;
+    const float s0 = half_bits_to_float(scales[t * 16 + g]) * unit;
+    const float s1 = half_bits_to_float(scales[t * 16 + g + 8]) * unit;
+    const int64_t ld = int64_t(blocks) * 32;
+    const int64_t r0 = int64_t(rt) * 16 + g, r1 = r0 + 8;
+    const int k0 = b * 32 + 4 * c;
+    /* a0: row g, cols 4c..4c+3; a1: row g+8, same; a2: row g, 16+4c..;
+       a3: row g+8, 16+4c.. (the m16n8k32 A fragment) */
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int64_t row = (r & 1) ? r1 : r0;
+        const float s = (r & 1) ? s1 : s0;
+        const int k = k0 + ((r & 2) ? 16 : 0);
+        __nv_bfloat16 *dst = out + row * ld + k;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int q = int(int8_t(uint8_t(a[r] >> (8 * j))));
+            dst[j] = __float2bfloat16_rn(float(q) * s);
+        }
+    }
+}
+
+/* fp32 [M][K] -> bf16 [M][Kp] (columns K..Kp-1 zero). */
+__global__ void round_bf16_kernel(const float *x, int M, int K, int Kp, __nv_bfloat16 *out) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= int64_t(M) * Kp)
+        return;
+    const int64_t m = i / Kp;
+    const int k = int(i - m * Kp);
+    out[i] = __float2bfloat16_rn(k < K ? x[m * K + k] : 0.0f);
+}
+
+/* ---- host side ---- */
+
+/* cuTensorMapEncodeTiled, resolved through the runtime so the library
+ * does not link the driver library (it loads on machines without one). */
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return EncodeTiledFn(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+bool encode_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols_elems,
+                int box_rows) {
+    const EncodeTiledFn encode = encode_fn();
+    if (encode == nullptr)
+        return false;
+    const cuuint64_t dims[2] = {cuuint64_t(cols_elems), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(cols_elems) * 2};
+    const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(
+        map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs &g,
+                      cudaStream_t stream) {
+    using S = GemmSmem<BN, STAGES>;
+    auto k = gemm_bf16_kernel<BN, STAGES>;
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
+    if (e != cudaSuccess)
+        return e;
+    const dim3 grid((g.N + BN - 1) / BN, (g.M + kBM - 1) / kBM);
+    k<<<grid, kThreadsG, S::kBytes, stream>>>(a, b, g);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+} // namespace
+
+cudaError_t dequant_tiles_bf16(const TileMatrix &m, uint16_t *out, cudaStream_t stream) {
+    const int64_t threads = int64_t(m.shape.row_tiles) * m.shape.blocks * 32;
+    const int grid = int((threads + 255) / 256);
+    if (m.shape.order != kRowMajor)
+        return cudaErrorInvalidValue;
+    auto *o = reinterpret_cast<__nv_bfloat16 *>(out);
+    if (m.shape.type == 1)
+        dequant_tiles_kernel<1><<<grid, 256, 0, stream>>>(m.data, m.scales, int(m.shape.row_tiles),
+                                                          int(m.shape.blocks), o);
+    else
+        dequant_tiles_kernel<0><<<grid, 256, 0, stream>>>(m.data, m.scales, int(m.shape.row_tiles),
+                                                          int(m.shape.blocks), o);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t round_bf16(const float *x, int M, int K, int Kp, uint16_t *out, cudaStream_t stream) {
+    const int64_t n = int64_t(M) * Kp;
+    round_bf16_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(
+        x, M, K, Kp, reinterpret_cast<__nv_bfloat16 *>(out));
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
+                      float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0 ||
+        (reinterpret_cast<uintptr_t>(A) & 15) != 0 || (reinterpret_cast<uintptr_t>(B) & 15) != 0)
+        return cudaErrorInvalidValue;
+    CUtensorMap ma, mb;
+    const bool wide = N >= 2048;
+    if (!encode_map(&ma, A, M, K, kBM) || !encode_map(&mb, B, N_alloc, K, wide ? 256 : 128))
+        return cudaErrorInvalidValue;
+    const GemmArgs g{M, N, K, Y, ldy, error, limit_ns};
+    return wide ? launch_bn<256, 4>(ma, mb, g, stream) : launch_bn<128, 6>(ma, mb, g, stream);
+}
+
+} // namespace nut
