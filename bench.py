@@ -14,7 +14,8 @@ whole loop on the device.
             (nut_generate_greedy: prompt from host memory in, ids out)
   roofline  the dominant kernel (the persistent token loop, one launch per
             generation) against the measured HBM copy bandwidth
-  qmatvec   microbenchmark: the quantised matvec at the BASELINE shapes
+  qmatvec   microbenchmark (a): the quantised matvec at the BASELINE shapes
+  prefill_gemm  microbenchmark (b): the tcgen05 prefill GEMM, 512 tokens
   cpu_baseline  the reference's own CPU token loop (oracle/_ref) on this
             host, all threads, on the whole workload once
 
@@ -72,7 +73,9 @@ def parse():
     p.add_argument("--workload", default="tinyllama-int4")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-micro", action="store_true",
-                   help="skip the qmatvec microbenchmark")
+                   help="skip the kernel microbenchmarks")
+    p.add_argument("--micro-only", action="store_true",
+                   help="run only the kernel microbenchmarks (one JSON line)")
     return p.parse_args()
 
 
@@ -228,6 +231,10 @@ def run_ours(args, rank, world, local):
         "traffic": NCU_TRAFFIC.get(wl.name),
     }
     micro = None if args.no_micro else qmatvec_micro(nb, local, peak)
+    tpeak, tsrc = measured_tensor_peak()
+    gemm = None if args.no_micro else {
+        "peak_tflops": tpeak, "peak_source": tsrc,
+        "shapes": gemm_micro(nb, local, tpeak)}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, c)
@@ -260,6 +267,7 @@ def run_ours(args, rank, world, local):
         "gpu_launches": int(launches),
         "roofline": roofline,
         "qmatvec": micro,
+        "prefill_gemm": gemm,
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
     }
@@ -324,6 +332,73 @@ def qmatvec_micro(nb, device, peak):
                         "frac": round(ach / peak, 4)})
             del g, mats, ys
     return out
+
+
+def gemm_micro(nb, device, peak_tflops, tokens=512):
+    """Kernel microbenchmark (b): the prefill GEMM (nut_qmatrix_gemm, fp16
+    operands on the tensor cores, fp32 accumulation) for `tokens` rows of
+    activations over every BASELINE weight shape, INT4 and INT8 weights
+    (dequantised once and cached).  Each call also rounds the fp32
+    activations to fp16; calls are replayed back to back from a CUDA
+    graph.  TFLOP/s = 2 tokens rows cols / device time per call."""
+    import torch
+    torch.cuda.set_device(device)
+    dev = f"cuda:{device}"
+    s = torch.cuda.Stream(device=dev)
+    out = []
+    for qtype, tname in ((nb.INT4, "int4"), (nb.INT8, "int8")):
+        for rows, cols in QMATVEC_SHAPES:
+            w = nb.synth_normal(SEED, 7, rows * cols, 0.02).reshape(rows, cols)
+            m = nb.DeviceQMatrix(nb.QuantizedMatrix.quantize(w, qtype), device)
+            x = torch.from_numpy(
+                nb.synth_normal(SEED, 8, tokens * cols, 1.0).reshape(tokens, cols)).to(dev)
+            y = torch.empty(tokens, rows, device=dev)
+            with torch.cuda.stream(s):
+                for _ in range(2):  # the first call dequantises and caches
+                    m.gemm_async(x.data_ptr(), tokens, y.data_ptr(), s.cuda_stream)
+            s.synchronize()
+            reps = 20
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(reps):
+                    m.gemm_async(x.data_ptr(), tokens, y.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream)
+            times = []
+            for _ in range(4):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(s):
+                    a.record(s)
+                    g.replay()
+                    b.record(s)
+                b.synchronize()
+                times.append(a.elapsed_time(b) * 1e-3 / reps)
+            m.check()
+            t = min(times[1:])
+            tf = 2.0 * tokens * rows * cols / t / 1e12
+            out.append({"type": tname, "rows": rows, "cols": cols, "tokens": tokens,
+                        "us": round(t * 1e6, 2), "TFLOP/s": round(tf, 1),
+                        "frac": round(tf / peak_tflops, 4)})
+            del g
+    return out
+
+
+def run_micro(device):
+    import nutllm_b200 as nb
+    peak, src = measured_peaks()
+    tpeak, tsrc = measured_tensor_peak()
+    print(json.dumps({"qmatvec": qmatvec_micro(nb, device, peak),
+                      "prefill_gemm": {"peak_tflops": tpeak, "peak_source": tsrc,
+                                       "shapes": gemm_micro(nb, device, tpeak)}}),
+          flush=True)
+
+
+def measured_tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def cpu_baseline(wl, c):
@@ -435,6 +510,9 @@ def main():
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.micro_only:
+        run_micro(local)
         return
     _init_dist(world)
     run_ours(args, rank, world, local)

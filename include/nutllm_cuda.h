@@ -106,9 +106,10 @@ nut_status nut_qmatvec_async(nut_qmatrix *matrix, const float *x_device,
 
 /* Prefill form of the quantised product on DEVICE buffers, enqueued on
  * `stream`: Y[tokens][rows] = X[tokens][cols] Q^T.  Runs on the 5th-gen
- * tensor cores with bf16 operands (Q dequantised once, q * scale rounded to
- * bf16, and cached with the matrix; X rounded to bf16 per call) and fp32
- * accumulation, so |Y - exact| <= 2^-7 sum_k |x_k q_k s_k| per element.
+ * tensor cores with fp16 operands (Q dequantised once, q * scale rounded to
+ * fp16, and cached with the matrix; X rounded to fp16 per call, saturating
+ * at +-65504) and fp32 accumulation, so |Y - exact| <= 2^-10 sum_k
+ * |x_k q_k s_k| per element (plus fp16's subnormal step below 2^-14).
  * The reference has no batched quantised product: prefill_quantized
  * (src/quant_model.cpp:208-220) runs matvec_quantized_threaded per token;
  * this entry point is that loop over a batch of tokens.  Device-side
@@ -135,6 +136,17 @@ nut_status nut_model_storage_bytes(const nut_model *model, uint64_t *bytes);
  * own CUDA events.  No counterpart in the reference (its loop is host
  * code). */
 nut_status nut_model_stream(const nut_model *model, void **stream);
+
+/* Prompts of at least min_tokens tokens (default 64; 0 = never) are
+ * prefilled as one batch: every projection of every layer as one GEMM on
+ * the tensor cores with fp16 operands (weights dequantised once, rounded to
+ * fp16; fp32 accumulation), instead of the per-token loop of
+ * prefill_quantized (src/quant_model.cpp:208-220).  Hidden states and the
+ * KV cache then carry fp16 rounding (a looser bound than the per-token
+ * path's parity); set 0 to keep every prompt on the per-token path.
+ * Applies to nut_prefill and nut_generate_greedy.  No counterpart in the
+ * reference. */
+nut_status nut_model_set_prefill_threshold(nut_model *model, int64_t min_tokens);
 
 /* Total kernels this library has launched in this process (all devices),
  * for callers that account for launches per step.  No counterpart in the

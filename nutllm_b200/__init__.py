@@ -152,6 +152,7 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_model_destroy", [_P])
         _declare(lib, "nut_model_storage_bytes", [_P, C.POINTER(C.c_uint64)])
         _declare(lib, "nut_model_stream", [_P, C.POINTER(_P)])
+        _declare(lib, "nut_model_set_prefill_threshold", [_P, _I64])
         _declare(lib, "nut_launch_count", [C.POINTER(C.c_uint64)])
         _declare(lib, "nut_kv_create", [_P, C.POINTER(_P)])
         _declare(lib, "nut_kv_destroy", [_P])
@@ -384,7 +385,7 @@ class DeviceQMatrix:
                                             stream or None))
 
     def gemm_async(self, x_dev: int, tokens: int, y_dev: int, stream: int = 0) -> None:
-        """Y[tokens][rows] = X[tokens][cols] Q^T on the tensor cores (bf16
+        """Y[tokens][rows] = X[tokens][cols] Q^T on the tensor cores (fp16
         operands, fp32 accumulation), device buffers."""
         _check(cuda_lib().nut_qmatrix_gemm(self.handle, x_dev, int(tokens), y_dev,
                                            stream or None))
@@ -429,6 +430,11 @@ class DeviceModel:
         out = C.c_uint64(0)
         _check(cuda_lib().nut_model_storage_bytes(self.handle, C.byref(out)))
         return out.value
+
+    def set_prefill_threshold(self, min_tokens: int) -> None:
+        """Prompts of at least min_tokens tokens (0 = never) are prefilled as
+        one batch of tensor-core GEMMs (fp16 operands)."""
+        _check(cuda_lib().nut_model_set_prefill_threshold(self.handle, int(min_tokens)))
 
     @property
     def stream(self) -> int:

@@ -21,6 +21,7 @@
 
 #include "../../include/nutllm_cuda.h"
 #include "decode_mk.h"
+#include "prefill.h"
 #include "kernels.h"
 #include "kernels_tc.h"
 
@@ -258,8 +259,8 @@ struct nut_qmatrix {
     float *x = nullptr, *y = nullptr; /* staging for host-buffer calls */
     int *error = nullptr;
     cudaStream_t stream = nullptr;
-    /* prefill GEMM state: the dequantised bf16 copy of the matrix
-     * [row_tiles * 16][blocks * 32] (made on first use) and the bf16
+    /* prefill GEMM state: the dequantised fp16 copy of the matrix
+     * [row_tiles * 16][blocks * 32] (made on first use) and the fp16
      * activation buffer */
     uint16_t *wbf = nullptr, *xbf = nullptr;
     size_t xbf_cap = 0;
@@ -314,11 +315,23 @@ struct nut_model {
     std::vector<nut::MkLayer> mk_layers;
     nut::MkLayerPtrs *mk_ptrs = nullptr;
     float *attn_norms = nullptr, *ffn_norms = nullptr; /* [layers][dim] */
+    /* batched prefill: prompts of at least prefill_min tokens (0 = never)
+     * run layer by layer as GEMMs over fp16 copies of the weights, made on
+     * first use */
+    int64_t prefill_min = 64;
+    struct F16Layer {
+        uint16_t *qkv = nullptr, *wo = nullptr, *gu = nullptr, *down = nullptr;
+    };
+    std::vector<F16Layer> f16w;
+    int *gemm_error = nullptr;
     ~nut_model() {
         if (stream) {
             cudaStreamSynchronize(stream);
             cudaStreamDestroy(stream);
         }
+        for (auto &b : f16w)
+            dev_free(b.qkv), dev_free(b.wo), dev_free(b.gu), dev_free(b.down);
+        dev_free(gemm_error);
         for (auto &l : mk_layers) {
             release(l.qkv), release(l.wo), release(l.gu), release(l.down);
         }
@@ -357,6 +370,19 @@ struct nut_kv {
     unsigned long long *mk_stamps = nullptr; /* [3] */
     float *mk_logits = nullptr;
     size_t mk_logits_cap = 0;
+    /* batched prefill scratch, rows for pf_cap tokens */
+    float *pf_h = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr;
+    uint16_t *pf_x = nullptr, *pf_ctx = nullptr, *pf_act = nullptr;
+    int32_t *pf_tok = nullptr;
+    int64_t pf_cap = 0;
+    void free_prefill() {
+        dev_free(pf_h), dev_free(pf_qkv), dev_free(pf_gu), dev_free(pf_x), dev_free(pf_ctx);
+        dev_free(pf_act), dev_free(pf_tok);
+        pf_h = pf_qkv = pf_gu = nullptr;
+        pf_x = pf_ctx = pf_act = nullptr;
+        pf_tok = nullptr;
+        pf_cap = 0;
+    }
     ~nut_kv() {
         if (model)
             cudaStreamSynchronize(model->stream);
@@ -365,6 +391,7 @@ struct nut_kv {
         dev_free(logits), dev_free(argmax_key), dev_free(ids);
         dev_free(tagged), dev_free(mk_keys), dev_free(mk_done), dev_free(mk_prompt);
         dev_free(mk_acc), dev_free(mk_cnt);
+        free_prefill();
         dev_free(mk_error), dev_free(mk_stamps), dev_free(mk_logits);
         for (auto e : ev)
             if (e)
@@ -585,6 +612,96 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
     }
 }
 
+/* fp16 copies of every layer's weights for the prefill GEMMs. */
+void ensure_f16(nut_model *m) {
+    if (!m->f16w.empty())
+        return;
+    auto make = [&](const nut::TileMatrix &t) {
+        const size_t n = size_t(t.shape.row_tiles * 16) * size_t(t.shape.blocks * 32);
+        uint16_t *p = dev_alloc<uint16_t>(n, "alloc fp16 weights");
+        cuda_check(nut::dequant_tiles_f16(t, p, m->stream), "dequantize");
+        return p;
+    };
+    for (const nut::MkLayer &L : m->mk_layers) {
+        nut_model::F16Layer b;
+        b.qkv = make(L.qkv);
+        b.wo = make(L.wo);
+        b.gu = make(L.gu);
+        b.down = make(L.down);
+        m->f16w.push_back(b);
+    }
+    m->gemm_error = dev_alloc<int>(1, "alloc error word");
+    cuda_check(cudaMemsetAsync(m->gemm_error, 0, sizeof(int), m->stream), "clear error word");
+}
+
+/* The prompt through every layer as one batch (positions 0 .. n - 1):
+ * per layer rmsnorm -> [q;k;v] GEMM -> RoPE + KV append -> causal attention
+ * -> h += Wo ctx (GEMM) -> rmsnorm -> gate/up GEMM -> SwiGLU -> h += Wdown a
+ * (GEMM).  Leaves the last token's hidden vector in kv->hidden. */
+void prefill_batched(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n) {
+    const nut_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    const int dim = int(c.dim), kvd = int(m->kv_heads * c.head_dim), ffn = int(c.ffn_dim);
+    const nut::MkLayer &L0 = m->mk_layers[0];
+    const int kp_dim = int(L0.qkv.shape.blocks * 32), kp_ffn = int(L0.down.shape.blocks * 32);
+    const int nqkv = dim + 2 * kvd, M = int(n);
+    ensure_f16(m);
+    if (kv->pf_cap < n) {
+        cuda_check(cudaStreamSynchronize(s), "synchronize");
+        kv->free_prefill();
+        const size_t r = size_t(n);
+        kv->pf_h = dev_alloc<float>(r * dim, "alloc prefill rows");
+        kv->pf_qkv = dev_alloc<float>(r * nqkv, "alloc prefill rows");
+        kv->pf_gu = dev_alloc<float>(r * 2 * ffn, "alloc prefill rows");
+        kv->pf_x = dev_alloc<uint16_t>(r * kp_dim, "alloc prefill rows");
+        kv->pf_ctx = dev_alloc<uint16_t>(r * kp_dim, "alloc prefill rows");
+        kv->pf_act = dev_alloc<uint16_t>(r * kp_ffn, "alloc prefill rows");
+        kv->pf_tok = dev_alloc<int32_t>(r, "alloc prefill tokens");
+        kv->pf_cap = n;
+    }
+    cuda_check(cudaMemcpyAsync(kv->pf_tok, tokens, size_t(n) * 4, cudaMemcpyHostToDevice, s),
+               "copy prompt");
+    cuda_check(nut::gather_rows(m->embeddings, kv->pf_tok, M, dim, int(c.vocab_size), kv->pf_h, s),
+               "embed");
+    auto gemm = [&](const uint16_t *a, const nut::TileMatrix &t, const uint16_t *w, int N,
+                    int K, float *y, bool acc) {
+        cuda_check(nut::gemm_f16(a, M, w, N, int(t.shape.row_tiles * 16), K, y, N,
+                                  m->gemm_error, nut::kDefaultWaitNs, s, acc),
+                   "prefill gemm");
+    };
+    for (int64_t l = 0; l < c.layers; l++) {
+        const nut::MkLayer &L = m->mk_layers[size_t(l)];
+        const nut_model::F16Layer &B = m->f16w[size_t(l)];
+        cuda_check(nut::rmsnorm_rows(kv->pf_h, m->attn_norms + l * dim, M, dim, kp_dim, kv->pf_x, s),
+                   "rmsnorm");
+        gemm(kv->pf_x, L.qkv, B.qkv, nqkv, kp_dim, kv->pf_qkv, false);
+        cuda_check(nut::rope_kv_rows(kv->pf_qkv, M, nqkv, 0, m->rope_cos, m->rope_sin,
+                                     int(c.heads), int(m->kv_heads), int(c.head_dim), dim, kvd,
+                                     kv->keys, kv->values, int(l), int(c.max_seq), s),
+                   "rope");
+        cuda_check(nut::attention_rows(kv->pf_qkv, M, nqkv, 0, kv->keys, kv->values, int(l),
+                                       int(c.heads), int(m->kv_heads), int(c.head_dim), dim,
+                                       int(c.max_seq), kp_dim, kv->pf_ctx, s),
+                   "attention");
+        gemm(kv->pf_ctx, L.wo, B.wo, dim, kp_dim, kv->pf_h, true);
+        cuda_check(nut::rmsnorm_rows(kv->pf_h, m->ffn_norms + l * dim, M, dim, kp_dim, kv->pf_x, s),
+                   "rmsnorm");
+        gemm(kv->pf_x, L.gu, B.gu, 2 * ffn, kp_dim, kv->pf_gu, false);
+        cuda_check(nut::swiglu_rows(kv->pf_gu, M, ffn, kp_ffn, kv->pf_act, s), "swiglu");
+        gemm(kv->pf_act, L.down, B.down, dim, kp_ffn, kv->pf_h, true);
+    }
+    cuda_check(cudaMemcpyAsync(kv->hidden, kv->pf_h + size_t(n - 1) * dim, size_t(dim) * 4,
+                               cudaMemcpyDeviceToDevice, s),
+               "copy hidden");
+    check_device_error(m->gemm_error, s);
+    kv->length = n;
+    kv->has_hidden = true;
+}
+
+bool use_batched_prefill(const nut_model *m, int64_t n) {
+    return m->mk && m->prefill_min > 0 && n >= m->prefill_min;
+}
+
 } // namespace
 
 extern "C" {
@@ -697,20 +814,20 @@ nut_status nut_qmatrix_gemm(nut_qmatrix *matrix, const float *x_device, int64_t 
         const nut::TileShape &sh = matrix->t.shape;
         const int64_t kp = sh.blocks * 32, n_alloc = sh.row_tiles * 16;
         if (matrix->wbf == nullptr) {
-            matrix->wbf = dev_alloc<uint16_t>(size_t(n_alloc * kp), "alloc bf16 weights");
-            cuda_check(nut::dequant_tiles_bf16(matrix->t, matrix->wbf, s), "dequantize");
+            matrix->wbf = dev_alloc<uint16_t>(size_t(n_alloc * kp), "alloc fp16 weights");
+            cuda_check(nut::dequant_tiles_f16(matrix->t, matrix->wbf, s), "dequantize");
         }
         const size_t need = size_t(tokens * kp);
         if (matrix->xbf_cap < need) {
             cuda_check(cudaStreamSynchronize(s), "synchronize");
             dev_free(matrix->xbf);
-            matrix->xbf = dev_alloc<uint16_t>(need, "alloc bf16 activations");
+            matrix->xbf = dev_alloc<uint16_t>(need, "alloc fp16 activations");
             matrix->xbf_cap = need;
         }
-        cuda_check(nut::round_bf16(x_device, int(tokens), int(matrix->cols), int(kp),
+        cuda_check(nut::round_f16(x_device, int(tokens), int(matrix->cols), int(kp),
                                    matrix->xbf, s),
                    "round activations");
-        cuda_check(nut::gemm_bf16(matrix->xbf, int(tokens), matrix->wbf, int(matrix->rows),
+        cuda_check(nut::gemm_f16(matrix->xbf, int(tokens), matrix->wbf, int(matrix->rows),
                                   int(n_alloc), int(kp), y_device, int(matrix->rows),
                                   matrix->error, nut::kDefaultWaitNs, s),
                    "gemm launch");
@@ -917,6 +1034,14 @@ nut_status nut_model_stream(const nut_model *model, void **stream) {
     });
 }
 
+nut_status nut_model_set_prefill_threshold(nut_model *model, int64_t min_tokens) {
+    return guarded([&] {
+        if (model == nullptr || min_tokens < 0)
+            raise(NUT_INVALID_ARGUMENT, "model: invalid prefill threshold");
+        model->prefill_min = min_tokens;
+    });
+}
+
 nut_status nut_launch_count(uint64_t *count) {
     if (count == nullptr) {
         g_error = "launch count: null argument";
@@ -1069,7 +1194,9 @@ nut_status nut_prefill(nut_model *model, nut_kv *kv, const int32_t *tokens,
         for (int64_t i = 0; i < n; i++)
             if (tokens[i] < 0 || tokens[i] >= model->cfg.vocab_size)
                 raise(NUT_OUT_OF_RANGE, "quantized decode: token out of range");
-        if (model->mk) {
+        if (use_batched_prefill(model, n)) {
+            prefill_batched(model, kv, tokens, n);
+        } else if (model->mk) {
             run_mk(model, kv, tokens, n, n, 0, 1, 0, nullptr, nullptr, nullptr);
         } else {
             for (int64_t i = 0; i < n; i++) {
@@ -1135,8 +1262,45 @@ nut_status nut_generate_greedy(nut_model *model, nut_kv *kv,
              * the last chosen token, as the reference loop does) */
             const int64_t steps = std::min<int64_t>(max_tokens, c.max_seq - n);
             std::vector<int32_t> chosen(size_t(std::max<int64_t>(steps, 1)));
-            run_mk(model, kv, prompt, n, n + steps, 0, n - 1, n + steps - 2, logits,
-                   chosen.data(), stats);
+            if (use_batched_prefill(model, n)) {
+                /* the prompt as one batch, the first token from its last
+                 * hidden vector, then the persistent loop from position n */
+                cuda_check(cudaEventRecord(kv->ev[0], s), "event");
+                prefill_batched(model, kv, prompt, n);
+                cuda_check(cudaEventRecord(kv->ev[1], s), "event");
+                double dec = 0.0;
+                if (steps > 0) {
+                    enqueue_logits(model, kv);
+                    unsigned long long key = 0;
+                    cuda_check(cudaMemcpyAsync(&key, kv->argmax_key, sizeof key,
+                                               cudaMemcpyDeviceToHost, s),
+                               "copy argmax");
+                    if (logits != nullptr)
+                        cuda_check(cudaMemcpyAsync(logits, kv->logits, c.vocab_size * 4,
+                                                   cudaMemcpyDeviceToHost, s),
+                                   "copy logits");
+                    cuda_check(cudaEventRecord(kv->ev[2], s), "event");
+                    sync(model);
+                    chosen[0] = int32_t(~uint32_t(key & 0xffffffffull));
+                    nut_generation_stats st{};
+                    run_mk(model, kv, chosen.data(), 1, steps, n, 0, steps - 2,
+                           logits != nullptr ? logits + c.vocab_size : nullptr,
+                           chosen.data() + 1, &st);
+                    float head_ms = 0.0f;
+                    cuda_check(cudaEventElapsedTime(&head_ms, kv->ev[1], kv->ev[2]), "elapsed");
+                    dec = st.prefill_seconds + st.decode_seconds + double(head_ms) * 1e-3;
+                }
+                sync(model);
+                float pre_ms = 0.0f;
+                cuda_check(cudaEventElapsedTime(&pre_ms, kv->ev[0], kv->ev[1]), "elapsed");
+                if (stats != nullptr) {
+                    stats->prefill_seconds = double(pre_ms) * 1e-3;
+                    stats->decode_seconds = dec;
+                }
+            } else {
+                run_mk(model, kv, prompt, n, n + steps, 0, n - 1, n + steps - 2, logits,
+                       chosen.data(), stats);
+            }
             int64_t produced = steps;
             if (stop_at_eos) {
                 for (int64_t k = 0; k < steps; k++)

@@ -4,13 +4,14 @@
  * tokens are processed at once (prefill_quantized, src/quant_model.cpp:
  * 208-220, feeds every prompt token through the same projections; a batch
  * of M tokens turns the N x K matrix-vector products into one dense
- * contraction).  Operands are bf16: W is the quantised matrix dequantised
- * once (q * scale rounded to bf16) and cached beside the fragment tiles; X
- * is rounded to bf16 per call.  Accumulation is fp32 in tensor memory.
+ * contraction).  Operands are fp16: W is the quantised matrix dequantised
+ * once (q * scale rounded to fp16) and cached beside the fragment tiles; X
+ * is rounded to fp16 per call (saturating at +-65504).  Accumulation is
+ * fp32 in tensor memory.
  *
  * One CTA computes one 128 x BN output tile:
  *   warp 4 (one lane)  TMA producer: A tile 128 x 64 and B tile BN x 64
- *                      (bf16, 128-byte swizzle) per stage of a ring
+ *                      (fp16, 128-byte swizzle) per stage of a ring
  *   warp 5             allocates BN TMEM columns; one lane issues four
  *                      tcgen05.mma (K = 16 each) per stage and commits
  *                      each stage back to its "empty" barrier
@@ -24,7 +25,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cuda.h>
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -35,11 +36,17 @@ namespace nut {
 namespace {
 
 constexpr int kBM = 128;  /* UMMA M */
-constexpr int kBK = 64;   /* bf16 elements per 128-byte swizzle row */
+constexpr int kBK = 64;   /* 16-bit elements per 128-byte swizzle row */
 constexpr int kEpiWarps = 4;
 constexpr int kThreadsG = (kEpiWarps + 2) * 32;
 
 enum : int { kGemmErrFull = 11, kGemmErrEmpty = 12, kGemmErrAccum = 13 };
+
+/* fp32 -> fp16, rounded to nearest, saturating at +-65504 (an outlier
+ * beyond fp16 range is clamped rather than turned into infinity). */
+__device__ __forceinline__ __half to_half_sat(float v) {
+    return __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f));
+}
 
 /* ---- tcgen05 / TMA wrappers ---- */
 
@@ -72,8 +79,8 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
 }
 
-/* D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, fp32 accumulation. */
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+/* D[tmem] (+)= A[smem] * B[smem]^T, fp16 inputs, fp32 accumulation. */
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
                                           uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -122,12 +129,10 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
     return d;
 }
 
-/* Instruction descriptor: dense, fp32 accumulator, bf16 A and B, both
- * K-major, shape M x N. */
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+/* Instruction descriptor: dense, fp32 accumulator, fp16 A and B (format
+ * code 0), both K-major, shape M x N. */
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
     return (1u << 4)                      /* accumulator format F32 */
-           | (1u << 7)                    /* A format BF16 */
-           | (1u << 10)                   /* B format BF16 */
            | (uint32_t(N >> 3) << 17)     /* N / 8 */
            | (uint32_t(M >> 4) << 24);    /* M / 16 */
 }
@@ -136,6 +141,7 @@ struct GemmArgs {
     int M, N, K;       /* K a multiple of 64 */
     float *Y;          /* [M][ldy] */
     int ldy;
+    int accumulate;    /* Y += A B^T instead of Y = A B^T */
     int *error;
     uint64_t limit_ns;
 };
@@ -150,7 +156,7 @@ struct GemmSmem {
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreadsG, 1)
-gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const GemmArgs g) {
     using S = GemmSmem<BN, STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -209,7 +215,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     } else if (warp == kEpiWarps + 1) {
         /* MMA issuer */
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+            constexpr uint32_t idesc = idesc_f16(kBM, BN);
             for (int kb = 0; kb < kb_count; kb++) {
                 const int s = kb % STAGES;
                 const uint32_t par = uint32_t((kb / STAGES) & 1);
@@ -222,7 +228,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 const uint32_t a = smem_u32(tiles + s * S::kStage), b = a + S::kA;
 #pragma unroll
                 for (int k = 0; k < kBK / 16; k++)
-                    umma_bf16(tmem, smem_desc_sw128(a + k * 32), smem_desc_sw128(b + k * 32),
+                    umma_f16(tmem, smem_desc_sw128(a + k * 32), smem_desc_sw128(b + k * 32),
                               idesc, (kb | k) != 0);
                 umma_commit(&empty[s]);
             }
@@ -246,13 +252,18 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     float *y = g.Y + size_t(row) * g.ldy + n0 + c;
                     if (n0 + c + 16 <= g.N && (g.ldy % 4) == 0) {
 #pragma unroll
-                        for (int j = 0; j < 16; j += 4)
-                            *reinterpret_cast<float4 *>(y + j) =
-                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        for (int j = 0; j < 16; j += 4) {
+                            float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                            if (g.accumulate) {
+                                const float4 r = *reinterpret_cast<const float4 *>(y + j);
+                                o.x += r.x, o.y += r.y, o.z += r.z, o.w += r.w;
+                            }
+                            *reinterpret_cast<float4 *>(y + j) = o;
+                        }
                     } else {
                         for (int j = 0; j < 16; j++)
                             if (n0 + c + j < g.N)
-                                y[j] = v[j];
+                                y[j] = g.accumulate ? y[j] + v[j] : v[j];
                     }
                 }
             }
@@ -268,19 +279,22 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
 /* ---- dequantisation and activation rounding ---- */
 
-/* Fragment tiles (row-major order) -> bf16 [row_tiles * 16][blocks * 32]
- * (q * scale exact in fp32, rounded to nearest bf16).  One thread per
+/* Fragment tiles (any tile order) -> fp16 [row_tiles * 16][blocks * 32]
+ * (q * scale exact in fp32, rounded to nearest fp16).  One thread per
  * (tile, lane). */
 template <int TYPE>
 __global__ void dequant_tiles_kernel(const uint8_t *tiles, const uint16_t *scales, int row_tiles,
-                                     int blocks, __nv_bfloat16 *out) {
+                                     int blocks, int order, __half *out) {
     const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t ntiles = int64_t(row_tiles) * blocks;
     if (gid >= ntiles * 32)
         return;
     const int lane = int(gid & 31);
-    const int64_t t = gid >> 5;
-    const int rt = int(t / blocks), b = int(t % blocks);
+    const int64_t lt = gid >> 5; /* logical tile: row tile lt / blocks, block lt % blocks */
+    const int rt = int(lt / blocks), b = int(lt % blocks);
+    const int64_t t = order == kPairColumn   ? (int64_t(b >> 1) * row_tiles + rt) * 2 + (b & 1)
+                      : order == kBlockColumn ? int64_t(b) * row_tiles + rt
+                                              : lt;
     const int g = lane >> 2, c = lane & 3;
     uint32_t a[4];
     if (TYPE == 0) {
@@ -304,23 +318,23 @@ __global__ void dequant_tiles_kernel(const uint8_t *tiles, const uint16_t *scale
         const int64_t row = (r & 1) ? r1 : r0;
         const float s = (r & 1) ? s1 : s0;
         const int k = k0 + ((r & 2) ? 16 : 0);
-        __nv_bfloat16 *dst = out + row * ld + k;
+        __half *dst = out + row * ld + k;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int q = int(int8_t(uint8_t(a[r] >> (8 * j))));
-            dst[j] = __float2bfloat16_rn(float(q) * s);
+            dst[j] = to_half_sat(float(q) * s);
         }
     }
 }
 
-/* fp32 [M][K] -> bf16 [M][Kp] (columns K..Kp-1 zero). */
-__global__ void round_bf16_kernel(const float *x, int M, int K, int Kp, __nv_bfloat16 *out) {
+/* fp32 [M][K] -> fp16 [M][Kp] (columns K..Kp-1 zero). */
+__global__ void round_f16_kernel(const float *x, int M, int K, int Kp, __half *out) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= int64_t(M) * Kp)
         return;
     const int64_t m = i / Kp;
     const int k = int(i - m * Kp);
-    out[i] = __float2bfloat16_rn(k < K ? x[m * K + k] : 0.0f);
+    out[i] = to_half_sat(k < K ? x[m * K + k] : 0.0f);
 }
 
 /* ---- host side ---- */
@@ -355,7 +369,7 @@ bool encode_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols_e
     const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode(
-        map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+        map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -365,7 +379,7 @@ template <int BN, int STAGES>
 cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs &g,
                       cudaStream_t stream) {
     using S = GemmSmem<BN, STAGES>;
-    auto k = gemm_bf16_kernel<BN, STAGES>;
+    auto k = gemm_f16_kernel<BN, STAGES>;
     cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
     if (e != cudaSuccess)
@@ -378,41 +392,51 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs
 
 } // namespace
 
-cudaError_t dequant_tiles_bf16(const TileMatrix &m, uint16_t *out, cudaStream_t stream) {
+cudaError_t dequant_tiles_f16(const TileMatrix &m, uint16_t *out, cudaStream_t stream) {
     const int64_t threads = int64_t(m.shape.row_tiles) * m.shape.blocks * 32;
     const int grid = int((threads + 255) / 256);
-    if (m.shape.order != kRowMajor)
-        return cudaErrorInvalidValue;
-    auto *o = reinterpret_cast<__nv_bfloat16 *>(out);
+    auto *o = reinterpret_cast<__half *>(out);
+    const int rt = int(m.shape.row_tiles), nb = int(m.shape.blocks), order = m.shape.order;
     if (m.shape.type == 1)
-        dequant_tiles_kernel<1><<<grid, 256, 0, stream>>>(m.data, m.scales, int(m.shape.row_tiles),
-                                                          int(m.shape.blocks), o);
+        dequant_tiles_kernel<1><<<grid, 256, 0, stream>>>(m.data, m.scales, rt, nb, order, o);
     else
-        dequant_tiles_kernel<0><<<grid, 256, 0, stream>>>(m.data, m.scales, int(m.shape.row_tiles),
-                                                          int(m.shape.blocks), o);
+        dequant_tiles_kernel<0><<<grid, 256, 0, stream>>>(m.data, m.scales, rt, nb, order, o);
     count_launches(1);
     return cudaGetLastError();
 }
 
-cudaError_t round_bf16(const float *x, int M, int K, int Kp, uint16_t *out, cudaStream_t stream) {
+cudaError_t round_f16(const float *x, int M, int K, int Kp, uint16_t *out, cudaStream_t stream) {
     const int64_t n = int64_t(M) * Kp;
-    round_bf16_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(
-        x, M, K, Kp, reinterpret_cast<__nv_bfloat16 *>(out));
+    round_f16_kernel<<<int((n + 255) / 256), 256, 0, stream>>>(
+        x, M, K, Kp, reinterpret_cast<__half *>(out));
     count_launches(1);
     return cudaGetLastError();
 }
 
-cudaError_t gemm_bf16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
-                      float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream) {
+cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
+                      float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream,
+                      bool accumulate) {
     if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0 ||
         (reinterpret_cast<uintptr_t>(A) & 15) != 0 || (reinterpret_cast<uintptr_t>(B) & 15) != 0)
         return cudaErrorInvalidValue;
+    /* the widest output tile (256, 128, 64 columns) that still gives every
+     * SM a tile, so small matrices do not leave most of the GPU idle */
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int mt = (M + kBM - 1) / kBM;
+    int bn = 256;
+    while (bn > 64 && mt * ((N + bn - 1) / bn) < sms)
+        bn /= 2;
     CUtensorMap ma, mb;
-    const bool wide = N >= 2048;
-    if (!encode_map(&ma, A, M, K, kBM) || !encode_map(&mb, B, N_alloc, K, wide ? 256 : 128))
+    if (!encode_map(&ma, A, M, K, kBM) || !encode_map(&mb, B, N_alloc, K, bn))
         return cudaErrorInvalidValue;
-    const GemmArgs g{M, N, K, Y, ldy, error, limit_ns};
-    return wide ? launch_bn<256, 4>(ma, mb, g, stream) : launch_bn<128, 6>(ma, mb, g, stream);
+    const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns};
+    if (bn == 256)
+        return launch_bn<256, 4>(ma, mb, g, stream);
+    if (bn == 128)
+        return launch_bn<128, 6>(ma, mb, g, stream);
+    return launch_bn<64, 8>(ma, mb, g, stream);
 }
 
 } // namespace nut

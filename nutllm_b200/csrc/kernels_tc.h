@@ -22,13 +22,14 @@ cudaError_t launch_qmatvec_tc(const TileMatrix &m, const float *x, float *y,
                               int *error, uint64_t limit_ns, cudaStream_t stream);
 
 /* Prefill GEMM (gemm_tc.cu).  Y[M][N] (row stride ldy, fp32) =
- * A[M][K] B[N][K]^T with bf16 operands (K a multiple of 64, B allocated
+ * A[M][K] B[N][K]^T with fp16 operands (K a multiple of 64, B allocated
  * with N_alloc >= N rows); device-side timeouts land in *error. */
-cudaError_t gemm_bf16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
-                      float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream);
-/* Fragment tiles (row-major order) -> bf16 [row_tiles * 16][blocks * 32]. */
-cudaError_t dequant_tiles_bf16(const TileMatrix &m, uint16_t *out, cudaStream_t stream);
-/* fp32 [M][K] -> bf16 [M][Kp], zero padded. */
-cudaError_t round_bf16(const float *x, int M, int K, int Kp, uint16_t *out, cudaStream_t stream);
+cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
+                     float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream,
+                     bool accumulate = false);
+/* Fragment tiles (any tile order) -> fp16 [row_tiles * 16][blocks * 32]. */
+cudaError_t dequant_tiles_f16(const TileMatrix &m, uint16_t *out, cudaStream_t stream);
+/* fp32 [M][K] -> fp16 [M][Kp], zero padded, saturating. */
+cudaError_t round_f16(const float *x, int M, int K, int Kp, uint16_t *out, cudaStream_t stream);
 
 } // namespace nut

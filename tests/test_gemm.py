@@ -1,10 +1,12 @@
 """The prefill GEMM (nut_qmatrix_gemm) on the tensor cores.
 
-Y[tokens][rows] = X[tokens][cols] Q^T with bf16 operands and fp32
-accumulation.  Rounding both operands to bf16 perturbs each product by a
-relative 2^-8 + 2^-8 at most (plus fp32 accumulation, far smaller), so every
-element must satisfy |y - exact| <= 2^-7 sum_k |x_k w_k|; "exact" is the
-float64 product of X and the exactly dequantised weights (q * scale).
+Y[tokens][rows] = X[tokens][cols] Q^T with fp16 operands and fp32
+accumulation.  Rounding both operands to fp16 perturbs each product by a
+relative 2^-11 + 2^-11 at most (plus fp32 accumulation, far smaller; the
+activations here are N(0, 1), so fp16's subnormal range only adds an
+absolute error far below 1e-6), so every element must satisfy
+|y - exact| <= 2^-10 sum_k |x_k w_k| + 1e-6; "exact" is the float64
+product of X and the exactly dequantised weights (q * scale).
 """
 import numpy as np
 import pytest
@@ -41,13 +43,13 @@ def run_gemm(gpu, rows, cols, tokens, qtype):
     xd = torch.from_numpy(x).to(dev)
     yd = torch.full((tokens, rows), float("nan"), device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    for _ in range(2):  # the second call reuses the cached bf16 weights
+    for _ in range(2):  # the second call reuses the cached fp16 weights
         m.gemm_async(xd.data_ptr(), tokens, yd.data_ptr(), stream)
     torch.cuda.synchronize(dev)
     m.check()
     wd = dequantize(q)
     exact = x.astype(np.float64) @ wd.T
-    bound = 2.0 ** -7 * (np.abs(x).astype(np.float64) @ np.abs(wd).T) + 1e-6
+    bound = 2.0 ** -10 * (np.abs(x).astype(np.float64) @ np.abs(wd).T) + 1e-6
     return yd.cpu().numpy().astype(np.float64), exact, bound
 
 
@@ -56,7 +58,7 @@ SHAPES = [(2048, 2048, 512), (5632, 2048, 512), (2048, 5632, 512)]
 
 @pytest.mark.parametrize("qtype", [nb.INT4, nb.INT8], ids=["int4", "int8"])
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}xM{s[2]}")
-def test_gemm_within_bf16_bound(gpu, qtype, shape):
+def test_gemm_within_f16_bound(gpu, qtype, shape):
     y, exact, bound = run_gemm(gpu, *shape, qtype)
     err = np.abs(y - exact)
     assert np.all(np.isfinite(y))

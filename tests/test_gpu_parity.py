@@ -102,7 +102,10 @@ def _dequantize(q: nb.QuantizedMatrix) -> np.ndarray:
     return (vals * np.repeat(scales, 32)[:n]).reshape(q.rows, q.cols)
 
 
-def _run(name, orc, gpu, steps=None, prompt_len=None):
+def _run(name, orc, gpu, steps=None, prompt_len=None, prefill_min=0):
+    """Greedy generation on the GPU and in the oracle.  prefill_min = 0 keeps
+    the prompt on the per-token path (the tight bound); otherwise prompts of
+    at least that many tokens take the batched bf16 GEMM prefill."""
     wl = syn.WORKLOADS[name]
     c = wl.model_config()
     w = syn.build_model(c, wl.qtype, SEED)
@@ -111,6 +114,7 @@ def _run(name, orc, gpu, steps=None, prompt_len=None):
     om = orc.model(w)
     ids_o, lg_o, hid_o = om.generate(prompt, steps)
     model = nb.DeviceModel(w, gpu)
+    model.set_prefill_threshold(prefill_min)
     kv = nb.KVCache(model)
     ids_g, lg_g, stats = nb.generate_greedy(model, kv, prompt, steps,
                                             stop_at_eos=False, want_logits=True)
@@ -203,3 +207,31 @@ def test_tinyllama_int8_long_context(gpu, orc):
     first_close = next((i for i, m in enumerate(margin) if m < 2 * LOGIT_ATOL),
                        len(margin))
     assert np.array_equal(r["ids_g"][:first_close], r["ids_o"][:first_close])
+
+
+def _batched_deviation(r):
+    err = np.abs(r["lg_g"] - r["lg_o"])
+    rel = err / np.maximum(np.abs(r["lg_o"]), 1e-6)
+    return float(err.max()), float(np.median(err)), float(rel[np.abs(r["lg_o"]) > 0.5].max())
+
+
+# The batched prefill runs every projection of the prompt with fp16
+# operands (weights q * scale and activations rounded to fp16, fp32
+# accumulation), so hidden states and the KV cache carry fp16 rounding
+# through every layer; its stated bound is looser than the per-token path's:
+PREFILL_ATOL = 3e-2
+PREFILL_RTOL = 1e-2
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name,prompt_len", [("tinyllama-int8-long", 200), ("tiny-int8", 100)])
+def test_batched_prefill_generation(gpu, orc, name, prompt_len):
+    """The prompt prefilled as one batch of tensor-core GEMMs, then greedy
+    decoding: every step's logits within the prefill bound, and the median
+    deviation an order of magnitude inside it."""
+    r = _run(name, orc, gpu, steps=8, prompt_len=prompt_len, prefill_min=1)
+    mx, med, rel = _batched_deviation(r)
+    print(f"batched prefill {name}: max abs {mx:.3e}, median {med:.3e}, max rel {rel:.3e}")
+    err = np.abs(r["lg_g"] - r["lg_o"])
+    assert np.all(err <= PREFILL_ATOL + PREFILL_RTOL * np.abs(r["lg_o"])), f"max {mx:.3e}"
+    assert med <= PREFILL_ATOL / 10
