@@ -76,6 +76,8 @@ def parse():
                    help="skip the kernel microbenchmarks")
     p.add_argument("--micro-only", action="store_true",
                    help="run only the kernel microbenchmarks (one JSON line)")
+    p.add_argument("--micro-shape", default=None,
+                   help="restrict the microbenchmarks to one ROWSxCOLS weight shape")
     return p.parse_args()
 
 
@@ -511,6 +513,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if args.micro_shape:
+        r, c = (int(v) for v in args.micro_shape.lower().split("x"))
+        QMATVEC_SHAPES[:] = [(r, c)]
     if args.micro_only:
         run_micro(local)
         return

@@ -170,7 +170,9 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+    /* blockIdx.x walks the M tiles fastest, so the CTAs that share one B
+     * (weight) tile run together and all but the first read it from L2 */
+    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
     const int kb_count = g.K / kBK;
 
     if (threadIdx.x == 0) {
@@ -384,7 +386,7 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
     if (e != cudaSuccess)
         return e;
-    const dim3 grid((g.N + BN - 1) / BN, (g.M + kBM - 1) / kBM);
+    const dim3 grid((g.M + kBM - 1) / kBM, (g.N + BN - 1) / BN);
     k<<<grid, kThreadsG, S::kBytes, stream>>>(a, b, g);
     count_launches(1);
     return cudaGetLastError();
