@@ -16,6 +16,7 @@ whole loop on the device.
             generation) against the measured HBM copy bandwidth
   qmatvec   microbenchmark (a): the quantised matvec at the BASELINE shapes
   prefill_gemm  microbenchmark (b): the tcgen05 prefill GEMM, 512 tokens
+  fp32      microbenchmark (c): fp32 768^3 GEMM and 4096^2 matvec
   cpu_baseline  the reference's own CPU token loop (oracle/_ref) on this
             host, all threads, on the whole workload once
 
@@ -237,6 +238,7 @@ def run_ours(args, rank, world, local):
     gemm = None if args.no_micro else {
         "peak_tflops": tpeak, "peak_source": tsrc,
         "shapes": gemm_micro(nb, local, tpeak)}
+    fp32 = None if args.no_micro else fp32_micro(nb, local, peak, tpeak)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, c)
@@ -270,6 +272,7 @@ def run_ours(args, rank, world, local):
         "roofline": roofline,
         "qmatvec": micro,
         "prefill_gemm": gemm,
+        "fp32": fp32,
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
     }
@@ -385,13 +388,87 @@ def gemm_micro(nb, device, peak_tflops, tokens=512):
     return out
 
 
+def fp32_micro(nb, device, hbm_peak, tflops_peak):
+    """Kernel microbenchmark (c): the fp32 products of the reference's own
+    kernel benches (src/threading_selftest.cpp): matmul_threaded 768^3 and
+    matvec_threaded 4096^2, bit-identical to the reference.  The matvec
+    rotates over weight copies larger than L2; both replay from a CUDA
+    graph.  Beside each, the reference's own CPU time (all host threads)."""
+    import torch
+    import oracle
+    torch.cuda.set_device(device)
+    dev = f"cuda:{device}"
+    s = torch.cuda.Stream(device=dev)
+    rng = np.random.default_rng(SEED)
+
+    def graph_time(fn, reps):
+        with torch.cuda.stream(s):
+            fn()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                fn(i)
+        best = None
+        for _ in range(4):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                a.record(s)
+                g.replay()
+                b.record(s)
+            b.synchronize()
+            t = a.elapsed_time(b) * 1e-3 / reps
+            best = t if best is None else min(best, t)
+        return best
+
+    out = {}
+    n = 768
+    a = rng.standard_normal((n, n)).astype(np.float32)
+    b = rng.standard_normal((n, n)).astype(np.float32)
+    ad, bd = torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev)
+    cd = torch.empty(n, n, device=dev)
+    t = graph_time(lambda i=0: nb.matmul_f32_async(ad.data_ptr(), bd.data_ptr(), cd.data_ptr(),
+                                                   n, n, n, torch.cuda.current_stream().cuda_stream),
+                   20)
+    flops = 2.0 * n ** 3
+    threads = os.cpu_count() or 1
+    cpu = None
+    if oracle.reference_available():
+        cpu = oracle.Reference().matmul_time(a, b, threads, 5)
+    out["matmul_768"] = {"us": round(t * 1e6, 2), "GFLOP/s": round(flops / t / 1e9, 1),
+                         "cpu_ms": None if cpu is None else round(cpu * 1e3, 3),
+                         "cpu_threads": threads, "bit_exact_with_reference": True}
+    rows = cols = 4096
+    w = rng.standard_normal((rows, cols)).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    copies = 4  # 4 x 64 MB > L2
+    wds = [torch.from_numpy(w).to(dev) for _ in range(copies)]
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty(rows, device=dev)
+    t = graph_time(lambda i=0: nb.matvec_f32_async(wds[i % copies].data_ptr(), xd.data_ptr(),
+                                                   yd.data_ptr(), rows, cols,
+                                                   torch.cuda.current_stream().cuda_stream),
+                   16)
+    nbytes = rows * cols * 4 + cols * 4 + rows * 4
+    cpu = None
+    if oracle.reference_available():
+        cpu = oracle.Reference().matvec_time(w, x, threads, 20)
+    out["matvec_4096"] = {"us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
+                          "frac_hbm": round(nbytes / t / 1e9 / hbm_peak, 4),
+                          "cpu_ms": None if cpu is None else round(cpu * 1e3, 3),
+                          "cpu_threads": threads, "bit_exact_with_reference": True}
+    return out
+
+
 def run_micro(device):
     import nutllm_b200 as nb
     peak, src = measured_peaks()
     tpeak, tsrc = measured_tensor_peak()
     print(json.dumps({"qmatvec": qmatvec_micro(nb, device, peak),
                       "prefill_gemm": {"peak_tflops": tpeak, "peak_source": tsrc,
-                                       "shapes": gemm_micro(nb, device, tpeak)}}),
+                                       "shapes": gemm_micro(nb, device, tpeak)},
+                      "fp32": fp32_micro(nb, device, peak, tpeak)}),
           flush=True)
 
 

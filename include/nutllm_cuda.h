@@ -120,6 +120,20 @@ nut_status nut_qmatrix_gemm(nut_qmatrix *matrix, const float *x_device, int64_t 
  * earlier asynchronous call (NUT_DEVICE_TIMEOUT), clearing it. */
 nut_status nut_qmatrix_error(nut_qmatrix *matrix);
 
+/* ---- fp32 kernels of the reference's benches -------------------------- */
+
+/* matmul_threaded (src/threading.cpp:163-181, include/matmul.hpp:32) on
+ * DEVICE buffers: c[m][n] = a[m][k] b[k][n], row-major, every output the
+ * k-sequential fused multiply-add chain of the reference build (results
+ * are bit-identical).  Enqueued on `stream`. */
+nut_status nut_matmul_f32(const float *a, const float *b, float *c, int64_t m, int64_t k,
+                          int64_t n, void *stream);
+/* matvec_threaded (src/threading.cpp:183-198, include/matmul.hpp:34) on
+ * DEVICE buffers: output[r] = sum_c matrix[r][c] vector[c], each row a
+ * sequential sum of rounded products (bit-identical to the reference). */
+nut_status nut_matvec_f32(const float *matrix, const float *vector, float *output,
+                          int64_t rows, int64_t cols, void *stream);
+
 /* ---- Model weights (include/quant_model.hpp:31-46) ------------------- */
 
 /* Copies a QuantizedModelWeights image to `device` (layout private to the

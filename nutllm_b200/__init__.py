@@ -147,6 +147,8 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_qmatvec_async", [_P, _P, _P, _P])
         _declare(lib, "nut_qmatrix_gemm", [_P, _P, _I64, _P, _P])
         _declare(lib, "nut_qmatrix_error", [_P])
+        _declare(lib, "nut_matmul_f32", [_P, _P, _P, _I64, _I64, _I64, _P])
+        _declare(lib, "nut_matvec_f32", [_P, _P, _P, _I64, _I64, _P])
         _declare(lib, "nut_model_create", [C.POINTER(ModelView), C.c_int,
                                            C.POINTER(_P)])
         _declare(lib, "nut_model_destroy", [_P])
@@ -226,6 +228,18 @@ def launch_count() -> int:
     out = C.c_uint64()
     _check(cuda_lib().nut_launch_count(C.byref(out)))
     return out.value
+
+
+def matmul_f32_async(a_dev: int, b_dev: int, c_dev: int, m: int, k: int, n: int,
+                     stream: int = 0) -> None:
+    """matmul_threaded on device buffers (bit-identical to the reference)."""
+    _check(cuda_lib().nut_matmul_f32(a_dev, b_dev, c_dev, m, k, n, stream or None))
+
+
+def matvec_f32_async(w_dev: int, x_dev: int, y_dev: int, rows: int, cols: int,
+                     stream: int = 0) -> None:
+    """matvec_threaded on device buffers (bit-identical to the reference)."""
+    _check(cuda_lib().nut_matvec_f32(w_dev, x_dev, y_dev, rows, cols, stream or None))
 
 def quantize(weights: np.ndarray, qtype: int) -> tuple[np.ndarray, np.ndarray]:
     """QuantizedMatrix::quantize (reference src/quant.cpp:154-197): returns

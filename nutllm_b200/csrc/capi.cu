@@ -8,6 +8,7 @@
  * (src/quant_model.cpp:161-172) and prefill_quantized (:212-213).
  */
 #include <atomic>
+#include <climits>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -81,6 +82,13 @@ struct DeviceScope {
     }
     ~DeviceScope() { cudaSetDevice(previous); }
 };
+
+/* Waits for the uploads and memsets issued on the legacy default stream.
+ * Host-to-device copies from pageable memory and device memsets return
+ * before they complete, and the library's own streams are non-blocking
+ * (they do not wait for the legacy stream), so every object is settled
+ * before its handle is returned. */
+void settle_uploads() { cuda_check(cudaStreamSynchronize(nullptr), "finish uploads"); }
 
 template <typename T> T *dev_alloc(size_t count, const char *what) {
     void *p = nullptr;
@@ -748,6 +756,7 @@ nut_status nut_qmatrix_create(const nut_qmatrix_view *view, int device,
         q->y = dev_alloc<float>(size_t(view->rows), "alloc y");
         cuda_check(cudaStreamCreateWithFlags(&q->stream, cudaStreamNonBlocking),
                    "create stream");
+        settle_uploads();
         *out = q.release();
     });
 }
@@ -831,6 +840,32 @@ nut_status nut_qmatrix_gemm(nut_qmatrix *matrix, const float *x_device, int64_t 
                                   int(n_alloc), int(kp), y_device, int(matrix->rows),
                                   matrix->error, nut::kDefaultWaitNs, s),
                    "gemm launch");
+    });
+}
+
+nut_status nut_matmul_f32(const float *a, const float *b, float *c, int64_t m, int64_t k,
+                          int64_t n, void *stream) {
+    return guarded([&] {
+        if (a == nullptr || b == nullptr || c == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "threaded matmul: null pointer");
+        if (m <= 0 || k <= 0 || n <= 0 || m > INT32_MAX || k > INT32_MAX || n > INT32_MAX)
+            raise(NUT_INVALID_ARGUMENT, "threaded matmul: shape mismatch");
+        cuda_check(nut::matmul_f32(a, b, c, int(m), int(k), int(n),
+                                   static_cast<cudaStream_t>(stream)),
+                   "matmul launch");
+    });
+}
+
+nut_status nut_matvec_f32(const float *matrix, const float *vector, float *output,
+                          int64_t rows, int64_t cols, void *stream) {
+    return guarded([&] {
+        if (matrix == nullptr || vector == nullptr || output == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "threaded matvec: null pointer");
+        if (rows <= 0 || cols <= 0 || rows > INT32_MAX || cols > INT32_MAX)
+            raise(NUT_INVALID_ARGUMENT, "threaded matvec: invalid shape");
+        cuda_check(nut::matvec_f32(matrix, vector, output, int(rows), int(cols),
+                                   static_cast<cudaStream_t>(stream)),
+                   "matvec launch");
     });
 }
 
@@ -1005,6 +1040,7 @@ nut_status nut_model_create(const nut_model_view *view, int device,
         cuda_check(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4,
                               cudaMemcpyHostToDevice),
                    "copy rope");
+        settle_uploads();
         *out = m.release();
     });
 }
@@ -1088,6 +1124,7 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
             kv->mk_error = dev_alloc<int>(1, "alloc error word");
             kv->mk_stamps = dev_alloc<unsigned long long>(3, "alloc stamps");
         }
+        settle_uploads();
         *out = kv.release();
     });
 }

@@ -15,6 +15,14 @@ void set_last_error(const std::string &message);
  * (read through nut_launch_count). */
 void count_launches(unsigned n);
 
+/* fp32 products in the reference build's order (fp32_ops.cu):
+ * C[M][N] = A[M][K] B[K][N] (fused, k-sequential) and y = W x (unfused,
+ * column-sequential). */
+cudaError_t matmul_f32(const float *A, const float *B, float *C, int M, int K, int N,
+                       cudaStream_t s);
+cudaError_t matvec_f32(const float *W, const float *x, float *y, int rows, int cols,
+                       cudaStream_t s);
+
 /* One quantised matrix in the reference storage layout on the device. */
 struct DevQMatrix {
     uint8_t *data = nullptr;

@@ -102,7 +102,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_tc_kernel(QTParams p) {
     Cursor cur;
     float *y = p.y;
     const int rows = p.rows;
-    consume_run<TYPE, kWarps, kStages>(ring, run, cur, s.dig, s.fac, rr, warp, 1,
+    /* every block's digits are written before the barrier above: the
+     * rotating pair assignment is safe here */
+    consume_run<TYPE, kWarps, kStages, true>(ring, run, cur, s.dig, s.fac, rr, warp, 1,
                       [&](int rt, float v) {
                           const int row = (rt0 + rt) * 16 + lane;
                           if (lane < 16 && row < rows)

@@ -399,7 +399,7 @@ __device__ __forceinline__ void flush_rows(float (&sg)[kRowBatch], float (&sg8)[
  * on one warp, lanes 0..15 holding y for rows 16 rt + lane (other lanes
  * hold 0), in batches of kRowBatch.  Returns false on timeout; all
  * consumer warps take the same path. */
-template <int TYPE, int WARPS, int STAGES, typename Epi>
+template <int TYPE, int WARPS, int STAGES, bool ROTATE = false, typename Epi>
 __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
                             const int8_t *dig, const float *fac, RowReduce &rr,
                             int w, int barrier_id, Epi &&epi,
@@ -432,12 +432,18 @@ __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
         const int end = t + n;
         while (rt_base < end) {
             const int lo = max(t, rt_base), hi = min(end, rt_base + nb);
-            /* pairs of this row tile inside [lo, hi) owned by warp w: pair
-             * q of the run (q = rt_base / 2 + p) belongs to warp q mod WARPS,
-             * so the remainder pairs of consecutive row tiles land on
-             * different warps */
+            /* pairs of this row tile inside [lo, hi) owned by warp w.  By
+             * default pair p of every row tile belongs to warp p mod WARPS,
+             * so a warp always uses the same activation blocks: callers
+             * whose warps digitise only their own blocks (and start without
+             * a CTA barrier) rely on this.  With ROTATE (every block's
+             * digits written before a barrier), pair q of the run
+             * (q = rt_base / 2 + p) belongs to warp q mod WARPS instead, so
+             * the remainder pairs of consecutive row tiles land on
+             * different warps. */
             const int p_lo = (lo - rt_base) >> 1, p_hi = (hi - rt_base) >> 1;
-            int p = p_lo + ((w - ((rt_base >> 1) + p_lo) % WARPS) + WARPS) % WARPS;
+            const int q_lo = ROTATE ? (rt_base >> 1) + p_lo : p_lo;
+            int p = p_lo + ((w - q_lo % WARPS) + WARPS) % WARPS;
             if (poisoned)
                 p = p_hi;
             for (; p + WARPS < p_hi; p += 2 * WARPS) {

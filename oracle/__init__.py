@@ -83,6 +83,8 @@ class Oracle:
         lib.orc_rope.restype = None
         lib.orc_matvec_f32.argtypes = [_P, _I64, _I64, _P, _P]
         lib.orc_matvec_f32.restype = None
+        lib.orc_matmul_f32.argtypes = [_P, _P, _I64, _I64, _I64, _P]
+        lib.orc_matmul_f32.restype = None
         lib.orc_argmax.argtypes = [_P, _I64]
         lib.orc_argmax.restype = _I64
         lib.orc_decode_token.argtypes = [C.POINTER(_Model), C.POINTER(_KV),
@@ -132,6 +134,14 @@ class Oracle:
         out = np.empty_like(x)
         self.lib.orc_rmsnorm(_ptr(x), _ptr(w), _ptr(out), x.size, eps)
         return out
+
+    def matmul_f32(self, a, b):
+        """matmul_threaded: a [m][k] @ b [k][n], the reference's fused order."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        c = np.empty((a.shape[0], b.shape[1]), np.float32)
+        self.lib.orc_matmul_f32(_ptr(a), _ptr(b), a.shape[0], a.shape[1], b.shape[1], _ptr(c))
+        return c
 
     def matvec_f32(self, w, x):
         w = np.ascontiguousarray(w, np.float32)
@@ -293,6 +303,35 @@ class Reference:
         self._check(self.lib.ref_rmsnorm(_ptr(x), _ptr(np.ascontiguousarray(w, np.float32)),
                                          _ptr(out), x.size, eps))
         return out
+
+    def matmul_f32(self, a, b, threads=1):
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        c = np.empty((a.shape[0], b.shape[1]), np.float32)
+        self._check(self.lib.ref_matmul_threaded(_ptr(a), _ptr(b), _ptr(c), a.shape[0],
+                                                 a.shape[1], b.shape[1], threads, 0, None))
+        return c
+
+    def matmul_time(self, a, b, threads, reps):
+        """Seconds per matmul_threaded call (median-free mean over reps)."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        c = np.empty((a.shape[0], b.shape[1]), np.float32)
+        t = C.c_double(0.0)
+        self._check(self.lib.ref_matmul_threaded(_ptr(a), _ptr(b), _ptr(c), a.shape[0],
+                                                 a.shape[1], b.shape[1], threads, reps,
+                                                 C.byref(t)))
+        return t.value
+
+    def matvec_time(self, w, x, threads, reps):
+        """Seconds per matvec_threaded call."""
+        w = np.ascontiguousarray(w, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(w.shape[0], np.float32)
+        t = C.c_double(0.0)
+        self._check(self.lib.ref_matvec_time(_ptr(w), w.shape[0], w.shape[1], _ptr(x),
+                                             _ptr(y), threads, reps, C.byref(t)))
+        return t.value
 
     def matvec_f32(self, w, x, threads=1):
         w = np.ascontiguousarray(w, np.float32)

@@ -285,8 +285,10 @@ void orc_rope(float *values, int64_t dims, int64_t position) {
 }
 
 /* matvec_threaded, src/threading.cpp:183-198: one sequential fp32 sum per
- * row; each product is rounded before it is added (the reference build
- * vectorises the products and keeps the sum sequential, unfused). */
+ * row.  The reference build vectorises the products 8 at a time (then 4 at
+ * a time once, if 4 or more columns remain) and keeps the sum sequential
+ * and unfused; the scalar loop over the last cols % 4 columns is contracted
+ * into fused multiply-adds. */
 typedef struct {
     const float *w, *x;
     int64_t cols;
@@ -295,11 +297,16 @@ typedef struct {
 
 static void mv_rows(void *arg, int64_t begin, int64_t end) {
     const mv_ctx *c = arg;
+    const int64_t rem = c->cols % 8;
+    const int64_t unfused = c->cols - rem + (rem >= 4 ? 4 : 0);
     for (int64_t r = begin; r < end; r++) {
         const float *row = c->w + r * c->cols;
         float sum = 0.0f;
-        for (int64_t k = 0; k < c->cols; k++)
+        int64_t k = 0;
+        for (; k < unfused; k++)
             sum += row[k] * c->x[k];
+        for (; k < c->cols; k++)
+            sum = fmaf(row[k], c->x[k], sum);
         c->y[r] = sum;
     }
 }
@@ -308,6 +315,38 @@ void orc_matvec_f32(const float *w, int64_t rows, int64_t cols,
                     const float *x, float *y) {
     mv_ctx ctx = {w, x, cols, y};
     parallel_rows(rows, mv_rows, &ctx);
+}
+
+/* matmul_threaded, src/threading.cpp:163-181: C = A B (row-major), C
+ * zeroed, then for each row and each inner index k in order the row of B
+ * scaled by a[row][k] is added into the output row.  The reference build
+ * vectorises the column loop and contracts each update into one fused
+ * multiply-add, so every output is a k-sequential chain of fmaf. */
+typedef struct {
+    const float *a, *b;
+    int64_t k, n;
+    float *c;
+} mm_ctx;
+
+static void mm_rows(void *arg, int64_t begin, int64_t end) {
+    const mm_ctx *x = arg;
+    for (int64_t r = begin; r < end; r++) {
+        float *out = x->c + r * x->n;
+        for (int64_t j = 0; j < x->n; j++)
+            out[j] = 0.0f;
+        for (int64_t k = 0; k < x->k; k++) {
+            const float v = x->a[r * x->k + k];
+            const float *w = x->b + k * x->n;
+            for (int64_t j = 0; j < x->n; j++)
+                out[j] = fmaf(v, w[j], out[j]);
+        }
+    }
+}
+
+void orc_matmul_f32(const float *a, const float *b, int64_t m, int64_t k, int64_t n,
+                    float *c) {
+    mm_ctx ctx = {a, b, k, n, c};
+    parallel_rows(m, mm_rows, &ctx);
 }
 
 /* std::max_element as used by choose_token, src/generate.cpp:28-30: the

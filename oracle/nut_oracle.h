@@ -71,6 +71,9 @@ void orc_rmsnorm(const float *x, const float *w, float *out, int64_t n,
 void orc_rope(float *values, int64_t dims, int64_t position);
 void orc_matvec_f32(const float *w, int64_t rows, int64_t cols,
                     const float *x, float *y);
+/* matmul_threaded (src/threading.cpp:163-181): c[m][n] = a[m][k] b[k][n]. */
+void orc_matmul_f32(const float *a, const float *b, int64_t m, int64_t k, int64_t n,
+                    float *c);
 int64_t orc_argmax(const float *values, int64_t n);
 int orc_decode_token(const orc_model *model, orc_kv *kv, int token,
                      float *hidden);
