@@ -178,6 +178,11 @@ nut_status nut_kv_reset(nut_kv *kv);                   /* KVCache::reset */
 nut_status nut_kv_length(const nut_kv *kv, int64_t *length);
 nut_status nut_kv_set_length(nut_kv *kv, int64_t length); /* :231-235 */
 nut_status nut_kv_memory_bytes(const nut_kv *kv, uint64_t *bytes);
+/* KVCache::store (src/kvcache.cpp:216-229): writes the keys and values of
+ * every kv head (kv_heads x head_dim floats each, host) at (layer,
+ * position); the length is unchanged. */
+nut_status nut_kv_write(nut_kv *kv, int64_t layer, int64_t position, const float *keys,
+                        const float *values);
 /* KVCache::key / KVCache::value (src/kvcache.cpp:207-214): copies one
  * head_dim vector of each to the host (either pointer may be NULL). */
 nut_status nut_kv_read(const nut_kv *kv, int64_t layer, int64_t head,

@@ -1,5 +1,7 @@
 /* nutllm_host.h — C entry points of libnutllm.so, the C++17 host library
- * (load-time quantiser and seeded synthetic inputs).  Status codes are the
+ * (load-time quantiser, llama2.c loader, generation and seeded synthetic
+ * inputs; the C++ API itself is declared in nutllm_b200/host/, one header
+ * per reference header).  Status codes are the
  * nut_status values of nutllm_cuda.h. */
 #ifndef NUTLLM_HOST_H
 #define NUTLLM_HOST_H
@@ -22,6 +24,35 @@ int nut_host_quantize(const float *source, int64_t rows, int64_t cols,
 
 /* fp16 encoding of one positive scale as the quantiser rounds it. */
 int nut_host_scale_to_half(float value, uint16_t *bits);
+
+/* load_llama2c_quantized_model + generate_tokens_cached (reference
+ * include/llama2.hpp:27-29, include/generate.hpp:29-36): loads a llama2.c
+ * checkpoint, quantises it (type 0 INT8, 1 INT4) and generates up to
+ * max_tokens ids after the prompt on the current device, stopping at eos
+ * (token 1) like the reference.  temperature <= 0 is greedy; otherwise
+ * top-p sampling with std::mt19937(seed).  ids has room for max_tokens;
+ * stats (may be NULL) receives GenerationStats. */
+struct nut_generation_stats;
+int nut_host_llama2c_generate(const char *path, int32_t type, const int32_t *prompt,
+                              int64_t n, int64_t max_tokens, float temperature,
+                              float top_p, uint32_t seed, int32_t *ids, int64_t *n_out,
+                              struct nut_generation_stats *stats);
+
+/* Loads a llama2.c checkpoint on the host only and describes it: config
+ * (9 values in nut_config order: layers, heads, dim, head_dim, ffn_dim,
+ * vocab_size, max_seq, eos_token, kv_heads), whether the classifier is the
+ * embedding table, storage_bytes(), and a 64-bit FNV-1a digest of every
+ * loaded byte in this order: embeddings; per layer the data then scales of
+ * query, key, value, output, gate, up, down, then the attention and ffn
+ * norms; the final norm; the classifier when it is separate. */
+int nut_host_llama2c_inspect(const char *path, int32_t type, int64_t *config,
+                             int32_t *tied, uint64_t *storage_bytes, uint64_t *digest);
+
+/* The generation token choice (choose_token, reference
+ * src/generate.cpp:25-73) over `steps` rows of logits [steps][vocab] with
+ * one std::mt19937(seed) shared by the steps, as one generation uses it. */
+int nut_host_choose_tokens(const float *logits, int64_t steps, int64_t vocab,
+                           float temperature, float top_p, uint32_t seed, int64_t *tokens);
 
 /* Seeded synthetic inputs (documented in nutllm_b200/host/synth.cpp). */
 void nut_synth_normal(uint64_t seed, uint64_t stream, float sigma, float *out,

@@ -189,6 +189,14 @@ def host_lib() -> C.CDLL:
                                            _P, C.c_size_t], None)
         _declare(lib, "nut_synth_tokens", [C.c_uint64, C.c_uint64, C.c_int,
                                            C.c_int, _P, C.c_size_t], None)
+        _declare(lib, "nut_host_llama2c_generate",
+                 [C.c_char_p, C.c_int32, _P, _I64, _I64, C.c_float, C.c_float,
+                  C.c_uint32, _P, _PI64, C.POINTER(GenerationStats)])
+        _declare(lib, "nut_host_llama2c_inspect",
+                 [C.c_char_p, C.c_int32, _PI64, C.POINTER(C.c_int32),
+                  C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)])
+        _declare(lib, "nut_host_choose_tokens",
+                 [_P, _I64, _I64, C.c_float, C.c_float, C.c_uint32, _P])
         _host = lib
     return _host
 
@@ -273,6 +281,48 @@ def synth_normal(seed: int, stream: int, n: int, sigma: float = 0.02) -> np.ndar
 def synth_tokens(seed: int, stream: int, n: int, lo: int, hi: int) -> np.ndarray:
     out = np.empty(n, np.int32)
     host_lib().nut_synth_tokens(seed, stream, lo, hi, _ptr(out), n)
+    return out
+
+
+def llama2c_generate(path: str, qtype: int, prompt, max_tokens: int,
+                     temperature: float = 0.0, top_p: float = 1.0,
+                     seed: int = 1) -> tuple[np.ndarray, GenerationStats]:
+    """load_llama2c_quantized_model + generate_tokens_cached through the C++
+    host API (reference include/llama2.hpp:27-29, include/generate.hpp:29-36):
+    stops at eos (token 1) or a full context like the reference."""
+    lib = host_lib()
+    p = np.ascontiguousarray(prompt, np.int32)
+    ids = np.zeros(max(max_tokens, 1), np.int32)
+    n = C.c_int64(0)
+    st = GenerationStats()
+    _check(lib.nut_host_llama2c_generate(os.fsencode(path), qtype, _ptr(p), p.size,
+                                         max_tokens, temperature, top_p, seed, _ptr(ids),
+                                         C.byref(n), C.byref(st)), lib)
+    return ids[:n.value], st
+
+
+def llama2c_inspect(path: str, qtype: int) -> tuple[list, bool, int, int]:
+    """(config[9], tied classifier, storage_bytes, FNV-1a digest of the
+    loaded bytes) of the host loader; no device involved."""
+    lib = host_lib()
+    cfg = (C.c_int64 * 9)()
+    tied = C.c_int32(0)
+    nbytes = C.c_uint64(0)
+    digest = C.c_uint64(0)
+    _check(lib.nut_host_llama2c_inspect(os.fsencode(path), qtype, cfg, C.byref(tied),
+                                        C.byref(nbytes), C.byref(digest)), lib)
+    return list(cfg), bool(tied.value), nbytes.value, digest.value
+
+
+def choose_tokens(logits: np.ndarray, temperature: float, top_p: float,
+                  seed: int) -> np.ndarray:
+    """The generation token choice over rows of logits with one seeded
+    std::mt19937 (reference src/generate.cpp:25-73)."""
+    lib = host_lib()
+    lg = np.ascontiguousarray(np.atleast_2d(logits), np.float32)
+    out = np.zeros(lg.shape[0], np.int64)
+    _check(lib.nut_host_choose_tokens(_ptr(lg), lg.shape[0], lg.shape[1], temperature,
+                                      top_p, seed, _ptr(out)), lib)
     return out
 
 

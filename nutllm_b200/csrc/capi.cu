@@ -1173,6 +1173,30 @@ nut_status nut_kv_memory_bytes(const nut_kv *kv, uint64_t *bytes) {
     });
 }
 
+nut_status nut_kv_write(nut_kv *kv, int64_t layer, int64_t position, const float *keys,
+                        const float *values) {
+    return guarded([&] {
+        if (kv == nullptr || keys == nullptr || values == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "kv cache: null argument");
+        const nut_model *m = kv->model;
+        const nut_config &c = m->cfg;
+        if (layer < 0 || layer >= c.layers || position < 0 || position >= c.max_seq)
+            raise(NUT_OUT_OF_RANGE, "kv cache: store out of range");
+        DeviceScope scope(m->device);
+        const int64_t hd = c.head_dim;
+        for (int64_t h = 0; h < m->kv_heads; h++) {
+            const size_t off = size_t(((layer * m->kv_heads + h) * c.max_seq + position) * hd);
+            cuda_check(cudaMemcpyAsync(kv->keys + off, keys + h * hd, size_t(hd) * 4,
+                                       cudaMemcpyHostToDevice, m->stream),
+                       "store key");
+            cuda_check(cudaMemcpyAsync(kv->values + off, values + h * hd, size_t(hd) * 4,
+                                       cudaMemcpyHostToDevice, m->stream),
+                       "store value");
+        }
+        cuda_check(cudaStreamSynchronize(m->stream), "synchronize");
+    });
+}
+
 nut_status nut_kv_read(const nut_kv *kv, int64_t layer, int64_t head,
                        int64_t position, float *key, float *value) {
     return guarded([&] {

@@ -1,11 +1,16 @@
 /* C entry points of the host library (include/nutllm_host.h). */
 #include <cstring>
+#include <random>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "../../include/nutllm_cuda.h"
 #include "../../include/nutllm_host.h"
+#include "generate.hpp"
+#include "llama2.hpp"
 #include "quant.hpp"
+#include "quant_model.hpp"
 
 namespace {
 
@@ -33,6 +38,25 @@ template <typename F> int guarded(F &&body) {
     }
 }
 
+QuantType quant_type(int32_t type) {
+    if (type != 0 && type != 1)
+        throw std::invalid_argument("quantize: unknown type");
+    return type == 0 ? QuantType::int8 : QuantType::int4;
+}
+
+/* 64-bit FNV-1a over a byte stream. */
+struct Fnv1a {
+    uint64_t h = 0xcbf29ce484222325ull;
+    void add(const void *p, size_t n) {
+        const unsigned char *b = static_cast<const unsigned char *>(p);
+        for (size_t i = 0; i < n; i++) {
+            h ^= b[i];
+            h *= 0x100000001b3ull;
+        }
+    }
+    template <typename T> void add(const std::vector<T> &v) { add(v.data(), v.size() * sizeof(T)); }
+};
+
 } // namespace
 
 extern "C" {
@@ -58,6 +82,89 @@ int nut_host_quantize(const float *source, int64_t rows, int64_t cols,
 
 int nut_host_scale_to_half(float value, uint16_t *bits) {
     return guarded([&] { *bits = quant_scale_to_half(value); });
+}
+
+int nut_host_llama2c_generate(const char *path, int32_t type, const int32_t *prompt,
+                              int64_t n, int64_t max_tokens, float temperature,
+                              float top_p, uint32_t seed, int32_t *ids, int64_t *n_out,
+                              nut_generation_stats *stats) {
+    return guarded([&] {
+        if (path == nullptr || prompt == nullptr || n_out == nullptr || max_tokens < 0 ||
+            (max_tokens > 0 && ids == nullptr) || n < 0)
+            throw std::invalid_argument("generation: invalid argument");
+        const QuantizedModelWeights model = load_llama2c_quantized_model(path, quant_type(type));
+        SamplingConfig sampling;
+        sampling.max_tokens = size_t(max_tokens);
+        sampling.temperature = temperature;
+        sampling.top_p = top_p;
+        sampling.seed = seed;
+        GenerationStats st;
+        const std::vector<int> out =
+            generate_tokens_cached(model, std::vector<int>(prompt, prompt + n), sampling, &st);
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = int64_t(out.size());
+        if (stats != nullptr) {
+            stats->prefill_tokens = int64_t(st.prefill_tokens);
+            stats->generated_tokens = int64_t(st.generated_tokens);
+            stats->prefill_seconds = st.prefill_seconds;
+            stats->decode_seconds = st.decode_seconds;
+        }
+    });
+}
+
+int nut_host_llama2c_inspect(const char *path, int32_t type, int64_t *config,
+                             int32_t *tied, uint64_t *storage_bytes, uint64_t *digest) {
+    return guarded([&] {
+        if (path == nullptr)
+            throw std::invalid_argument("llama2 checkpoint: null path");
+        const QuantizedModelWeights m = load_llama2c_quantized_model(path, quant_type(type));
+        const ModelConfig &c = m.config;
+        if (config != nullptr) {
+            const size_t v[9] = {c.layers,     c.heads,   c.dim,       c.head_dim, c.ffn_dim,
+                                 c.vocab_size, c.max_seq, c.eos_token, c.kv_heads};
+            for (int i = 0; i < 9; i++)
+                config[i] = int64_t(v[i]);
+        }
+        if (tied != nullptr)
+            *tied = m.tied_embeddings ? 1 : 0;
+        if (storage_bytes != nullptr)
+            *storage_bytes = uint64_t(m.storage_bytes());
+        if (digest != nullptr) {
+            Fnv1a f;
+            f.add(m.embeddings.data(), m.embeddings.size() * sizeof(float));
+            for (const QuantizedLayerWeights &l : m.layers) {
+                for (const QuantizedMatrix *q :
+                     {&l.query, &l.key, &l.value, &l.output, &l.gate, &l.up, &l.down}) {
+                    f.add(q->data());
+                    f.add(q->scales());
+                }
+                f.add(l.attention_norm);
+                f.add(l.ffn_norm);
+            }
+            f.add(m.final_norm);
+            if (!m.tied_embeddings)
+                f.add(m.lm_head.data(), m.lm_head.size() * sizeof(float));
+            *digest = f.h;
+        }
+    });
+}
+
+int nut_host_choose_tokens(const float *logits, int64_t steps, int64_t vocab,
+                           float temperature, float top_p, uint32_t seed, int64_t *tokens) {
+    return guarded([&] {
+        if (steps < 0 || vocab < 0 || (steps > 0 && (logits == nullptr || tokens == nullptr)))
+            throw std::invalid_argument("sampling: invalid argument");
+        SamplingConfig sampling;
+        sampling.temperature = temperature;
+        sampling.top_p = top_p;
+        sampling.seed = seed;
+        std::mt19937 rng(seed);
+        std::vector<float> row(static_cast<size_t>(vocab));
+        for (int64_t s = 0; s < steps; s++) {
+            std::copy(logits + s * vocab, logits + (s + 1) * vocab, row.begin());
+            tokens[s] = int64_t(choose_token(row, sampling, rng));
+        }
+    });
 }
 
 } // extern "C"

@@ -1,0 +1,44 @@
+#pragma once
+/* Generation — host side of the drop-in for the reference's
+ * include/generate.hpp:11-36 (quantised overload of generate_tokens_cached,
+ * src/generate.cpp:174-216).
+ *
+ * temperature <= 0 (greedy) runs the whole loop on the device
+ * (nut_generate_greedy: prefill, then final norm + classifier + argmax and
+ * the next token's forward in one persistent launch), and the statistics
+ * are device-event times.  temperature > 0 reads each step's logits back
+ * and draws on the host with the reference's sampler, so a given seed picks
+ * the same ids as the reference for the same logits; its statistics are
+ * wall-clock, as in the reference. */
+#include <cstddef>
+#include <cstdint>
+#include <random>
+#include <vector>
+
+struct QuantizedModelWeights;
+
+struct SamplingConfig {
+    size_t max_tokens = 32;
+    float temperature = 0.0f;
+    float top_p = 1.0f;
+    uint32_t seed = 1;
+    size_t threads = 1;
+};
+
+struct GenerationStats {
+    size_t prefill_tokens = 0;
+    size_t generated_tokens = 0;
+    double prefill_seconds = 0.0;
+    double decode_seconds = 0.0;
+};
+
+std::vector<int> generate_tokens_cached(const QuantizedModelWeights &model,
+                                        const std::vector<int> &prompt,
+                                        const SamplingConfig &sampling,
+                                        GenerationStats *stats = nullptr);
+
+/* The token choice of one step (src/generate.cpp:25-73): first-index argmax
+ * for temperature <= 0; otherwise a draw from the smallest set of most
+ * probable tokens whose probability reaches top_p.  Exposed for tests. */
+size_t choose_token(const std::vector<float> &logits, const SamplingConfig &sampling,
+                    std::mt19937 &rng);

@@ -1,0 +1,231 @@
+/* llama2.c loader.  The checks and their exception classes and messages
+ * follow the reference (src/llama2.cpp:133-150,199-298) so callers see the
+ * same errors; reading is positioned std::ifstream reads of one tensor at a
+ * time, and the layers' projections are quantised by a few host threads
+ * (each matrix is quantised independently, so the bytes do not depend on
+ * the split). */
+#include "llama2.hpp"
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <fstream>
+#include <limits>
+#include <memory>
+#include <stdexcept>
+#include <thread>
+#include <utility>
+#include <vector>
+
+namespace {
+
+constexpr size_t kHeaderBytes = 7 * sizeof(int32_t);
+
+size_t mul_checked(size_t a, size_t b, const char *what) {
+    if (a != 0 && b > std::numeric_limits<size_t>::max() / a)
+        throw std::length_error(std::string("llama2 checkpoint: ") + what + " overflows");
+    return a * b;
+}
+
+void add_checked(size_t &sum, size_t v) {
+    if (v > std::numeric_limits<size_t>::max() - sum)
+        throw std::length_error("llama2 checkpoint: size overflows");
+    sum += v;
+}
+
+size_t dimension(int32_t v, const char *name) {
+    if (v <= 0)
+        throw std::runtime_error(std::string("llama2 checkpoint: invalid ") + name);
+    return size_t(v);
+}
+
+/* Section offsets, in floats from the end of the header. */
+struct Sections {
+    ModelConfig config;
+    bool shared_classifier = false;
+    size_t embeddings = 0, attention_norms = 0, wq = 0, wk = 0, wv = 0, wo = 0,
+           ffn_norms = 0, w1 = 0, w2 = 0, w3 = 0, final_norm = 0, classifier = 0;
+};
+
+class Checkpoint {
+public:
+    explicit Checkpoint(const std::string &path) : in_(path, std::ios::binary) {
+        if (!in_)
+            throw std::runtime_error("llama2 checkpoint: cannot open " + path);
+        in_.seekg(0, std::ios::end);
+        const std::streamoff end = in_.tellg();
+        if (end < 0)
+            throw std::runtime_error("llama2 checkpoint: cannot stat " + path);
+        size_ = size_t(end);
+        if (size_ == 0)
+            throw std::runtime_error("llama2 checkpoint: empty file");
+    }
+
+    size_t size() const { return size_; }
+
+    /* count floats starting `first` floats after the header. */
+    void read(float *dst, size_t first, size_t count) {
+        const size_t at = kHeaderBytes + mul_checked(first, sizeof(float), "read");
+        const size_t bytes = mul_checked(count, sizeof(float), "read");
+        if (at > size_ || bytes > size_ - at)
+            throw std::runtime_error("llama2 checkpoint: read outside file");
+        in_.clear();
+        in_.seekg(std::streamoff(at));
+        in_.read(reinterpret_cast<char *>(dst), std::streamsize(bytes));
+        if (!in_)
+            throw std::runtime_error("llama2 checkpoint: read failed");
+    }
+
+    void header(int32_t (&h)[7]) {
+        if (size_ < kHeaderBytes)
+            throw std::runtime_error("llama2 checkpoint: truncated header");
+        in_.seekg(0);
+        in_.read(reinterpret_cast<char *>(h), kHeaderBytes);
+        if (!in_)
+            throw std::runtime_error("llama2 checkpoint: read failed");
+    }
+
+private:
+    std::ifstream in_;
+    size_t size_ = 0;
+};
+
+Sections parse(Checkpoint &file) {
+    int32_t h[7];
+    file.header(h);
+    const size_t dim = dimension(h[0], "dimension");
+    const size_t ffn = dimension(h[1], "ffn dimension");
+    const size_t layers = dimension(h[2], "layer count");
+    const size_t heads = dimension(h[3], "head count");
+    const size_t kv_heads = dimension(h[4], "kv head count");
+    if (h[5] == 0 || h[5] == std::numeric_limits<int32_t>::min())
+        throw std::runtime_error("llama2 checkpoint: invalid vocabulary");
+    const size_t vocab = size_t(h[5] > 0 ? h[5] : -h[5]);
+    const size_t max_seq = dimension(h[6], "context length");
+    if (dim % heads != 0)
+        throw std::runtime_error("llama2 checkpoint: heads do not divide dimension");
+
+    Sections s;
+    s.config.layers = layers;
+    s.config.heads = heads;
+    s.config.dim = dim;
+    s.config.head_dim = dim / heads;
+    s.config.ffn_dim = ffn;
+    s.config.vocab_size = vocab;
+    s.config.max_seq = max_seq;
+    s.config.eos_token = 1;
+    s.config.kv_heads = kv_heads;
+    s.config.validate();
+    s.shared_classifier = h[5] > 0;
+
+    const size_t emb = mul_checked(vocab, dim, "embeddings");
+    const size_t norms = mul_checked(layers, dim, "norms");
+    const size_t att = mul_checked(layers, mul_checked(dim, dim, "attention matrix"),
+                                   "attention weights");
+    const size_t kv = mul_checked(layers, mul_checked(dim, s.config.kv_dim(), "kv matrix"),
+                                  "kv weights");
+    const size_t ff = mul_checked(layers, mul_checked(dim, ffn, "ffn matrix"), "ffn weights");
+    const size_t rope = mul_checked(max_seq, s.config.head_dim, "rope frequencies");
+
+    size_t at = 0;
+    auto section = [&](size_t count) {
+        const size_t here = at;
+        add_checked(at, count);
+        return here;
+    };
+    s.embeddings = section(emb);
+    s.attention_norms = section(norms);
+    s.wq = section(att);
+    s.wk = section(kv);
+    s.wv = section(kv);
+    s.wo = section(att);
+    s.ffn_norms = section(norms);
+    s.w1 = section(ff);
+    s.w2 = section(ff);
+    s.w3 = section(ff);
+    s.final_norm = section(dim);
+    section(rope);
+    s.classifier = s.shared_classifier ? s.embeddings : section(emb);
+    if (at > (std::numeric_limits<size_t>::max() - kHeaderBytes) / sizeof(float))
+        throw std::length_error("llama2 checkpoint: file size overflows");
+    if (file.size() != kHeaderBytes + at * sizeof(float))
+        throw std::runtime_error("llama2 checkpoint: size does not match configuration");
+    return s;
+}
+
+/* One projection of every layer: rows x cols per layer at `first`. */
+std::vector<QuantizedMatrix> quantize_layers(Checkpoint &file, size_t first, size_t rows,
+                                             size_t cols, size_t layers, QuantType type) {
+    const size_t n = mul_checked(rows, cols, "quantized projection");
+    const size_t workers =
+        std::max<size_t>(1, std::min<size_t>(layers, std::thread::hardware_concurrency()));
+    std::vector<std::vector<float>> raw(workers, std::vector<float>(n));
+    std::vector<QuantizedMatrix> out;
+    out.reserve(layers);
+    for (size_t base = 0; base < layers; base += workers) {
+        const size_t count = std::min(workers, layers - base);
+        for (size_t w = 0; w < count; w++)
+            file.read(raw[w].data(), first + (base + w) * n, n);
+        std::vector<std::unique_ptr<QuantizedMatrix>> done(count);
+        std::vector<std::exception_ptr> errors(count);
+        std::vector<std::thread> pool;
+        for (size_t w = 0; w < count; w++)
+            pool.emplace_back([&, w] {
+                try {
+                    done[w].reset(new QuantizedMatrix(
+                        QuantizedMatrix::quantize(raw[w].data(), rows, cols, type)));
+                } catch (...) {
+                    errors[w] = std::current_exception();
+                }
+            });
+        for (std::thread &t : pool)
+            t.join();
+        for (size_t w = 0; w < count; w++) {
+            if (errors[w])
+                std::rethrow_exception(errors[w]);
+            out.push_back(std::move(*done[w]));
+        }
+    }
+    return out;
+}
+
+std::vector<std::vector<float>> read_norms(Checkpoint &file, size_t first, size_t layers,
+                                           size_t dim) {
+    std::vector<std::vector<float>> norms(layers, std::vector<float>(dim));
+    for (size_t l = 0; l < layers; l++)
+        file.read(norms[l].data(), first + l * dim, dim);
+    return norms;
+}
+
+} // namespace
+
+QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, QuantType type) {
+    Checkpoint file(path);
+    const Sections s = parse(file);
+    const ModelConfig &c = s.config;
+    QuantizedModelWeights model(c, type, !s.shared_classifier);
+    model.tied_embeddings = s.shared_classifier;
+    file.read(model.embeddings.data(), s.embeddings, c.vocab_size * c.dim);
+
+    auto att_norms = read_norms(file, s.attention_norms, c.layers, c.dim);
+    auto wq = quantize_layers(file, s.wq, c.dim, c.dim, c.layers, type);
+    auto wk = quantize_layers(file, s.wk, c.kv_dim(), c.dim, c.layers, type);
+    auto wv = quantize_layers(file, s.wv, c.kv_dim(), c.dim, c.layers, type);
+    auto wo = quantize_layers(file, s.wo, c.dim, c.dim, c.layers, type);
+    auto ffn_norms = read_norms(file, s.ffn_norms, c.layers, c.dim);
+    auto gate = quantize_layers(file, s.w1, c.ffn_dim, c.dim, c.layers, type);
+    auto down = quantize_layers(file, s.w2, c.dim, c.ffn_dim, c.layers, type);
+    auto up = quantize_layers(file, s.w3, c.ffn_dim, c.dim, c.layers, type);
+    file.read(model.final_norm.data(), s.final_norm, c.dim);
+    if (!s.shared_classifier)
+        file.read(model.lm_head.data(), s.classifier, c.vocab_size * c.dim);
+
+    model.layers.reserve(c.layers);
+    for (size_t l = 0; l < c.layers; l++)
+        model.layers.emplace_back(std::move(wq[l]), std::move(wk[l]), std::move(wv[l]),
+                                  std::move(wo[l]), std::move(gate[l]), std::move(up[l]),
+                                  std::move(down[l]), std::move(att_norms[l]),
+                                  std::move(ffn_norms[l]));
+    return model;
+}

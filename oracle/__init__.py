@@ -92,6 +92,11 @@ class Oracle:
         lib.orc_logits.argtypes = [C.POINTER(_Model), _P, _P, C.POINTER(_I64)]
         lib.orc_generate.argtypes = [C.POINTER(_Model), C.POINTER(_KV), _P,
                                      _I64, _I64, _P, _P, _P]
+        lib.orc_choose_tokens.argtypes = [_P, _I64, _I64, C.c_float, C.c_float,
+                                          C.c_uint32, _P]
+        lib.orc_generate_sampled.argtypes = [C.POINTER(_Model), C.POINTER(_KV), _P,
+                                             _I64, _I64, C.c_float, C.c_float,
+                                             C.c_uint32, _P, C.POINTER(_I64)]
         self.lib = lib
 
     def _check(self, status):
@@ -149,6 +154,16 @@ class Oracle:
         y = np.empty(w.shape[0], np.float32)
         self.lib.orc_matvec_f32(_ptr(w), w.shape[0], w.shape[1], _ptr(x), _ptr(y))
         return y
+
+    def choose_tokens(self, logits: np.ndarray, temperature: float, top_p: float,
+                      seed: int) -> np.ndarray:
+        """choose_token over rows of logits with one seeded mt19937
+        (src/generate.cpp:25-73)."""
+        lg = np.ascontiguousarray(np.atleast_2d(logits), np.float32)
+        out = np.zeros(lg.shape[0], np.int64)
+        self._check(self.lib.orc_choose_tokens(_ptr(lg), lg.shape[0], lg.shape[1],
+                                               temperature, top_p, seed, _ptr(out)))
+        return out
 
     def model(self, weights) -> "OracleModel":
         return OracleModel(self, weights)
@@ -213,6 +228,19 @@ class OracleModel:
                                               _ptr(lg), _ptr(hid)))
         return ids[:steps], lg[:steps], hid
 
+    def generate_cached(self, prompt: Sequence[int], max_tokens: int,
+                        temperature: float = 0.0, top_p: float = 1.0,
+                        seed: int = 1) -> np.ndarray:
+        """generate_tokens_cached (src/generate.cpp:174-216): eos stop and
+        context limit, greedy or top-p sampled."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(max(max_tokens, 1), np.int32)
+        n = _I64(0)
+        self.o._check(self.o.lib.orc_generate_sampled(
+            C.byref(self._model), C.byref(self.kv), _ptr(p), p.size, max_tokens,
+            temperature, top_p, seed, _ptr(ids), C.byref(n)))
+        return ids[:n.value]
+
 
 # ------------------------------------------------------------- reference
 
@@ -251,8 +279,13 @@ class Reference:
         lib.ref_generate.argtypes = [_P, _P, S, S, S, _P, _P, _P,
                                      C.POINTER(C.c_double), C.POINTER(C.c_double)]
         lib.ref_trace.argtypes = [_P, _P, S, S, S, _P]
-        lib.ref_llama2c_generate.argtypes = [C.c_char_p, C.c_int, _P, S, S, _P,
-                                             C.POINTER(S)]
+        lib.ref_llama2c_generate.argtypes = [C.c_char_p, C.c_int, _P, S, S, C.c_float,
+                                             C.c_float, C.c_uint, _P, C.POINTER(S)]
+        lib.ref_llama2c_inspect.argtypes = [C.c_char_p, C.c_int, C.POINTER(_I64),
+                                            C.POINTER(C.c_int), C.POINTER(C.c_uint64),
+                                            C.POINTER(C.c_uint64)]
+        lib.ref_llama2c_encode.argtypes = [C.c_char_p, S, C.c_char_p, C.c_int, _P, S,
+                                           C.POINTER(S)]
         self.lib = lib
 
     def _check(self, status):
@@ -346,13 +379,32 @@ class Reference:
         return RefModel(self, config, qtype, seed, tied, layer_fp32, embeddings,
                         lm_head)
 
-    def llama2c_generate(self, path: str, qtype: int, prompt, max_tokens: int):
+    def llama2c_generate(self, path: str, qtype: int, prompt, max_tokens: int,
+                         temperature: float = 0.0, top_p: float = 1.0, seed: int = 1):
+        """load_llama2c_quantized_model + generate_tokens_cached (eos stop)."""
         p = np.ascontiguousarray(prompt, np.int32)
-        ids = np.zeros(max_tokens, np.int32)
+        ids = np.zeros(max(max_tokens, 1), np.int32)
         n = C.c_size_t(0)
         self._check(self.lib.ref_llama2c_generate(path.encode(), qtype, _ptr(p),
-                                                  p.size, max_tokens, _ptr(ids),
-                                                  C.byref(n)))
+                                                  p.size, max_tokens, temperature, top_p,
+                                                  seed, _ptr(ids), C.byref(n)))
+        return ids[:n.value]
+
+    def llama2c_inspect(self, path: str, qtype: int):
+        """(config[9], tied, storage_bytes, fnv1a digest) of the reference loader."""
+        cfg = (_I64 * 9)()
+        tied = C.c_int(0)
+        nbytes = C.c_uint64(0)
+        digest = C.c_uint64(0)
+        self._check(self.lib.ref_llama2c_inspect(path.encode(), qtype, cfg, C.byref(tied),
+                                                 C.byref(nbytes), C.byref(digest)))
+        return list(cfg), bool(tied.value), nbytes.value, digest.value
+
+    def llama2c_encode(self, tokenizer_path: str, vocab: int, text: str, bos: bool = True):
+        ids = np.zeros(4 * len(text.encode()) + 8, np.int32)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_llama2c_encode(tokenizer_path.encode(), vocab, text.encode(),
+                                                int(bos), _ptr(ids), ids.size, C.byref(n)))
         return ids[:n.value]
 
 
@@ -417,3 +469,40 @@ class RefModel:
             self.r.lib.ref_model_free(self.h)
         except Exception:
             pass
+
+
+# ------------------------------------------------------------- llama2.c
+
+
+def read_llama2c(path: str) -> dict:
+    """The fp32 tensors of a llama2.c checkpoint, sectioned as the
+    reference's parse_layout does (src/llama2.cpp:199-298): header of seven
+    int32, then embeddings, attention norms, wq, wk, wv, wo, ffn norms, w1,
+    w2, w3, final norm, RoPE tables (skipped), classifier if vocab < 0.
+    eos is token 1.  Raises ValueError if the size does not match."""
+    raw = np.fromfile(path, dtype=np.uint8)
+    head = raw[:28].view(np.int32)
+    dim, ffn, layers, heads, kv, vocab_s, max_seq = (int(v) for v in head)
+    vocab = abs(vocab_s)
+    hd = dim // heads
+    kvd = kv * hd
+    f = raw[28:].view(np.float32)
+    sizes = [("embeddings", (vocab, dim)), ("attention_norm", (layers, dim)),
+             ("wq", (layers, dim, dim)), ("wk", (layers, kvd, dim)),
+             ("wv", (layers, kvd, dim)), ("wo", (layers, dim, dim)),
+             ("ffn_norm", (layers, dim)), ("w1", (layers, ffn, dim)),
+             ("w2", (layers, dim, ffn)), ("w3", (layers, ffn, dim)),
+             ("final_norm", (dim,)), ("rope", (max_seq, hd))]
+    if vocab_s < 0:
+        sizes.append(("classifier", (vocab, dim)))
+    out, at = {}, 0
+    for name, shape in sizes:
+        n = int(np.prod(shape))
+        out[name] = f[at:at + n].reshape(shape)
+        at += n
+    if at != f.size:
+        raise ValueError("llama2 checkpoint: size does not match configuration")
+    out["config"] = dict(layers=layers, heads=heads, dim=dim, head_dim=hd, ffn_dim=ffn,
+                         vocab_size=vocab, max_seq=max_seq, eos_token=1, kv_heads=kv)
+    out["tied"] = vocab_s > 0
+    return out

@@ -525,3 +525,156 @@ int orc_generate(const orc_model *m, orc_kv *kv, const int *prompt,
     free(hidden), free(row);
     return status;
 }
+
+/* ---- Sampling ----------------------------------------------------------
+ *
+ * The reference draws with std::mt19937 and
+ * std::uniform_real_distribution<double>, so the checker restates both:
+ *   MT19937 — Matsumoto & Nishimura, "Mersenne Twister: a 623-dimensionally
+ *   equidistributed uniform pseudo-random number generator", ACM TOMACS 8(1),
+ *   1998 (the 32-bit generator with the 1812433253 seeding recurrence that
+ *   C++11 [rand.eng.mers] specifies for mt19937);
+ *   uniform_real_distribution<double>(a, b) in GNU libstdc++ (the library
+ *   the reference is built against): generate_canonical<double, 53> takes
+ *   two 32-bit draws g1, g2 and returns (g1 + g2 * 2^32) / 2^64, replaced by
+ *   the largest double below 1 if it rounds up to 1; the draw is then
+ *   canonical * (b - a) + a. */
+
+typedef struct {
+    uint32_t mt[624];
+    int next;
+} orc_mt19937;
+
+static void mt_seed(orc_mt19937 *g, uint32_t seed) {
+    g->mt[0] = seed;
+    for (uint32_t i = 1; i < 624; i++)
+        g->mt[i] = 1812433253u * (g->mt[i - 1] ^ (g->mt[i - 1] >> 30)) + i;
+    g->next = 624;
+}
+
+static uint32_t mt_draw(orc_mt19937 *g) {
+    if (g->next >= 624) {
+        for (int i = 0; i < 624; i++) {
+            const uint32_t y = (g->mt[i] & 0x80000000u) | (g->mt[(i + 1) % 624] & 0x7fffffffu);
+            g->mt[i] = g->mt[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+        }
+        g->next = 0;
+    }
+    uint32_t y = g->mt[g->next++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+}
+
+static double uniform_double(orc_mt19937 *g, double lo, double hi) {
+    double sum = (double)mt_draw(g);
+    sum += (double)mt_draw(g) * 4294967296.0;
+    double canonical = sum / 18446744073709551616.0;
+    if (canonical >= 1.0)
+        canonical = nextafter(1.0, 0.0);
+    return canonical * (hi - lo) + lo;
+}
+
+/* Probability order: larger weight first, lower token id on ties. */
+static const float *g_sort_weights;
+static int by_weight(const void *a, const void *b) {
+    const int64_t i = *(const int64_t *)a, j = *(const int64_t *)b;
+    const float wi = g_sort_weights[i], wj = g_sort_weights[j];
+    if (wi != wj)
+        return wi > wj ? -1 : 1;
+    return i < j ? -1 : (i > j);
+}
+
+/* choose_token (src/generate.cpp:25-73). */
+static int choose_one(const float *logits, int64_t vocab, float temperature, float top_p,
+                      orc_mt19937 *g, float *weight, int64_t *order, int64_t *token) {
+    if (vocab <= 0)
+        return fail(ORC_INVALID_ARGUMENT, "sampling: empty logits");
+    const int64_t best = orc_argmax(logits, vocab);
+    if (temperature <= 0.0f) {
+        *token = best;
+        return ORC_OK;
+    }
+    if (!isfinite(temperature) || top_p <= 0.0f || top_p > 1.0f)
+        return fail(ORC_INVALID_ARGUMENT, "sampling: invalid temperature or top-p");
+    const float peak = logits[best];
+    double total = 0.0;
+    for (int64_t t = 0; t < vocab; t++) {
+        const float p = expf((logits[t] - peak) / temperature);
+        if (!isfinite(p))
+            return fail(ORC_RUNTIME, "sampling: non-finite probability");
+        weight[t] = p;
+        order[t] = t;
+        total += p;
+    }
+    if (!(total > 0.0))
+        return fail(ORC_RUNTIME, "sampling: zero probability mass");
+    g_sort_weights = weight;
+    qsort(order, (size_t)vocab, sizeof(int64_t), by_weight);
+    const double cutoff = (double)top_p * total;
+    double nucleus = 0.0;
+    int64_t count = 0;
+    do {
+        nucleus += weight[order[count]];
+        count++;
+    } while (count < vocab && nucleus < cutoff);
+    const double target = uniform_double(g, 0.0, nucleus);
+    double cumulative = 0.0;
+    for (int64_t k = 0; k < count; k++) {
+        cumulative += weight[order[k]];
+        if (target <= cumulative) {
+            *token = order[k];
+            return ORC_OK;
+        }
+    }
+    *token = order[count - 1];
+    return ORC_OK;
+}
+
+int orc_choose_tokens(const float *logits, int64_t steps, int64_t vocab,
+                      float temperature, float top_p, uint32_t seed,
+                      int64_t *tokens) {
+    orc_mt19937 g;
+    mt_seed(&g, seed);
+    float *weight = malloc(sizeof(float) * (size_t)(vocab > 0 ? vocab : 1));
+    int64_t *order = malloc(sizeof(int64_t) * (size_t)(vocab > 0 ? vocab : 1));
+    int status = (weight && order) ? ORC_OK : fail(ORC_RUNTIME, "oracle: out of memory");
+    for (int64_t s = 0; s < steps && status == ORC_OK; s++)
+        status = choose_one(logits + s * vocab, vocab, temperature, top_p, &g, weight, order,
+                            &tokens[s]);
+    free(weight), free(order);
+    return status;
+}
+
+int orc_generate_sampled(const orc_model *m, orc_kv *kv, const int *prompt,
+                         int64_t n, int64_t max_tokens, float temperature,
+                         float top_p, uint32_t seed, int *ids, int64_t *n_out) {
+    const orc_config *c = &m->config;
+    if (n <= 0 || n > c->max_seq)
+        return fail(ORC_INVALID_ARGUMENT, "generation: invalid prompt length");
+    kv->length = 0;
+    *n_out = 0;
+    float *hidden = malloc(sizeof(float) * (size_t)c->dim);
+    float *row = malloc(sizeof(float) * (size_t)c->vocab_size);
+    float *weight = malloc(sizeof(float) * (size_t)c->vocab_size);
+    int64_t *order = malloc(sizeof(int64_t) * (size_t)c->vocab_size);
+    int status = (hidden && row && weight && order) ? ORC_OK
+                                                    : fail(ORC_RUNTIME, "oracle: out of memory");
+    for (int64_t i = 0; i < n && status == ORC_OK; i++)
+        status = orc_decode_token(m, kv, prompt[i], hidden);
+    orc_mt19937 g;
+    mt_seed(&g, seed);
+    while (status == ORC_OK && *n_out < max_tokens && kv->length < c->max_seq) {
+        int64_t token = 0;
+        orc_logits(m, hidden, row, NULL);
+        status = choose_one(row, c->vocab_size, temperature, top_p, &g, weight, order, &token);
+        if (status != ORC_OK || token == c->eos_token)
+            break;
+        ids[(*n_out)++] = (int)token;
+        status = orc_decode_token(m, kv, (int)token, hidden);
+    }
+    free(hidden), free(row), free(weight), free(order);
+    return status;
+}

@@ -83,6 +83,21 @@ int orc_generate(const orc_model *model, orc_kv *kv, const int *prompt,
                  int64_t n, int64_t steps, int *ids, float *logits,
                  float *prefill_hidden);
 
+/* Token sampling of generate_tokens_cached (src/generate.cpp:25-73) with the
+ * random source the reference uses: std::mt19937 seeded with `seed`, drawn
+ * through std::uniform_real_distribution<double>.  orc_choose_tokens runs
+ * `steps` choices over rows of logits [steps][vocab] with one generator.
+ * orc_generate_sampled is the reference's quantised generate_tokens_cached
+ * loop (src/generate.cpp:174-216): prefill, then while fewer than
+ * max_tokens ids and the cache is not full: logits, choose, stop at eos,
+ * decode.  Greedy when temperature <= 0. */
+int orc_choose_tokens(const float *logits, int64_t steps, int64_t vocab,
+                      float temperature, float top_p, uint32_t seed,
+                      int64_t *tokens);
+int orc_generate_sampled(const orc_model *model, orc_kv *kv, const int *prompt,
+                         int64_t n, int64_t max_tokens, float temperature,
+                         float top_p, uint32_t seed, int *ids, int64_t *n_out);
+
 #ifdef __cplusplus
 }
 #endif

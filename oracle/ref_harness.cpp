@@ -15,6 +15,8 @@
  *     directly, without the eos stop, as the parity harness must do)
  *   matvec_threaded / matmul_threaded    src/threading.cpp:163-198
  *   load_llama2c_quantized_model         src/llama2.cpp:339-412
+ *   generate_tokens_cached (quantised)   src/generate.cpp:174-216
+ *   Llama2Tokenizer::encode              src/llama2.cpp:455-514
  *
  * Reading the private byte and scale arrays needs access to QuantizedMatrix
  * internals, so this translation unit alone compiles quant.hpp with private
@@ -369,17 +371,78 @@ int ref_trace(void *model, const int *prompt, size_t n, size_t steps,
 }
 
 /* The reference's own end-to-end path on a llama2.c checkpoint:
- * load_llama2c_quantized_model + generate_tokens_cached (greedy, eos stop). */
+ * load_llama2c_quantized_model + generate_tokens_cached (eos stop; greedy
+ * for temperature <= 0, else its top-p sampler with std::mt19937(seed)). */
 int ref_llama2c_generate(const char *path, int type, const int *prompt,
-                         size_t n, size_t max_tokens, int *ids,
-                         size_t *n_out) {
+                         size_t n, size_t max_tokens, float temperature,
+                         float top_p, unsigned seed, int *ids, size_t *n_out) {
     return guarded([&] {
         QuantizedModelWeights model =
             load_llama2c_quantized_model(path, to_type(type));
         SamplingConfig sampling;
         sampling.max_tokens = max_tokens;
+        sampling.temperature = temperature;
+        sampling.top_p = top_p;
+        sampling.seed = seed;
         const std::vector<int> out = generate_tokens_cached(
             model, std::vector<int>(prompt, prompt + n), sampling);
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = out.size();
+    });
+}
+
+/* The reference loader's result, described as nut_host_llama2c_inspect
+ * describes the build's: config, tied flag, storage_bytes() and a 64-bit
+ * FNV-1a digest of embeddings; per layer data+scales of q k v o gate up
+ * down, attention norm, ffn norm; final norm; separate classifier. */
+int ref_llama2c_inspect(const char *path, int type, int64_t *config,
+                        int *tied, uint64_t *storage_bytes, uint64_t *digest) {
+    return guarded([&] {
+        const QuantizedModelWeights m =
+            load_llama2c_quantized_model(path, to_type(type));
+        const ModelConfig &c = m.config;
+        const size_t v[9] = {c.layers,     c.heads,   c.dim,
+                             c.head_dim,   c.ffn_dim, c.vocab_size,
+                             c.max_seq,    c.eos_token, c.kv_heads};
+        for (int i = 0; i < 9; i++)
+            config[i] = int64_t(v[i]);
+        *tied = m.tied_embeddings ? 1 : 0;
+        *storage_bytes = m.storage_bytes();
+        uint64_t h = 0xcbf29ce484222325ull;
+        auto add = [&h](const void *p, size_t bytes) {
+            const unsigned char *b = static_cast<const unsigned char *>(p);
+            for (size_t i = 0; i < bytes; i++) {
+                h ^= b[i];
+                h *= 0x100000001b3ull;
+            }
+        };
+        add(m.embeddings.data(), m.embeddings.size() * 4);
+        for (const QuantizedLayerWeights &l : m.layers) {
+            for (const QuantizedMatrix *q : {&l.query, &l.key, &l.value,
+                                             &l.output, &l.gate, &l.up,
+                                             &l.down}) {
+                add(q->data_.data(), q->data_.size());
+                add(q->scales_.data(), q->scales_.size() * 2);
+            }
+            add(l.attention_norm.data(), l.attention_norm.size() * 4);
+            add(l.ffn_norm.data(), l.ffn_norm.size() * 4);
+        }
+        add(m.final_norm.data(), m.final_norm.size() * 4);
+        if (!m.tied_embeddings)
+            add(m.lm_head.data(), m.lm_head.size() * 4);
+        *digest = h;
+    });
+}
+
+/* Llama2Tokenizer::load(path, vocab).encode(text, bos, false). */
+int ref_llama2c_encode(const char *tokenizer_path, size_t vocab,
+                       const char *text, int bos, int *ids, size_t capacity,
+                       size_t *n_out) {
+    return guarded([&] {
+        const Llama2Tokenizer tok = Llama2Tokenizer::load(tokenizer_path, vocab);
+        const std::vector<int> out = tok.encode(text, bos != 0, false);
+        if (out.size() > capacity)
+            throw std::length_error("ref harness: encode capacity");
         std::copy(out.begin(), out.end(), ids);
         *n_out = out.size();
     });

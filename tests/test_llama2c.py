@@ -1,0 +1,229 @@
+"""llama2.c checkpoints end to end: the host loader (load_llama2c_quantized_model,
+reference src/llama2.cpp:199-412), the generation sampler (choose_token,
+src/generate.cpp:25-73) and generate_tokens_cached (src/generate.cpp:174-216)
+through the C++ host API.
+
+Checkpoints are rebuilt from seeds by tests/golden/make_llama2c_fixture.py;
+the goldens in tests/golden/llama2c_golden.npz were produced by the
+unmodified reference from the same bytes.  CPU tests pin the oracle's
+restatement and the host loader/sampler; GPU tests run the product path.
+"""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+import nutllm_b200 as nb
+import oracle
+from tests.conftest import golden_path
+from tests.golden import make_llama2c_fixture as fx
+
+G = np.load(golden_path("llama2c_golden.npz"))
+QTYPES = ((0, "int8"), (1, "int4"))
+REF_FIXTURES = os.path.join(os.environ.get("NUTLLM_REFERENCE", "/root/reference"),
+                            "tests", "fixtures")
+
+
+@pytest.fixture(scope="module")
+def checkpoints(tmp_path_factory):
+    d = tmp_path_factory.mktemp("llama2c")
+    return {name: fx.write_checkpoint(str(d / f"{name}.bin"), name) for name in fx.CONFIGS}
+
+
+def _oracle_model(orc, path, qtype):
+    """A host image of the checkpoint quantised by the oracle's quantiser."""
+    t = oracle.read_llama2c(path)
+    c = nb.Config(**t["config"])
+
+    def q(w):
+        data, scales = orc.quantize(w, qtype)
+        return nb.QuantizedMatrix(data, scales, w.shape[0], w.shape[1], qtype)
+
+    layers = []
+    for l in range(c.layers):
+        layers.append(nb.LayerWeights(
+            q(t["wq"][l]), q(t["wk"][l]), q(t["wv"][l]), q(t["wo"][l]), q(t["w1"][l]),
+            q(t["w3"][l]), q(t["w2"][l]),
+            attention_norm=np.ascontiguousarray(t["attention_norm"][l]),
+            ffn_norm=np.ascontiguousarray(t["ffn_norm"][l])))
+    return nb.ModelWeights(
+        config=c, qtype=qtype, embeddings=np.ascontiguousarray(t["embeddings"]),
+        layers=layers, final_norm=np.ascontiguousarray(t["final_norm"]),
+        lm_head=None if t["tied"] else np.ascontiguousarray(t["classifier"]),
+        tied_embeddings=t["tied"])
+
+
+# ------------------------------------------------------------------ CPU
+
+
+@pytest.mark.parametrize("name", list(fx.CONFIGS))
+def test_fixture_bytes_match_golden(checkpoints, name):
+    digest = hashlib.sha256(open(checkpoints[name], "rb").read()).digest()
+    assert np.array_equal(np.frombuffer(digest, np.uint8), G[f"{name}/sha256"])
+
+
+@pytest.mark.parametrize("qtype,qname", QTYPES)
+@pytest.mark.parametrize("name", list(fx.CONFIGS))
+def test_host_loader_matches_reference_bytes(checkpoints, name, qtype, qname):
+    """Config, tied flag, storage_bytes() and every loaded byte (quantised
+    data, fp16 scales, fp32 norms/embeddings/classifier) equal the reference
+    loader's."""
+    cfg, tied, nbytes, digest = nb.llama2c_inspect(checkpoints[name], qtype)
+    key = f"{name}/{qname}"
+    assert cfg == G[f"{key}/config"].tolist()
+    assert tied == bool(G[f"{key}/tied"])
+    assert nbytes == int(G[f"{key}/storage_bytes"])
+    assert digest == int(G[f"{key}/digest"])
+
+
+@pytest.mark.parametrize("qtype,qname", QTYPES)
+@pytest.mark.parametrize("name", list(fx.CONFIGS))
+def test_oracle_generation_matches_reference(orc, checkpoints, name, qtype, qname):
+    """The oracle's generate_tokens_cached (eos stop, context limit, greedy
+    and seeded top-p) gives the reference's ids on the reference's bytes."""
+    m = orc.model(_oracle_model(orc, checkpoints[name], qtype))
+    c = fx.config_of(name)
+    prompt = G[f"{name}/prompt"]
+    key = f"{name}/{qname}"
+    assert m.generate_cached(prompt, c["max_tokens"]).tolist() == G[f"{key}/greedy"].tolist()
+    assert (m.generate_cached(prompt, c["max_tokens"], **fx.SAMPLING).tolist()
+            == G[f"{key}/sampled"].tolist())
+
+
+def _logit_rows(seed):
+    rng = np.random.default_rng(seed)
+    rows = [rng.standard_normal(300).astype(np.float32) * 3,
+            np.zeros(17, np.float32),                                   # all ties
+            np.repeat(rng.standard_normal(8), 5).astype(np.float32),    # tied pairs
+            np.array([5.0], np.float32),
+            (rng.standard_normal(2000) * 0.01).astype(np.float32)]
+    return rows
+
+
+@pytest.mark.parametrize("temperature,top_p", [(0.0, 1.0), (0.7, 0.9), (1.0, 1.0),
+                                               (2.5, 0.5), (0.3, 1e-6), (1.3, 0.999)])
+def test_sampler_matches_oracle(orc, temperature, top_p):
+    for seed in (1, 7, 4242):
+        for i, row in enumerate(_logit_rows(seed)):
+            steps = np.tile(row, (6, 1))  # six draws from one generator
+            want = orc.choose_tokens(steps, temperature, top_p, seed + i)
+            got = nb.choose_tokens(steps, temperature, top_p, seed + i)
+            assert got.tolist() == want.tolist(), (seed, i)
+
+
+@pytest.mark.parametrize("temperature,top_p", [(0.5, 0.0), (0.5, 1.5), (float("inf"), 0.9),
+                                               (float("nan"), 0.9)])
+def test_sampler_rejects_bad_settings(temperature, top_p):
+    with pytest.raises(ValueError, match="sampling: invalid temperature or top-p"):
+        nb.choose_tokens(np.zeros((1, 4), np.float32), temperature, top_p, 1)
+
+
+def _write_header(path, header, floats=0):
+    with open(path, "wb") as f:
+        f.write(np.array(header, np.int32).tobytes())
+        f.write(np.zeros(floats, np.float32).tobytes())
+    return str(path)
+
+
+@pytest.mark.parametrize("header,floats,error,message", [
+    ([4, 4], 0, RuntimeError, "llama2 checkpoint: truncated header"),
+    ([0, 4, 1, 1, 1, 6, 8], 0, RuntimeError, "llama2 checkpoint: invalid dimension"),
+    ([4, 4, 1, 1, 1, 0, 8], 0, RuntimeError, "llama2 checkpoint: invalid vocabulary"),
+    ([6, 4, 1, 4, 4, 6, 8], 0, RuntimeError, "heads do not divide dimension"),
+    ([4, 4, 1, 1, 1, 6, 8], 10, RuntimeError, "size does not match configuration"),
+    ([4, 4, 1, 1, 2, 6, 8], 0, ValueError, "model config: invalid dimensions"),
+])
+def test_loader_errors_match_reference(tmp_path, header, floats, error, message):
+    path = _write_header(tmp_path / "bad.bin", header, floats)
+    with pytest.raises(error, match=message):
+        nb.llama2c_inspect(path, 1)
+    if oracle.reference_available():
+        with pytest.raises(RuntimeError, match=message):
+            oracle.Reference().llama2c_inspect(path, 1)
+
+
+def test_loader_missing_file(tmp_path):
+    with pytest.raises(RuntimeError, match="llama2 checkpoint: cannot open"):
+        nb.llama2c_inspect(str(tmp_path / "absent.bin"), 0)
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_FIXTURES) or not oracle.reference_available(),
+                    reason="reference fixtures are only present where the reference is")
+@pytest.mark.parametrize("fname", ["tiny-llama2.bin", "tiny-llama2-shared.bin"])
+@pytest.mark.parametrize("qtype,qname", QTYPES)
+def test_reference_fixtures(orc, ref, fname, qtype, qname):
+    """The reference's own llama2.c fixtures: the host loader reads the same
+    bytes as the reference loader, and the oracle reproduces the reference's
+    known answer (greedy ids {4, 5} after the prompt "H", both quantisations,
+    src/loader_selftest.cpp:96-116)."""
+    path = os.path.join(REF_FIXTURES, fname)
+    assert nb.llama2c_inspect(path, qtype) == ref.llama2c_inspect(path, qtype)
+    if fname == "tiny-llama2.bin":
+        prompt = ref.llama2c_encode(os.path.join(REF_FIXTURES, "tiny-llama2.tokenizer"),
+                                    6, "H")
+        want = ref.llama2c_generate(path, qtype, prompt, 32)
+        assert want.tolist() == [4, 5]
+        m = orc.model(_oracle_model(orc, path, qtype))
+        assert m.generate_cached(prompt, 32).tolist() == [4, 5]
+
+
+# ------------------------------------------------------------------ GPU
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype,qname", QTYPES)
+@pytest.mark.parametrize("name", list(fx.CONFIGS))
+def test_llama2c_generation_matches_reference(gpu, checkpoints, name, qtype, qname):
+    """Loader + generate_tokens_cached through the C++ host API on the
+    device: greedy and seeded top-p ids equal the reference's."""
+    c = fx.config_of(name)
+    prompt = G[f"{name}/prompt"]
+    key = f"{name}/{qname}"
+    ids, st = nb.llama2c_generate(checkpoints[name], qtype, prompt, c["max_tokens"])
+    assert ids.tolist() == G[f"{key}/greedy"].tolist()
+    assert st.prefill_tokens == len(prompt) and st.generated_tokens == len(ids)
+    ids, st = nb.llama2c_generate(checkpoints[name], qtype, prompt, c["max_tokens"],
+                                  **fx.SAMPLING)
+    assert ids.tolist() == G[f"{key}/sampled"].tolist()
+    assert st.generated_tokens == len(ids)
+
+
+@pytest.mark.gpu
+def test_llama2c_generation_errors(gpu, checkpoints):
+    path = checkpoints["gqa_separate"]
+    with pytest.raises(ValueError, match="generation: invalid prompt length"):
+        nb.llama2c_generate(path, 1, np.zeros(0, np.int32), 4)
+    with pytest.raises(ValueError, match="generation: invalid prompt length"):
+        nb.llama2c_generate(path, 1, np.full(49, 2, np.int32), 4)
+    with pytest.raises(IndexError, match="token out of range"):
+        nb.llama2c_generate(path, 1, np.array([2, 300], np.int32), 4)
+    with pytest.raises(ValueError, match="sampling: invalid temperature or top-p"):
+        nb.llama2c_generate(path, 1, np.array([2, 3], np.int32), 4, temperature=0.5,
+                            top_p=0.0)
+    ids, _ = nb.llama2c_generate(path, 1, np.array([2, 3], np.int32), 0)
+    assert ids.size == 0
+
+
+SELFTEST = os.path.join(os.path.dirname(nb.HOST_LIB), "..", "bin", "nutllm_selftest")
+
+
+def test_host_selftest_binary_built():
+    import subprocess
+    r = subprocess.run([SELFTEST], capture_output=True, text=True)
+    assert r.returncode == 2 and "usage" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qname", ["int8", "int4"])
+@pytest.mark.parametrize("name", list(fx.CONFIGS))
+def test_host_api_selftest(gpu, checkpoints, name, qname):
+    """The C++ API a reference caller uses (KVCache, prefill_quantized,
+    decode_quantized_token, generate_tokens_cached, loader) and its
+    exception classes, exercised by nutllm_selftest on the device."""
+    import subprocess
+    prompt = [str(int(t)) for t in G[f"{name}/prompt"]]
+    r = subprocess.run([SELFTEST, checkpoints[name], qname, *prompt], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "FAIL" not in r.stdout and "all host API checks passed" in r.stdout
