@@ -8,6 +8,7 @@
  * It exercises the calls a reference caller makes — KVCache,
  * load_llama2c_quantized_model, prefill_quantized, decode_quantized_token,
  * generate_tokens_cached — and the exception classes of their failures. */
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -119,12 +120,20 @@ int main(int argc, char **argv) {
                    stats.generated_tokens == generated.size() && stats.decode_seconds >= 0.0,
                "generate_tokens_cached: same ids as prefill + decode_quantized_token");
 
-        /* the same prompt again from a reset cache gives the same state */
+        /* the same prompt again from a reset cache gives the same state, up
+         * to the order of the split-K float reductions (device atomics) */
         KVCache again(c);
         const std::vector<float> h1 = prefill_quantized(model, prompt, again, 1);
         const std::vector<float> h2 = prefill_quantized(model, prompt, again, 1);
-        report(h1 == h2 && again.length() == prompt.size(),
-               "prefill_quantized: resets the cache and repeats bit-exactly");
+        bool close = h1.size() == h2.size();
+        float worst = 0.0f;
+        for (size_t i = 0; close && i < h1.size(); i++) {
+            worst = std::max(worst, std::fabs(h1[i] - h2[i]));
+            close = std::fabs(h1[i] - h2[i]) <= 1e-4f + 1e-4f * std::fabs(h1[i]);
+        }
+        report(close && again.length() == prompt.size(),
+               "prefill_quantized: resets the cache and repeats (max |diff| " +
+                   std::to_string(worst) + ")");
 
         /* key / value / store / set_length */
         const size_t kvh = c.effective_kv_heads(), hd = c.head_dim;
