@@ -297,7 +297,10 @@ __device__ __forceinline__ void red_add4(float *dst, float4 v) {
 /* Collective end of a contributor's share of accumulator step `step`:
  * adds yacc[0, nrows) into rows row0.. of the step's slot, zeroes this
  * contributor's share (index `me` of `count`) of the next step's slot, and
- * counts itself in once every thread's stores are fenced. */
+ * counts itself in.  The grid-barrier pattern: the CTA barrier orders every
+ * thread's red.add and stores before thread 0's gpu-scope fence, which is
+ * cumulative, so one fence ahead of the counter increment publishes them
+ * all to any reader that acquires the counter. */
 __device__ void finish_step(const Shared &s, const MkParams &p, int step, int row0, int nrows,
                             int me, int count) {
     cbar();
@@ -310,10 +313,11 @@ __device__ void finish_step(const Shared &s, const MkParams &p, int step, int ro
     float4 *next = reinterpret_cast<float4 *>(slot_of(p, step + 1));
     for (int k = z0 + int(threadIdx.x); k < z1; k += NT)
         next[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    __threadfence();
     cbar();
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
+        __threadfence();
         atomicAdd(p.cnt + step % kAccSlots, 1u);
+    }
 }
 
 /* Norm weights of this thread's elements (k = tid + j NT), loaded before
@@ -491,10 +495,12 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor 
     const uint32_t tag = qkv_tag(p, i, l);
     const int lane = threadIdx.x & 31;
     const float *cs = rope_cs, *sn = rope_sn;
-    /* The cache rows of this token are read only by later tokens: the
-     * fence ahead of each token's key/value tags orders the rows written
-     * by the same lane one token earlier, and the readers acquire those
-     * tags (load, then fence) before fetching history. */
+    /* The cache rows of this token are read only by later tokens.  Each
+     * lane that stored key/value rows fences once its tags are out (after
+     * the run, off the path the attention waits on), which orders those
+     * rows before the same lane's tags of the next token; the readers
+     * acquire those tags (load, then fence) before fetching history. */
+    bool wrote_kv = false;
     float nsc = -1.0f; /* the rmsnorm scale, computed at the first epilogue */
     auto epi = [&](int rt, float y) {
         if (nsc < 0.0f)
@@ -510,20 +516,22 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor 
             const int kr = row - p.dim, h = kr / p.hd, d = kr % p.hd;
             const float out = rope(y, lane, cs[d >> 1], sn[d >> 1]);
             if (lane < 16) {
-                __threadfence();
                 st_relaxed(p.qkv + row, out, tag);
                 p.kcache[((size_t(l) * p.kv_heads + h) * p.max_seq + pos) * p.hd + d] = out;
+                wrote_kv = true;
             }
         } else if (lane < 16) {                   /* value */
             const int vr = row - p.dim - p.kvd, h = vr / p.hd, d = vr % p.hd;
-            __threadfence();
             st_relaxed(p.qkv + row, y, tag);
             p.vcache[((size_t(l) * p.kv_heads + h) * p.max_seq + pos) * p.hd + d] = y;
+            wrote_kv = true;
         }
     };
     const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
                                                  threadIdx.x >> 5, kBar, epi,
                                                  tr.wait_acc());
+    if (wrote_kv)
+        __threadfence();
     tr.mark(5);
     tr.put_wait();
     return healthy(s) && ok;
