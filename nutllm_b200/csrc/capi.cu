@@ -554,8 +554,11 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
     p.cpp = std::max(1, std::min(m->sms / p.wo_pairs, p.rt_wo));
     p.count_aw = p.wo_pairs * p.cpp;
     p.nbf = int(c.ffn_dim / 32);
-    p.count_gd = std::min(p.nbf, m->sms);
+    p.count_gd = m->sms;
     p.rt_down_pairs = int(L0.down.shape.row_tiles / 2);
+    p.gd_unit = nut::ffn_units_per_block(p.rt_down_pairs);
+    p.gd_total = p.nbf * p.gd_unit;
+    p.act = kv->tagged + dim + 2 * kvd;
     p.prompt = kv->mk_prompt;
     p.n_prompt = int(n_prompt);
     p.n_tokens = int(n_tokens);
@@ -1114,7 +1117,7 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
         for (auto &e : kv->ev)
             cuda_check(cudaEventCreate(&e), "create event");
         if (model->mk) {
-            kv->tagged_count = size_t(c.dim) + 2 * kvd;
+            kv->tagged_count = size_t(c.dim) + 2 * kvd + size_t(c.ffn_dim);
             kv->mk_acc = dev_alloc<float>(size_t(nut::kAccSlots) * c.dim, "alloc accumulators");
             kv->mk_cnt = dev_alloc<unsigned int>(nut::kAccSlots, "alloc step counters");
             kv->tagged = dev_alloc<nut::Tagged>(kv->tagged_count, "alloc tagged");

@@ -768,20 +768,59 @@ __device__ bool phase_attwo(const Shared &s, const MkParams &p, Trace &tr, Curso
     return healthy(s) && ok;
 }
 
-/* GUDOWN (hB = hA + Wdown silu(gate) * up), split by FFN block: CTA
- * c < count_gd owns blocks [j0, j1) (32 hidden units each): the gate and up
- * rows of those units (row tiles 4 j0 .. 4 j1 of the interleaved matrix),
- * SwiGLU into shared memory (src/quant_model.cpp:197-198), then columns
- * 32 j0 .. 32 j1 of Wdown, plus its share of the residual rows, added into
- * step 2 (i L + l) + 1. */
+/* The FFN step's work, split evenly over the CTAs.  Each 32-unit block b
+ * is U = gd_unit work units: its 4 gate/up row tiles 4 b .. 4 b + 3 (row
+ * tiles of the interleaved matrix, 8 units each), then its Wdown column
+ * block in units of kDownUnitPairs row-tile pairs.  CTA c takes the
+ * contiguous unit range [u0, u1) of the nbf U units.  A block's Wdown
+ * units need all 32 SwiGLU outputs of the block, so gate/up tiles whose
+ * block's Wdown is (partly) owned by a later CTA are "exported": computed
+ * first and published as tagged values; only the first Wdown block of a
+ * range can "import" tiles computed by earlier CTAs. */
+struct GdPlan {
+    int gu_lo, gu_hi; /* gate/up row tiles [gu_lo, gu_hi) */
+    int ex_lo;        /* exported tiles [ex_lo, gu_hi) (run first) */
+    int d_lo, d_hi;   /* Wdown units [d_lo, d_hi) (block d / du, part d % du) */
+    int du;           /* Wdown units per block */
+    int db_lo, nd;    /* Wdown blocks db_lo .. db_lo + nd - 1 (digit slots) */
+};
+
+__device__ __forceinline__ GdPlan gd_plan(const MkParams &p, int c) {
+    const int U = p.gd_unit, du = U - 4;
+    int u0, u1;
+    share_of(p.gd_total, c, int(gridDim.x), u0, u1);
+    GdPlan g;
+    g.du = du;
+    /* gate/up tiles and Wdown units among units [0, u) */
+    auto gu_before = [&](int u) { return 4 * (u / U) + min(u % U, 4); };
+    auto d_before = [&](int u) { return du * (u / U) + max(u % U - 4, 0); };
+    g.gu_lo = gu_before(u0);
+    g.gu_hi = gu_before(u1);
+    g.d_lo = d_before(u0);
+    g.d_hi = d_before(u1);
+    g.ex_lo = g.gu_hi;
+    if (g.gu_hi > g.gu_lo) {
+        const int bl = (g.gu_hi - 1) / 4; /* block of the last gate/up tile */
+        if ((bl + 1) * du > g.d_hi)
+            g.ex_lo = max(g.gu_lo, 4 * bl);
+    }
+    g.db_lo = g.d_lo / du;
+    g.nd = g.d_hi > g.d_lo ? (g.d_hi - 1) / du - g.db_lo + 1 : 0;
+    return g;
+}
+
+/* GUDOWN (hB = hA + Wdown silu(gate) * up) over this CTA's work units: the
+ * exported gate/up tiles, the other gate/up tiles, SwiGLU
+ * (src/quant_model.cpp:197-198) into shared memory (and, for exported
+ * tiles, into the tagged act vector), then its Wdown units, plus its share
+ * of the residual rows, added into step 2 (i L + l) + 1. */
 template <int TYPE, int STAGES>
 __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                              RowReduce &rr, int i, int l) {
     const int c = blockIdx.x;
     if (c >= p.count_gd)
         return true;
-    int j0, j1;
-    share_of(p.nbf, c, p.count_gd, j0, j1);
+    const GdPlan g = gd_plan(p, c);
     const int st = step_of(p, i, l, 1);
     if (!wait_step(s, p, st - 1))
         return false;
@@ -795,8 +834,9 @@ __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Curs
         const int r = r0 * 16 + int(threadIdx.x) + j * NT;
         resv[j] = r < r1 * 16 ? __ldcg(hA + r) : 0.0f;
     }
-    float ss;
-    warp_slice<TYPE>(s, hA, p.dim, p.nb_dim, p.ffn_norm + size_t(l) * p.dim, ss);
+    float ss = 0.0f;
+    if (g.gu_hi > g.gu_lo)
+        warp_slice<TYPE>(s, hA, p.dim, p.nb_dim, p.ffn_norm + size_t(l) * p.dim, ss);
     slice_ss(s, ss);
     for (int r = threadIdx.x; r < p.dim + 32; r += NT)
         s.yacc[r] = 0.0f;
@@ -812,34 +852,72 @@ __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Curs
     tr.mark(2);
     constexpr int TB = TileGeom<TYPE>::kTileBytes;
     const MkLayerPtrs &L = p.layer[l];
-    const int a = 4 * j0, b = 4 * j1;
-    const TileRun run{L.gu + size_t(a) * p.nb_dim * TB, L.gu_s + size_t(a) * p.nb_dim * 16,
-                      (b - a) * p.nb_dim, p.nb_dim};
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    /* tile rt: lanes 0-7 gate rows, lanes 8-15 up rows of units 8 rt .. 8 rt + 7
-     * of the owned blocks */
+    const uint32_t tag = qkv_tag(p, i, l);
+    /* tile t: lanes 0-7 gate rows, lanes 8-15 up rows of units 8 t .. 8 t + 7 */
     float nsc = -1.0f; /* the rmsnorm scale, computed at the first epilogue */
+    int t_first = 0;   /* first tile of the run being consumed */
     auto epi = [&](int rt, float y) {
         if (nsc < 0.0f)
             nsc = norm_scale(s, p.dim);
         y *= nsc;
         const float up = __shfl_down_sync(0xffffffffu, y, 8);
-        if (lane < 8)
-            s.actv[rt * 8 + lane] = y / (1.0f + expf(-y)) * up;
+        const int t = t_first + rt, b = t >> 2, unit = 8 * (t & 3) + lane;
+        if (lane < 8) {
+            const float a = y / (1.0f + expf(-y)) * up;
+            if (b >= g.db_lo && b < g.db_lo + g.nd)
+                s.actv[(b - g.db_lo) * 32 + unit] = a;
+            if (t >= g.ex_lo)
+                st_relaxed(p.act + 32 * b + unit, a, tag);
+        }
     };
-    bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr, w, kBar, epi,
-                                           tr.wait_acc());
-    cbar(); /* every SwiGLU output written; the GU digits are free */
-    const int nblk = j1 - j0;
-    for (int k = w; k < nblk; k += W)
-        digit_block(s.actv, nblk * 32, k, s.dig, s.fac, TYPE == 1 ? 1.0f / 16.0f : 1.0f);
-    cbar();
+    bool ok = true;
+    if (g.gu_hi > g.ex_lo) {
+        t_first = g.ex_lo;
+        const TileRun ex{L.gu + size_t(g.ex_lo) * p.nb_dim * TB,
+                         L.gu_s + size_t(g.ex_lo) * p.nb_dim * 16,
+                         (g.gu_hi - g.ex_lo) * p.nb_dim, p.nb_dim};
+        ok = consume_run<TYPE, W, STAGES>(s.ring, ex, cur, s.dig, s.fac, rr, w, kBar, epi,
+                                          tr.wait_acc());
+    }
+    if (g.ex_lo > g.gu_lo) {
+        t_first = g.gu_lo;
+        const TileRun rest{L.gu + size_t(g.gu_lo) * p.nb_dim * TB,
+                           L.gu_s + size_t(g.gu_lo) * p.nb_dim * 16,
+                           (g.ex_lo - g.gu_lo) * p.nb_dim, p.nb_dim};
+        ok = consume_run<TYPE, W, STAGES>(s.ring, rest, cur, s.dig, s.fac, rr, w, kBar, epi,
+                                          tr.wait_acc()) &&
+             ok;
+    }
+    cbar(); /* every SwiGLU output written; the gate/up digits are free */
+    if (w < g.nd) {
+        /* digits of Wdown block db_lo + w; tiles before gu_lo come from
+         * earlier CTAs through the tagged vector */
+        const int b = g.db_lo + w, t = 4 * b + (lane >> 3);
+        float v = 0.0f;
+        if (t < g.gu_lo) {
+            if (!wait_tag<false>(p.act + 32 * b + lane, tag, p.limit_ns, v))
+                fatal(s, p, kErrTimeoutInput);
+        } else {
+            v = s.actv[w * 32 + lane];
+        }
+        digit_from(v, __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))), w, s.dig,
+                   s.fac, TYPE == 1 ? 1.0f / 16.0f : 1.0f);
+    }
+    if (!healthy(s))
+        return false;
     tr.mark(4);
-    const size_t t0 = size_t(j0) * size_t(2 * p.rt_down_pairs);
-    const TileRun down{L.down + t0 * TB, L.down_s + t0 * 16, nblk * 2 * p.rt_down_pairs, 1};
-    ok = consume_cols<TYPE, W, STAGES, false>(s.ring, down, cur, s.dig, s.fac,
-                                              p.rt_down_pairs, s.yacc, w, tr.wait_acc()) &&
-         ok;
+    for (int d = g.d_lo; d < g.d_hi; d++) {
+        const int b = d / g.du, part = d - b * g.du, slot = b - g.db_lo;
+        const int q0 = part * kDownUnitPairs;
+        const int np = min(kDownUnitPairs, p.rt_down_pairs - q0);
+        const size_t t0 = size_t(b) * size_t(2 * p.rt_down_pairs) + size_t(2 * q0);
+        const TileRun down{L.down + t0 * TB, L.down_s + t0 * 16, 2 * np, 1};
+        ok = consume_cols<TYPE, W, STAGES, false>(s.ring, down, cur, s.dig + slot * 128,
+                                                  s.fac + 2 * slot, np, s.yacc + 32 * q0, w,
+                                                  tr.wait_acc()) &&
+             ok;
+    }
     tr.mark(5);
     tr.put_wait();
     finish_step(s, p, st, 0, p.dim, c, p.count_gd);
@@ -980,18 +1058,29 @@ __device__ void producer(const Shared &s, const MkParams &p) {
                     return;
             }
             if (c < p.count_gd) {
-                int j0, j1;
-                share_of(p.nbf, c, p.count_gd, j0, j1);
-                if (!produce_run_c<TYPE, STAGES>(s.ring,
-                        TileRun{L.gu + size_t(4 * j0) * p.nb_dim * TB,
-                                L.gu_s + size_t(4 * j0) * p.nb_dim * 16,
-                                4 * (j1 - j0) * p.nb_dim, p.nb_dim}, cur))
+                /* the consumer's order: exported gate/up tiles, the other
+                 * gate/up tiles, then the Wdown units */
+                const GdPlan g = gd_plan(p, c);
+                if (g.gu_hi > g.ex_lo &&
+                    !produce_run_c<TYPE, STAGES>(s.ring,
+                        TileRun{L.gu + size_t(g.ex_lo) * p.nb_dim * TB,
+                                L.gu_s + size_t(g.ex_lo) * p.nb_dim * 16,
+                                (g.gu_hi - g.ex_lo) * p.nb_dim, p.nb_dim}, cur))
                     return;
-                const size_t t0 = size_t(j0) * size_t(2 * p.rt_down_pairs);
-                if (!produce_run_c<TYPE, STAGES>(s.ring,
-                        TileRun{L.down + t0 * TB, L.down_s + t0 * 16,
-                                (j1 - j0) * 2 * p.rt_down_pairs, 1}, cur))
+                if (g.ex_lo > g.gu_lo &&
+                    !produce_run_c<TYPE, STAGES>(s.ring,
+                        TileRun{L.gu + size_t(g.gu_lo) * p.nb_dim * TB,
+                                L.gu_s + size_t(g.gu_lo) * p.nb_dim * 16,
+                                (g.ex_lo - g.gu_lo) * p.nb_dim, p.nb_dim}, cur))
                     return;
+                for (int d = g.d_lo; d < g.d_hi; d++) {
+                    const int b = d / g.du, q0 = (d - b * g.du) * kDownUnitPairs;
+                    const int np = min(kDownUnitPairs, p.rt_down_pairs - q0);
+                    const size_t t0 = size_t(b) * size_t(2 * p.rt_down_pairs) + size_t(2 * q0);
+                    if (!produce_run_c<TYPE, STAGES>(s.ring,
+                            TileRun{L.down + t0 * TB, L.down_s + t0 * 16, 2 * np, 1}, cur))
+                        return;
+                }
             }
         }
         if (wants_logits(p, i)) {
@@ -1157,8 +1246,11 @@ bool mk_supported(int dim, int ffn, int kvd, int head_dim, int heads, int type,
         head_dim % 2 != 0 || head_dim > 256 || heads % (kvd / head_dim) != 0 ||
         dim < 64 + head_dim || sms <= 0)
         return false;
-    const int nbf = ffn / 32, cgd = nbf < sms ? nbf : sms;
-    if ((nbf + cgd - 1) / cgd > kMaxFfnBlocks)
+    /* the FFN step's unit ranges touch at most kMaxFfnBlocks blocks */
+    const int rt_down = (dim / 16 + 1) / 2 * 2;
+    const int U = ffn_units_per_block(rt_down / 2);
+    const int per_cta = (ffn / 32 * U + sms - 1) / sms;
+    if ((per_cta + U - 1) / U + 1 > kMaxFfnBlocks)
         return false;
     /* every Wo block pair needs its own CTA (the step counts them all) */
     if ((dim / 32 + 1) / 2 > sms)

@@ -20,8 +20,17 @@ struct MkLayer {
 
 /* Accumulator slots of the split-K reductions (a ring; see decode_mk.cu). */
 constexpr int kAccSlots = 8;
-/* Most FFN blocks (32 hidden units) one CTA may own. */
+/* Most FFN blocks (32 hidden units) whose Wdown columns one CTA may own. */
 constexpr int kMaxFfnBlocks = 4;
+/* Row-tile pairs of one Wdown work unit (a column block is split into units
+ * of this many pairs). */
+constexpr int kDownUnitPairs = 32;
+
+/* FFN work units of one 32-unit block: its 4 gate/up row tiles, then its
+ * Wdown column block in units of kDownUnitPairs row-tile pairs. */
+inline int ffn_units_per_block(int rt_down_pairs) {
+    return 4 + (rt_down_pairs + kDownUnitPairs - 1) / kDownUnitPairs;
+}
 
 /* Device-side view of a layer (pointers only). */
 struct MkLayerPtrs {
@@ -45,6 +54,8 @@ struct MkParams {
     const float *rope_cos, *rope_sin;   /* [max_seq][hd / 2] */
     float *kcache, *vcache;             /* [layers][kv_heads][max_seq][hd] */
     Tagged *qkv;                        /* tagged q | k | v of the current token */
+    Tagged *act;                        /* [ffn] tagged SwiGLU outputs that cross
+                                           CTAs */
     float *hacc;                        /* [kAccSlots][dim] residual stream
                                            accumulators (fp32, red.add) */
     float *hidden_out;                  /* [dim] last hidden vector */
@@ -53,6 +64,7 @@ struct MkParams {
     int count_aw;                       /* CTAs of the attention + Wo step */
     int nbf, count_gd;                  /* FFN blocks; CTAs of the FFN step */
     int rt_down_pairs;                  /* row-tile pairs per Wdown block */
+    int gd_unit, gd_total;              /* FFN work units per block, in all */
     const int *prompt;                  /* [n_prompt] */
     int n_prompt, n_tokens, start_pos;
     int logits_from, logits_to;         /* lm_head after tokens in [from, to] */
