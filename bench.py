@@ -279,6 +279,115 @@ def run_ours(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- 7B batched, TP
+
+LLAMA7B = dict(layers=32, heads=32, dim=4096, head_dim=128, ffn_dim=11008, vocab_size=32000,
+               max_seq=256, eos_token=1, kv_heads=32)
+TP_WORKLOADS = {
+    # batch 64, 128-token prompts, 128 greedy steps
+    "llama7b-int4-b64": dict(cfg=LLAMA7B, batch=64, prompt=128, steps=128),
+    # the same shape with 4 layers, for quick checks
+    "llama7b-int4-b64-4l": dict(cfg=dict(LLAMA7B, layers=4), batch=64, prompt=128, steps=128),
+}
+
+
+def tp_decode_bytes(cfg, batch, prompt, steps, world):
+    """Algorithmic bytes one rank reads per decode step, averaged over the
+    steps: its share of the INT4 linears (q/4 + 2 bytes per 32 weights) and
+    of the fp32 classifier, the replicated norms, and its heads' fp32 keys and
+    values for every sequence at positions 0..pos."""
+    d, f, L, V = cfg["dim"], cfg["ffn_dim"], cfg["layers"], cfg["vocab_size"]
+    kvd = cfg["kv_heads"] * cfg["head_dim"]
+    params = L * (2 * d * d + 2 * d * kvd + 3 * d * f)
+    lin = params // 2 + params // 32 * 2
+    cls = V * d * 4
+    norms = (2 * L + 1) * d * 4
+    avg_ctx = prompt + steps / 2.0
+    kv = 2 * L * batch * kvd * 4 * avg_ctx
+    return (lin + cls + kv) / world + norms
+
+
+def run_batch_tp(args, rank, world, local):
+    import torch
+    import nutllm_b200 as nb
+    spec = TP_WORKLOADS[args.workload]
+    cfg = nb.Config(**spec["cfg"])
+    B, n, steps = spec["batch"], spec["prompt"], spec["steps"]
+    torch.cuda.set_device(local)
+    nccl_id = None
+    if world > 1:
+        box = [nb.tp_unique_id() if rank == 0 else None]
+        _pg.broadcast_object_list(box, src=0)
+        nccl_id = box[0]
+    tp = nb.TPBatch(B, rank=rank, world=world, nccl_id=nccl_id, config=cfg, seed=SEED,
+                    device=local)
+    rng = np.random.default_rng(SEED)
+    prompts = rng.integers(1, cfg.vocab_size, size=(B, n)).astype(np.int32)
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
+        tp.generate(prompts, steps)
+    barrier = _barrier(world)
+    barrier()
+    torch.cuda.synchronize(local)
+    launches0 = nb.launch_count()
+    dec_s = pre_s = 0.0
+    with Clocks(local) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            _, _, st = tp.generate(prompts, steps)
+            dec_s += st.decode_seconds
+            pre_s += st.prefill_seconds
+        wall = time.perf_counter() - t0
+    launches = nb.launch_count() - launches0
+    barrier()
+    dec_s = _max_over_ranks(dec_s, world)
+    pre_s = _max_over_ranks(pre_s, world)
+    wall = _max_over_ranks(wall, world)
+    info = tp.info()
+    tp.close()
+    if rank != 0:
+        return
+    value = B * steps * args.steps / dec_s
+    step_s = dec_s / (args.steps * steps)
+    peak, src = measured_peaks()
+    per_rank = tp_decode_bytes(spec["cfg"], B, n, steps, world)
+    ach = per_rank / step_s / 1e9
+    line = {
+        "metric": f"decode tok/s (Llama-2-7B INT4 shape, batch {B}, tensor parallel)",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": warmup,
+        "ms_per_step": round(1e3 * (dec_s + pre_s) / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16xfp16 (dequantised INT4 weights)",
+        "data": "synthetic (seeded random INT4 block-32 weights generated on the device, "
+                "N(0,0.02) embeddings and classifier, uniform prompt ids)",
+        "config": {"workload": args.workload, "layers": cfg.layers, "batch": B, "prompt": n,
+                   "decode_steps": steps, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (every decode step reads the weights and "
+                         "KV cache, several GB, from HBM)",
+                   "timing": "CUDA events on the library stream around prefill and decode"},
+        "prefill_tok_s": round(B * n * args.steps / pre_s, 2),
+        "e2e": {"value": round(B * steps * args.steps / wall, 2),
+                "unit": "generated tok/s via nut_batch_generate (incl. prefill)",
+                "h2d_bytes_per_step": int(prompts.nbytes),
+                "d2h_bytes_per_step": int(B * steps * 4)},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "whole decode step (per rank)", "bound": "hbm",
+                     "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(ach / peak, 4), "peak_source": src,
+                     "algorithmic_bytes_per_step_per_rank": int(per_rank),
+                     "weight_bytes_held_per_rank": info["weight_bytes"], "traffic": None},
+        "cpu_baseline": None,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
 # capture summarised in profiles/decode_mk_tinyllama_int4.md
 NCU_TRAFFIC: dict = {"tinyllama-int4": 15_660_146_000 + 6_856_704}
@@ -597,7 +706,10 @@ def main():
         run_micro(local)
         return
     _init_dist(world)
-    run_ours(args, rank, world, local)
+    if args.workload in TP_WORKLOADS:
+        run_batch_tp(args, rank, world, local)
+    else:
+        run_ours(args, rank, world, local)
     if world > 1:
         _pg.barrier()
         _pg.destroy_process_group()

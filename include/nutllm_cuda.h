@@ -216,6 +216,52 @@ nut_status nut_generate_greedy(nut_model *model, nut_kv *kv,
                                int32_t *ids, int64_t *n_generated,
                                float *logits, nut_generation_stats *stats);
 
+/* ---- Batched decode, tensor parallel ----------------------------------- */
+
+/* B independent sequences generated in lockstep (BASELINE's 7B-shape
+ * configuration: batch 64, equal prompt lengths), sharded over `world`
+ * ranks, one process per GPU: rank r holds heads [r H/world, (r+1) H/world)
+ * of Wq/Wk/Wv and the matching Wo columns, hidden units
+ * [r F/world, (r+1) F/world) of Wgate/Wup and the matching Wdown columns,
+ * and classifier rows [r V/world, (r+1) V/world); Wo and Wdown partial
+ * outputs are summed with one NCCL all-reduce each per layer, the argmax
+ * with a 64-bit max all-reduce (first-index tie rule of std::max_element).
+ * Heads, kv heads and ffn / 32 must divide by world.  No reference
+ * counterpart: the reference generates one sequence at a time on the CPU
+ * (src/generate.cpp:174-216); this is that loop for a batch, with the
+ * projections as fp16 tensor-core GEMMs (dequantised weights and fp16
+ * activations, so logits follow the prefill GEMM's stated bound). */
+typedef struct nut_batch nut_batch;
+
+/* ncclGetUniqueId for rank 0 to share with the others (size >= 128). */
+nut_status nut_tp_unique_id(uint8_t *id, int64_t size);
+/* This rank's shard of a host model (every rank passes the whole view);
+ * nccl_id may be NULL when world == 1. */
+nut_status nut_batch_create(const nut_model_view *view, int device, int64_t batch, int rank,
+                            int world, const uint8_t *nccl_id, nut_batch **out);
+/* The same with seeded synthetic weights generated on the device (random
+ * INT4 block-32 projections, N(0, 0.02) embeddings and classifier, unit norm
+ * gains), for shapes too large to build on the host. */
+nut_status nut_batch_create_synthetic(const nut_config *config, uint64_t seed, int device,
+                                      int64_t batch, int rank, int world,
+                                      const uint8_t *nccl_id, nut_batch **out);
+void nut_batch_destroy(nut_batch *batch);
+/* info[8] = {batch, heads, kv heads, ffn units, first vocabulary row, vocabulary
+ * rows (all of this rank), weight bytes held, world}. */
+nut_status nut_batch_info(const nut_batch *batch, int64_t *info);
+nut_status nut_batch_stream(nut_batch *batch, void **stream);
+/* This rank's shard without creating anything (host only): shard[8] =
+ * {first head, heads, first kv head, kv heads, first ffn unit, ffn units,
+ * first vocabulary row, vocabulary rows}. */
+nut_status nut_tp_shard(const nut_config *config, int rank, int world, int64_t *shard);
+/* Prompts [batch][n] (host), then `steps` greedy tokens per sequence
+ * without an eos stop: ids [batch][steps] (host).  logits [steps][batch]
+ * [this rank's vocabulary rows] (host) may be NULL.  Collective: every rank
+ * calls it with the same arguments. */
+nut_status nut_batch_generate(nut_batch *batch, const int32_t *prompts, int64_t n,
+                              int64_t steps, int32_t *ids, float *logits,
+                              nut_generation_stats *stats);
+
 /* ---- Greedy head without allocation ------------------------------------ */
 
 /* Largest batch of nut_greedy_head_static. */

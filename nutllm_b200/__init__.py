@@ -169,6 +169,18 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_generate_greedy", [
             _P, _P, _P, _I64, _I64, C.c_int32, _P, _PI64, _P,
             C.POINTER(GenerationStats)])
+        _declare(lib, "nut_tp_unique_id", [_P, _I64])
+        _declare(lib, "nut_batch_create", [C.POINTER(ModelView), C.c_int, _I64, C.c_int,
+                                           C.c_int, _P, C.POINTER(_P)])
+        _declare(lib, "nut_batch_create_synthetic", [C.POINTER(Config), C.c_uint64, C.c_int,
+                                                     _I64, C.c_int, C.c_int, _P,
+                                                     C.POINTER(_P)])
+        _declare(lib, "nut_batch_destroy", [_P], None)
+        _declare(lib, "nut_batch_info", [_P, _PI64])
+        _declare(lib, "nut_tp_shard", [C.POINTER(Config), C.c_int, C.c_int, _PI64])
+        _declare(lib, "nut_batch_stream", [_P, C.POINTER(_P)])
+        _declare(lib, "nut_batch_generate", [_P, _P, _I64, _I64, _P, _P,
+                                             C.POINTER(GenerationStats)])
         _cuda = lib
     return _cuda
 
@@ -469,6 +481,92 @@ class DeviceQMatrix:
     def close(self) -> None:
         if getattr(self, "handle", None):
             cuda_lib().nut_qmatrix_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def tp_shard(config: Config, rank: int, world: int) -> dict:
+    """This rank's slice of heads, kv heads, FFN units and classifier rows
+    (host only; raises ValueError when the split is not even)."""
+    v = (C.c_int64 * 8)()
+    _check(cuda_lib().nut_tp_shard(C.byref(config), rank, world, v))
+    keys = ("head0", "heads", "kv0", "kv_heads", "ffn0", "ffn", "vocab0", "vocab_rows")
+    return dict(zip(keys, [int(x) for x in v]))
+
+
+def tp_unique_id() -> bytes:
+    """ncclGetUniqueId, for rank 0 to broadcast to the other ranks."""
+    buf = (C.c_uint8 * 128)()
+    _check(cuda_lib().nut_tp_unique_id(buf, 128))
+    return bytes(buf)
+
+
+class TPBatch:
+    """One rank's shard of the tensor-parallel batched decoder (nut_batch):
+    `batch` sequences generated in lockstep, heads / FFN units / classifier
+    rows split over `world` ranks with NCCL all-reduces.  Build it from host
+    weights (`weights`, every rank passes the whole model) or, for shapes too
+    large for the host, from seeded synthetic weights (`config`, `seed`)."""
+
+    def __init__(self, batch: int, rank: int = 0, world: int = 1, nccl_id: bytes = None,
+                 weights: "ModelWeights" = None, config: Config = None, seed: int = 0,
+                 device: int = 0):
+        if world > 1 and (nccl_id is None or len(nccl_id) < 128):
+            raise ValueError("TPBatch: world > 1 needs the 128-byte NCCL id")
+        idbuf = (C.c_uint8 * 128).from_buffer_copy(nccl_id[:128]) if nccl_id else None
+        h = C.c_void_p()
+        lib = cuda_lib()
+        if weights is not None:
+            view, keep = weights.view()
+            _check(lib.nut_batch_create(C.byref(view), device, batch, rank, world, idbuf,
+                                        C.byref(h)))
+            del keep
+            self.config = Config(**weights.config.as_dict())
+        else:
+            if config is None:
+                raise ValueError("TPBatch: weights or config required")
+            _check(lib.nut_batch_create_synthetic(C.byref(config), seed, device, batch, rank,
+                                                  world, idbuf, C.byref(h)))
+            self.config = Config(**config.as_dict())
+        self.handle = h
+        self.batch, self.rank, self.world = batch, rank, world
+
+    def info(self) -> dict:
+        v = (C.c_int64 * 8)()
+        _check(cuda_lib().nut_batch_info(self.handle, v))
+        keys = ("batch", "heads", "kv_heads", "ffn", "vocab0", "vocab_rows",
+                "weight_bytes", "world")
+        return dict(zip(keys, [int(x) for x in v]))
+
+    @property
+    def stream(self) -> int:
+        out = _P()
+        _check(cuda_lib().nut_batch_stream(self.handle, C.byref(out)))
+        return int(out.value or 0)
+
+    def generate(self, prompts: np.ndarray, steps: int, want_logits: bool = False):
+        """prompts [batch][n] -> (ids [batch][steps], logits [steps][batch][this
+        rank's vocabulary rows] or None, GenerationStats).  Collective over
+        the ranks."""
+        p = np.ascontiguousarray(prompts, np.int32)
+        if p.ndim != 2 or p.shape[0] != self.batch:
+            raise ValueError("TPBatch.generate: prompts must be [batch][n]")
+        ids = np.zeros((self.batch, max(steps, 1)), np.int32)
+        rows = self.info()["vocab_rows"] if want_logits else 0
+        lg = np.zeros((max(steps, 1), self.batch, rows), np.float32) if want_logits else None
+        st = GenerationStats()
+        _check(cuda_lib().nut_batch_generate(self.handle, _ptr(p), p.shape[1], steps,
+                                             _ptr(ids), _ptr(lg), C.byref(st)))
+        return ids[:, :steps], (lg[:steps] if lg is not None else None), st
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            cuda_lib().nut_batch_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

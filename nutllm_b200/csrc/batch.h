@@ -1,0 +1,63 @@
+#pragma once
+/* Row kernels of the batched (multi-sequence) decode step (batch.cu).  A
+ * batch of B independent sequences advances one token per step, all at the
+ * same position, which is read from device memory so that a captured step
+ * can be replayed for every position.  The KV cache of a batch is fp32
+ * [layer][sequence][kv_head][max_seq][head_dim]: the reference's per-model
+ * layout (src/kvcache.cpp:196-205) repeated per sequence. */
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nut {
+
+/* h[b] += part[b] (when part is not null), then out[b][k] =
+ * fp16(rmsnorm(h[b]) * w) for k < dim and 0 for dim <= k < Kp
+ * (src/ops.cpp:111-134, eps 1e-5). */
+cudaError_t add_rmsnorm_rows(float *h, const float *part, const float *w, int B, int dim,
+                             int Kp, uint16_t *out, cudaStream_t s);
+
+/* RoPE (interleaved pairs, src/quant_model.cpp:26-37) of the q and k rows
+ * of qkv [B][ldq] (q: heads * hd values, then k and v: kv_heads * hd each)
+ * at position *pos, and the k and v rows appended to the batch cache. */
+cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const float *rope_cos,
+                          const float *rope_sin, int heads, int kv_heads, int hd,
+                          float *kcache, float *vcache, int layer, int max_seq,
+                          cudaStream_t s);
+
+/* Attention of every (sequence, head) at position *pos over cached
+ * positions 0 .. *pos (attention_step, src/quant_model.cpp:68-105: scores
+ * q.k / sqrt(hd), softmax, weighted values; GQA head -> kv head by
+ * head / (heads / kv_heads)); context fp16 [B][Kp], zero padded. */
+cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
+                            const float *kcache, const float *vcache, int layer, int heads,
+                            int kv_heads, int hd, int max_seq, int Kp, uint16_t *ctx,
+                            cudaStream_t s);
+
+/* Per row b: the first-index argmax of logits[b][0, V) as a 64-bit key
+ * (order-preserving value bits << 32 | ~(v0 + index)), so that the maximum
+ * key over any split of the vocabulary is the global first-index argmax
+ * (std::max_element, src/generate.cpp:28-30). */
+cudaError_t argmax_keys(const float *logits, int B, int V, int v0, unsigned long long *keys,
+                        cudaStream_t s);
+/* ids[b] = token of keys[b]; also appended to out[b * ld + step] when out
+ * is not null. */
+cudaError_t keys_to_ids(const unsigned long long *keys, int B, int32_t *ids, int32_t *out,
+                        int ld, const int *step, cudaStream_t s);
+/* ids[b] = prompts[b * n + *step] (the next prompt column). */
+cudaError_t prompt_column(const int32_t *prompts, int B, int n, const int *step, int32_t *ids,
+                          cudaStream_t s);
+/* *pos += 1 and *step += 1 (advances a captured step's position). */
+cudaError_t advance(int *pos, int *step, cudaStream_t s);
+
+/* Seeded synthetic weights generated on the device (benchmark shapes too
+ * large to build on the host): normal(0, sigma) fp32 values, and fp16
+ * values q * scale of random symmetric INT4 blocks (q uniform in [-7, 7],
+ * one fp16 scale per 32 consecutive values of a row, near sigma * 2.5 / 7),
+ * i.e. the dequantised form of a random INT4 block-32 matrix. */
+cudaError_t synth_normal_dev(uint64_t seed, uint64_t stream, float sigma, float *out, size_t n,
+                             cudaStream_t s);
+cudaError_t synth_int4_f16_dev(uint64_t seed, uint64_t stream, float sigma, int rows, int cols,
+                               int ld, uint16_t *out, cudaStream_t s);
+
+} // namespace nut

@@ -1,0 +1,647 @@
+/* Tensor-parallel batched decoder (nut_batch_* in nutllm_cuda.h).
+ *
+ * B independent sequences advance one token per step, all at the same
+ * position.  Each of `world` ranks (one process per GPU) holds one shard
+ * of every layer, as the survey of the reference's Llama decoder splits it
+ * ([out][in] storage, src/llama2.cpp:374-396):
+ *   column-parallel  Wq, Wk, Wv rows of this rank's heads (heads / world
+ *                    query heads, kv_heads / world kv heads), Wgate and
+ *                    Wup rows of its ffn / world hidden units;
+ *   row-parallel     Wo columns of its heads, Wdown columns of its units,
+ *                    whose partial outputs are summed over the ranks with
+ *                    one NCCL all-reduce each per layer;
+ *   vocabulary split the classifier rows [v0, v1), with the first-index
+ *                    argmax combined by a 64-bit max all-reduce of
+ *                    (value, ~index) keys.
+ * Embeddings and norms are replicated.  A step is: rmsnorm rows -> [q;k;v]
+ * GEMM -> RoPE + KV append -> attention -> Wo GEMM -> all-reduce ->
+ * residual + rmsnorm -> gate/up GEMM -> SwiGLU -> Wdown GEMM -> all-reduce,
+ * per layer, then the final norm, classifier GEMM and argmax.  The GEMMs
+ * are the tcgen05 fp16 GEMM of gemm_tc.cu over dequantised (q * scale
+ * rounded to fp16) weights; activations are rounded to fp16 per GEMM.
+ * NCCL is resolved at run time (dlopen of libnccl.so.2), so the library
+ * loads without it and shares the copy an embedding process already holds.
+ */
+#include <dlfcn.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include "../../include/nutllm_cuda.h"
+#include "batch.h"
+#include "kernels.h"
+#include "kernels_tc.h"
+#include "prefill.h"
+
+namespace {
+
+struct Failure {
+    nut_status status;
+    std::string message;
+};
+
+[[noreturn]] void raise(nut_status s, const std::string &m) { throw Failure{s, m}; }
+
+void cuda_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess)
+        raise(NUT_RUNTIME_ERROR, std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+
+template <typename F> nut_status guarded(F &&body) {
+    try {
+        body();
+        return NUT_OK;
+    } catch (const Failure &f) {
+        nut::set_last_error(f.message);
+        return f.status;
+    } catch (const std::bad_alloc &) {
+        nut::set_last_error("nutllm: host allocation failed");
+        return NUT_RUNTIME_ERROR;
+    } catch (const std::exception &e) {
+        nut::set_last_error(e.what());
+        return NUT_RUNTIME_ERROR;
+    }
+}
+
+struct DeviceScope {
+    int previous = 0;
+    explicit DeviceScope(int device) {
+        cuda_check(cudaGetDevice(&previous), "get device");
+        cuda_check(cudaSetDevice(device), "set device");
+    }
+    ~DeviceScope() { cudaSetDevice(previous); }
+};
+
+template <typename T> T *dev_alloc(size_t count, const char *what) {
+    void *p = nullptr;
+    cuda_check(cudaMalloc(&p, (count == 0 ? 1 : count) * sizeof(T)), what);
+    return static_cast<T *>(p);
+}
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+/* ---- NCCL, resolved at run time ------------------------------------ */
+
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                               ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi &nccl() {
+    static NcclApi api;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (h == nullptr)
+            h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (h != nullptr) {
+            api.get_unique_id =
+                reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+            api.comm_init_rank =
+                reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+            api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+            api.comm_destroy =
+                reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+            api.error_string =
+                reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        }
+    }
+    if (api.get_unique_id == nullptr || api.comm_init_rank == nullptr ||
+        api.all_reduce == nullptr || api.comm_destroy == nullptr)
+        raise(NUT_RUNTIME_ERROR, "tensor parallel: libnccl.so.2 not available");
+    return api;
+}
+
+void nccl_check(ncclResult_t r, const char *what) {
+    if (r != ncclSuccess) {
+        const char *msg = nccl().error_string ? nccl().error_string(r) : "error";
+        raise(NUT_RUNTIME_ERROR, std::string("nccl: ") + what + ": " + msg);
+    }
+}
+
+/* ---- host dequantisation of a view slice into fp16 ------------------ */
+
+float qvalue(const nut_qmatrix_view &v, int64_t r, int64_t c) {
+    const int64_t i = r * v.cols + c;
+    int q;
+    if (v.type == NUT_QUANT_INT8) {
+        q = int(int8_t(v.data[i]));
+    } else {
+        const int nib = (v.data[i / 2] >> ((i & 1) ? 4 : 0)) & 0xF;
+        q = nib >= 8 ? nib - 16 : nib;
+    }
+    return float(q) * __half2float(__ushort_as_half(v.scales[i / 32]));
+}
+
+uint16_t to_f16(float v) {
+    v = std::fmin(std::fmax(v, -65504.0f), 65504.0f);
+    return __half_as_ushort(__float2half_rn(v));
+}
+
+} // namespace
+
+struct nut_batch {
+    int device = 0, rank = 0, world = 1, B = 0;
+    nut_config cfg{};
+    int kvh = 0;                 /* kv heads of the model */
+    int heads_r = 0, kvh_r = 0, hd = 0, dim = 0, ffn_r = 0, vocab_r = 0, v0 = 0;
+    int max_seq = 0, layers = 0, nqkv = 0;
+    int kp_dim = 0, kp_ctx = 0, kp_ffn = 0;
+    cudaStream_t stream = nullptr;
+    ncclComm_t comm = nullptr;
+    struct Layer {
+        uint16_t *qkv = nullptr, *wo = nullptr, *gu = nullptr, *down = nullptr;
+        float *attn_norm = nullptr, *ffn_norm = nullptr;
+    };
+    std::vector<Layer> L;
+    float *emb = nullptr, *final_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    uint16_t *lm = nullptr;
+    float *kcache = nullptr, *vcache = nullptr;
+    float *h = nullptr, *part = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
+    uint16_t *x16 = nullptr, *ctx16 = nullptr, *act16 = nullptr;
+    unsigned long long *keys = nullptr;
+    int32_t *ids = nullptr, *out = nullptr, *prompts = nullptr;
+    int *pos = nullptr, *pstep = nullptr, *ostep = nullptr; /* device counters */
+    int *gemm_error = nullptr;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    uint64_t weight_bytes = 0; /* fp16 weights + fp32 tensors this rank holds */
+
+    ~nut_batch() {
+        if (stream == nullptr)
+            return; /* nothing was allocated (the stream is created first) */
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        if (stream)
+            cudaStreamSynchronize(stream);
+        for (Layer &l : L)
+            for (void *p : {(void *)l.qkv, (void *)l.wo, (void *)l.gu, (void *)l.down,
+                            (void *)l.attn_norm, (void *)l.ffn_norm})
+                if (p)
+                    cudaFree(p);
+        for (void *p : {(void *)emb, (void *)final_norm, (void *)rope_cos, (void *)rope_sin,
+                        (void *)lm, (void *)kcache, (void *)vcache, (void *)h, (void *)part,
+                        (void *)qkv, (void *)gu, (void *)logits, (void *)x16, (void *)ctx16,
+                        (void *)act16, (void *)keys, (void *)ids, (void *)out,
+                        (void *)prompts, (void *)pos, (void *)pstep, (void *)ostep,
+                        (void *)gemm_error})
+            if (p)
+                cudaFree(p);
+        for (cudaEvent_t e : ev)
+            if (e)
+                cudaEventDestroy(e);
+        if (comm)
+            nccl().comm_destroy(comm);
+        if (stream)
+            cudaStreamDestroy(stream);
+        cudaSetDevice(prev);
+    }
+};
+
+namespace {
+
+/* Shard shape of rank `rank` of `world` (checks the split points). */
+void plan_shard(nut_batch &b, const nut_config &c, int rank, int world, int64_t batch) {
+    const int64_t kvh = c.kv_heads == 0 ? c.heads : c.kv_heads;
+    if (c.layers <= 0 || c.heads <= 0 || c.dim <= 0 || c.head_dim <= 0 || c.ffn_dim <= 0 ||
+        c.vocab_size <= 0 || c.max_seq <= 0 || c.heads * c.head_dim != c.dim ||
+        c.head_dim % 4 != 0 || kvh <= 0 || c.heads % kvh != 0)
+        raise(NUT_INVALID_ARGUMENT, "model config: invalid dimensions");
+    if (world <= 0 || rank < 0 || rank >= world)
+        raise(NUT_INVALID_ARGUMENT, "tensor parallel: invalid rank");
+    if (c.heads % world != 0 || kvh % world != 0 || c.ffn_dim % (32 * world) != 0 ||
+        c.vocab_size < world)
+        raise(NUT_INVALID_ARGUMENT,
+              "tensor parallel: heads, kv heads and ffn blocks must split evenly");
+    if (batch <= 0 || batch > 4096)
+        raise(NUT_INVALID_ARGUMENT, "batch: invalid size");
+    b.cfg = c;
+    b.rank = rank;
+    b.world = world;
+    b.B = int(batch);
+    b.kvh = int(kvh);
+    b.hd = int(c.head_dim);
+    b.dim = int(c.dim);
+    b.layers = int(c.layers);
+    b.max_seq = int(c.max_seq);
+    b.heads_r = int(c.heads / world);
+    b.kvh_r = int(kvh / world);
+    b.ffn_r = int(c.ffn_dim / world);
+    b.v0 = int(c.vocab_size * rank / world);
+    b.vocab_r = int(c.vocab_size * (rank + 1) / world) - b.v0;
+    b.nqkv = (b.heads_r + 2 * b.kvh_r) * b.hd;
+    b.kp_dim = round_up(b.dim, 64);
+    b.kp_ctx = round_up(b.heads_r * b.hd, 64);
+    b.kp_ffn = round_up(b.ffn_r, 64);
+}
+
+void alloc_state(nut_batch &b) {
+    const size_t B = size_t(b.B);
+    cuda_check(cudaStreamCreateWithFlags(&b.stream, cudaStreamNonBlocking), "create stream");
+    for (cudaEvent_t &e : b.ev)
+        cuda_check(cudaEventCreate(&e), "create event");
+    const size_t kv = size_t(b.layers) * B * b.kvh_r * size_t(b.max_seq) * b.hd;
+    b.kcache = dev_alloc<float>(kv, "alloc kv cache");
+    b.vcache = dev_alloc<float>(kv, "alloc kv cache");
+    b.h = dev_alloc<float>(B * b.dim, "alloc rows");
+    b.part = dev_alloc<float>(B * b.dim, "alloc rows");
+    b.qkv = dev_alloc<float>(B * b.nqkv, "alloc rows");
+    b.gu = dev_alloc<float>(B * 2 * b.ffn_r, "alloc rows");
+    b.logits = dev_alloc<float>(B * b.vocab_r, "alloc rows");
+    b.x16 = dev_alloc<uint16_t>(B * b.kp_dim, "alloc rows");
+    b.ctx16 = dev_alloc<uint16_t>(B * b.kp_ctx, "alloc rows");
+    b.act16 = dev_alloc<uint16_t>(B * b.kp_ffn, "alloc rows");
+    b.keys = dev_alloc<unsigned long long>(B, "alloc keys");
+    b.ids = dev_alloc<int32_t>(B, "alloc ids");
+    b.out = dev_alloc<int32_t>(B * b.max_seq, "alloc ids");
+    b.prompts = dev_alloc<int32_t>(B * b.max_seq, "alloc prompts");
+    b.pos = dev_alloc<int>(1, "alloc counters");
+    b.pstep = dev_alloc<int>(1, "alloc counters");
+    b.ostep = dev_alloc<int>(1, "alloc counters");
+    b.gemm_error = dev_alloc<int>(1, "alloc error word");
+    cuda_check(cudaMemset(b.gemm_error, 0, sizeof(int)), "clear error word");
+    /* RoPE table with the reference's fp32 values (frequency and angle in
+     * double, rounded once; src/quant_model.cpp:26-37) */
+    const size_t half = size_t(b.hd / 2), S = size_t(b.max_seq);
+    std::vector<float> cs(S * half), sn(S * half);
+    for (size_t p = 0; p < S; p++)
+        for (size_t j = 0; j < half; j++) {
+            const double f = std::pow(10000.0, -double(2 * j) / double(b.hd));
+            cs[p * half + j] = float(std::cos(double(p) * f));
+            sn[p * half + j] = float(std::sin(double(p) * f));
+        }
+    b.rope_cos = dev_alloc<float>(S * half, "alloc rope");
+    b.rope_sin = dev_alloc<float>(S * half, "alloc rope");
+    cuda_check(cudaMemcpy(b.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice),
+               "copy rope");
+    cuda_check(cudaMemcpy(b.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice),
+               "copy rope");
+    b.L.resize(size_t(b.layers));
+}
+
+uint16_t *upload_f16(const std::vector<uint16_t> &v, uint64_t &bytes) {
+    uint16_t *p = dev_alloc<uint16_t>(v.size(), "alloc fp16 weights");
+    cuda_check(cudaMemcpy(p, v.data(), v.size() * 2, cudaMemcpyHostToDevice), "copy weights");
+    bytes += v.size() * 2;
+    return p;
+}
+
+float *upload_f32(const float *src, size_t n, uint64_t &bytes) {
+    float *p = dev_alloc<float>(n, "alloc fp32 tensor");
+    cuda_check(cudaMemcpy(p, src, n * 4, cudaMemcpyHostToDevice), "copy fp32 tensor");
+    bytes += n * 4;
+    return p;
+}
+
+/* This rank's shard of a host model (the reference's storage), dequantised
+ * to fp16 on the host. */
+void load_view(nut_batch &b, const nut_model_view &v) {
+    const nut_config &c = b.cfg;
+    if (v.n_layers != c.layers || v.layers == nullptr || v.embeddings == nullptr ||
+        v.final_norm == nullptr || (!v.tied_embeddings && v.lm_head == nullptr))
+        raise(NUT_INVALID_ARGUMENT, "model: incomplete view");
+    const int dim = b.dim, hd = b.hd;
+    const int q0 = b.rank * b.heads_r * hd, k0 = b.rank * b.kvh_r * hd;
+    const int kvd_r = b.kvh_r * hd, f0 = b.rank * b.ffn_r;
+    for (int l = 0; l < b.layers; l++) {
+        const nut_layer_view &lv = v.layers[l];
+        for (const nut_qmatrix_view *m : {&lv.query, &lv.key, &lv.value, &lv.output, &lv.gate,
+                                          &lv.up, &lv.down})
+            if (m->data == nullptr || m->scales == nullptr || m->block_size != 32 ||
+                m->type != v.quant_type)
+                raise(NUT_INVALID_ARGUMENT, "model: invalid matrix view");
+        std::vector<uint16_t> qkv(size_t(b.nqkv) * b.kp_dim, 0);
+        for (int r = 0; r < b.nqkv; r++) {
+            const nut_qmatrix_view *m;
+            int src;
+            if (r < b.heads_r * hd) {
+                m = &lv.query;
+                src = q0 + r;
+            } else if (r < b.heads_r * hd + kvd_r) {
+                m = &lv.key;
+                src = k0 + r - b.heads_r * hd;
+            } else {
+                m = &lv.value;
+                src = k0 + r - b.heads_r * hd - kvd_r;
+            }
+            for (int k = 0; k < dim; k++)
+                qkv[size_t(r) * b.kp_dim + k] = to_f16(qvalue(*m, src, k));
+        }
+        std::vector<uint16_t> wo(size_t(dim) * b.kp_ctx, 0);
+        for (int r = 0; r < dim; r++)
+            for (int k = 0; k < b.heads_r * hd; k++)
+                wo[size_t(r) * b.kp_ctx + k] = to_f16(qvalue(lv.output, r, q0 + k));
+        std::vector<uint16_t> gu(size_t(2 * b.ffn_r) * b.kp_dim, 0);
+        for (int r = 0; r < 2 * b.ffn_r; r++) {
+            const int group = r / 16, within = r % 16;
+            const nut_qmatrix_view &m = within >= 8 ? lv.up : lv.gate;
+            const int src = f0 + group * 8 + within % 8;
+            for (int k = 0; k < dim; k++)
+                gu[size_t(r) * b.kp_dim + k] = to_f16(qvalue(m, src, k));
+        }
+        std::vector<uint16_t> down(size_t(dim) * b.kp_ffn, 0);
+        for (int r = 0; r < dim; r++)
+            for (int k = 0; k < b.ffn_r; k++)
+                down[size_t(r) * b.kp_ffn + k] = to_f16(qvalue(lv.down, r, f0 + k));
+        nut_batch::Layer &d = b.L[size_t(l)];
+        d.qkv = upload_f16(qkv, b.weight_bytes);
+        d.wo = upload_f16(wo, b.weight_bytes);
+        d.gu = upload_f16(gu, b.weight_bytes);
+        d.down = upload_f16(down, b.weight_bytes);
+        d.attn_norm = upload_f32(lv.attention_norm, size_t(dim), b.weight_bytes);
+        d.ffn_norm = upload_f32(lv.ffn_norm, size_t(dim), b.weight_bytes);
+    }
+    b.emb = upload_f32(v.embeddings, size_t(c.vocab_size) * dim, b.weight_bytes);
+    b.final_norm = upload_f32(v.final_norm, size_t(dim), b.weight_bytes);
+    const float *cls = v.tied_embeddings ? v.embeddings : v.lm_head;
+    std::vector<uint16_t> lm(size_t(b.vocab_r) * b.kp_dim, 0);
+    for (int r = 0; r < b.vocab_r; r++)
+        for (int k = 0; k < dim; k++)
+            lm[size_t(r) * b.kp_dim + k] = to_f16(cls[size_t(b.v0 + r) * dim + k]);
+    b.lm = upload_f16(lm, b.weight_bytes);
+}
+
+/* Seeded synthetic shard generated on the device: random INT4 block-32
+ * projections (dequantised to fp16), N(0, 0.02) embeddings and classifier,
+ * unit norm gains. */
+void load_synthetic(nut_batch &b, uint64_t seed) {
+    const int dim = b.dim;
+    cudaStream_t s = b.stream;
+    const float sigma = 0.02f;
+    auto stream_id = [&](int layer, int which) {
+        return uint64_t(layer) * 64 + uint64_t(which) * 8 + uint64_t(b.rank) + 1;
+    };
+    auto make = [&](int rows, int cols, int ld, uint64_t id) {
+        uint16_t *p = dev_alloc<uint16_t>(size_t(rows) * ld, "alloc fp16 weights");
+        cuda_check(nut::synth_int4_f16_dev(seed, id, sigma, rows, cols, ld, p, s), "synth");
+        b.weight_bytes += size_t(rows) * ld * 2;
+        return p;
+    };
+    std::vector<float> ones(size_t(dim), 1.0f);
+    for (int l = 0; l < b.layers; l++) {
+        nut_batch::Layer &d = b.L[size_t(l)];
+        d.qkv = make(b.nqkv, dim, b.kp_dim, stream_id(l, 0));
+        d.wo = make(dim, b.heads_r * b.hd, b.kp_ctx, stream_id(l, 1));
+        d.gu = make(2 * b.ffn_r, dim, b.kp_dim, stream_id(l, 2));
+        d.down = make(dim, b.ffn_r, b.kp_ffn, stream_id(l, 3));
+        d.attn_norm = upload_f32(ones.data(), size_t(dim), b.weight_bytes);
+        d.ffn_norm = upload_f32(ones.data(), size_t(dim), b.weight_bytes);
+    }
+    const size_t V = size_t(b.cfg.vocab_size);
+    b.emb = dev_alloc<float>(V * dim, "alloc embeddings");
+    cuda_check(nut::synth_normal_dev(seed, 1u << 20, sigma, b.emb, V * dim, s), "synth");
+    b.weight_bytes += V * dim * 4;
+    b.final_norm = upload_f32(ones.data(), size_t(dim), b.weight_bytes);
+    float *cls = dev_alloc<float>(size_t(b.vocab_r) * dim, "alloc classifier");
+    cuda_check(nut::synth_normal_dev(seed, (2u << 20) + uint64_t(b.rank), sigma, cls,
+                                     size_t(b.vocab_r) * dim, s),
+               "synth");
+    b.lm = dev_alloc<uint16_t>(size_t(b.vocab_r) * b.kp_dim, "alloc classifier");
+    cuda_check(nut::round_f16(cls, b.vocab_r, dim, b.kp_dim, b.lm, s), "round classifier");
+    b.weight_bytes += size_t(b.vocab_r) * b.kp_dim * 2;
+    cuda_check(cudaStreamSynchronize(s), "synthesise weights");
+    cudaFree(cls);
+}
+
+void gemm(nut_batch &b, const uint16_t *a, const uint16_t *w, int N, int K, float *y) {
+    cuda_check(nut::gemm_f16(a, b.B, w, N, N, K, y, N, b.gemm_error, nut::kDefaultWaitNs,
+                             b.stream, false),
+               "batch gemm");
+}
+
+void all_reduce_sum(nut_batch &b, float *x, size_t n) {
+    if (b.world > 1)
+        nccl_check(nccl().all_reduce(x, x, n, ncclFloat32, ncclSum, b.comm, b.stream),
+                   "all-reduce");
+}
+
+/* One forward pass of the batch: token ids in b.ids at position *b.pos,
+ * every layer; the hidden rows stay in b.h with the last Wdown partial
+ * (already summed over the ranks) in b.part. */
+void forward(nut_batch &b) {
+    cudaStream_t s = b.stream;
+    const int B = b.B, dim = b.dim;
+    cuda_check(nut::gather_rows(b.emb, b.ids, B, dim, int(b.cfg.vocab_size), b.h, s), "embed");
+    for (int l = 0; l < b.layers; l++) {
+        const nut_batch::Layer &L = b.L[size_t(l)];
+        cuda_check(nut::add_rmsnorm_rows(b.h, l == 0 ? nullptr : b.part, L.attn_norm, B, dim,
+                                         b.kp_dim, b.x16, s),
+                   "rmsnorm");
+        gemm(b, b.x16, L.qkv, b.nqkv, b.kp_dim, b.qkv);
+        cuda_check(nut::rope_kv_batch(b.qkv, B, b.nqkv, b.pos, b.rope_cos, b.rope_sin,
+                                      b.heads_r, b.kvh_r, b.hd, b.kcache, b.vcache, l,
+                                      b.max_seq, s),
+                   "rope");
+        cuda_check(nut::attention_batch(b.qkv, B, b.nqkv, b.pos, b.kcache, b.vcache, l,
+                                        b.heads_r, b.kvh_r, b.hd, b.max_seq, b.kp_ctx, b.ctx16,
+                                        s),
+                   "attention");
+        gemm(b, b.ctx16, L.wo, dim, b.kp_ctx, b.part);
+        all_reduce_sum(b, b.part, size_t(B) * dim);
+        cuda_check(nut::add_rmsnorm_rows(b.h, b.part, L.ffn_norm, B, dim, b.kp_dim, b.x16, s),
+                   "rmsnorm");
+        gemm(b, b.x16, L.gu, 2 * b.ffn_r, b.kp_dim, b.gu);
+        cuda_check(nut::swiglu_rows(b.gu, B, b.ffn_r, b.kp_ffn, b.act16, s), "swiglu");
+        gemm(b, b.act16, L.down, dim, b.kp_ffn, b.part);
+        all_reduce_sum(b, b.part, size_t(B) * dim);
+    }
+}
+
+/* Final norm, this rank's classifier rows, and the global first-index
+ * argmax into b.ids (and b.out[:, *ostep]). */
+void head(nut_batch &b) {
+    cudaStream_t s = b.stream;
+    cuda_check(nut::add_rmsnorm_rows(b.h, b.part, b.final_norm, b.B, b.dim, b.kp_dim, b.x16, s),
+               "final norm");
+    gemm(b, b.x16, b.lm, b.vocab_r, b.kp_dim, b.logits);
+    cuda_check(nut::argmax_keys(b.logits, b.B, b.vocab_r, b.v0, b.keys, s), "argmax");
+    if (b.world > 1)
+        nccl_check(nccl().all_reduce(b.keys, b.keys, size_t(b.B), ncclUint64, ncclMax, b.comm, s),
+                   "argmax all-reduce");
+    cuda_check(nut::keys_to_ids(b.keys, b.B, b.ids, b.out, b.max_seq, b.ostep, s), "ids");
+}
+
+void check_gemm_error(nut_batch &b) {
+    int code = 0;
+    cuda_check(cudaMemcpyAsync(&code, b.gemm_error, sizeof code, cudaMemcpyDeviceToHost,
+                               b.stream),
+               "read error word");
+    cuda_check(cudaStreamSynchronize(b.stream), "synchronize");
+    if (code != 0) {
+        cudaMemsetAsync(b.gemm_error, 0, sizeof(int), b.stream);
+        cudaStreamSynchronize(b.stream);
+        raise(NUT_DEVICE_TIMEOUT, "device: bounded wait gave up (code " + std::to_string(code) +
+                                      ")");
+    }
+}
+
+nut_status create(const nut_config *config, const nut_model_view *view, uint64_t seed,
+                  int device, int64_t batch, int rank, int world, const uint8_t *nccl_id,
+                  nut_batch **out) {
+    return guarded([&] {
+        if (config == nullptr || out == nullptr || (world > 1 && nccl_id == nullptr))
+            raise(NUT_INVALID_ARGUMENT, "batch: null argument");
+        *out = nullptr;
+        DeviceScope scope(device);
+        auto b = std::make_unique<nut_batch>();
+        b->device = device;
+        plan_shard(*b, *config, rank, world, batch);
+        alloc_state(*b);
+        if (view != nullptr)
+            load_view(*b, *view);
+        else
+            load_synthetic(*b, seed);
+        if (world > 1) {
+            ncclUniqueId id;
+            std::memcpy(&id, nccl_id, sizeof id);
+            nccl_check(nccl().comm_init_rank(&b->comm, world, id, rank), "init communicator");
+        }
+        cuda_check(cudaDeviceSynchronize(), "finish uploads");
+        *out = b.release();
+    });
+}
+
+} // namespace
+
+extern "C" {
+
+nut_status nut_tp_unique_id(uint8_t *id, int64_t size) {
+    return guarded([&] {
+        if (id == nullptr || size < int64_t(sizeof(ncclUniqueId)))
+            raise(NUT_INVALID_ARGUMENT, "tensor parallel: id buffer too small");
+        ncclUniqueId u;
+        nccl_check(nccl().get_unique_id(&u), "unique id");
+        std::memcpy(id, &u, sizeof u);
+    });
+}
+
+nut_status nut_batch_create(const nut_model_view *view, int device, int64_t batch, int rank,
+                            int world, const uint8_t *nccl_id, nut_batch **out) {
+    if (view == nullptr) {
+        nut::set_last_error("batch: null argument");
+        return NUT_INVALID_ARGUMENT;
+    }
+    return create(&view->config, view, 0, device, batch, rank, world, nccl_id, out);
+}
+
+nut_status nut_batch_create_synthetic(const nut_config *config, uint64_t seed, int device,
+                                      int64_t batch, int rank, int world,
+                                      const uint8_t *nccl_id, nut_batch **out) {
+    return create(config, nullptr, seed, device, batch, rank, world, nccl_id, out);
+}
+
+void nut_batch_destroy(nut_batch *b) { delete b; }
+
+nut_status nut_tp_shard(const nut_config *config, int rank, int world, int64_t *shard) {
+    return guarded([&] {
+        if (config == nullptr || shard == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "batch: null argument");
+        nut_batch b;
+        plan_shard(b, *config, rank, world, 1);
+        const int64_t v[8] = {int64_t(rank) * b.heads_r, b.heads_r, int64_t(rank) * b.kvh_r,
+                              b.kvh_r, int64_t(rank) * b.ffn_r, b.ffn_r, b.v0, b.vocab_r};
+        std::memcpy(shard, v, sizeof v);
+    });
+}
+
+nut_status nut_batch_info(const nut_batch *b, int64_t *info) {
+    return guarded([&] {
+        if (b == nullptr || info == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "batch: null argument");
+        const int64_t v[8] = {b->B, b->heads_r, b->kvh_r, b->ffn_r, b->v0, b->vocab_r,
+                              int64_t(b->weight_bytes), b->world};
+        std::memcpy(info, v, sizeof v);
+    });
+}
+
+nut_status nut_batch_stream(nut_batch *b, void **stream) {
+    return guarded([&] {
+        if (b == nullptr || stream == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "batch: null argument");
+        *stream = b->stream;
+    });
+}
+
+nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, int64_t steps,
+                              int32_t *ids, float *logits, nut_generation_stats *stats) {
+    return guarded([&] {
+        if (b == nullptr || prompts == nullptr || (steps > 0 && ids == nullptr))
+            raise(NUT_INVALID_ARGUMENT, "generation: invalid argument");
+        if (n <= 0 || steps < 0 || n + steps > b->max_seq + 1 || n > b->max_seq)
+            raise(NUT_INVALID_ARGUMENT, "generation: invalid prompt length");
+        const int64_t V = b->cfg.vocab_size;
+        for (int64_t i = 0; i < int64_t(b->B) * n; i++)
+            if (prompts[i] < 0 || prompts[i] >= V)
+                raise(NUT_OUT_OF_RANGE, "quantized decode: token out of range");
+        DeviceScope scope(b->device);
+        cudaStream_t s = b->stream;
+        cuda_check(cudaMemcpyAsync(b->prompts, prompts, size_t(b->B) * n * 4,
+                                   cudaMemcpyHostToDevice, s),
+                   "copy prompts");
+        cuda_check(cudaMemsetAsync(b->pos, 0, sizeof(int), s), "reset position");
+        cuda_check(cudaMemsetAsync(b->pstep, 0, sizeof(int), s), "reset position");
+        cuda_check(cudaMemsetAsync(b->ostep, 0, sizeof(int), s), "reset position");
+        std::vector<float> lg;
+        cuda_check(cudaEventRecord(b->ev[0], s), "record event");
+        /* the prompt, one position per pass (its classifier only after the
+         * last prompt token) */
+        for (int64_t t = 0; t < n; t++) {
+            cuda_check(nut::prompt_column(b->prompts, b->B, int(n), b->pstep, b->ids, s),
+                       "prompt");
+            forward(*b);
+            if (t + 1 < n)
+                cuda_check(nut::advance(b->pos, b->pstep, s), "advance");
+        }
+        cuda_check(cudaEventRecord(b->ev[1], s), "record event");
+        for (int64_t k = 0; k < steps; k++) {
+            if (k > 0) {
+                cuda_check(nut::advance(b->pos, b->ostep, s), "advance");
+                forward(*b);
+            }
+            head(*b);
+            if (logits != nullptr)
+                cuda_check(cudaMemcpyAsync(logits + size_t(k) * b->B * b->vocab_r, b->logits,
+                                           size_t(b->B) * b->vocab_r * 4,
+                                           cudaMemcpyDeviceToHost, s),
+                           "copy logits");
+        }
+        cuda_check(cudaEventRecord(b->ev[2], s), "record event");
+        if (steps > 0) {
+            std::vector<int32_t> all(size_t(b->B) * b->max_seq);
+            cuda_check(cudaMemcpyAsync(all.data(), b->out, all.size() * 4,
+                                       cudaMemcpyDeviceToHost, s),
+                       "copy ids");
+            check_gemm_error(*b);
+            for (int r = 0; r < b->B; r++)
+                std::memcpy(ids + size_t(r) * steps, all.data() + size_t(r) * b->max_seq,
+                            size_t(steps) * 4);
+        } else {
+            check_gemm_error(*b);
+        }
+        if (stats != nullptr) {
+            float pre = 0.0f, dec = 0.0f;
+            cuda_check(cudaEventElapsedTime(&pre, b->ev[0], b->ev[1]), "elapsed");
+            cuda_check(cudaEventElapsedTime(&dec, b->ev[1], b->ev[2]), "elapsed");
+            stats->prefill_tokens = int64_t(b->B) * n;
+            stats->generated_tokens = int64_t(b->B) * steps;
+            stats->prefill_seconds = double(pre) * 1e-3;
+            stats->decode_seconds = double(dec) * 1e-3;
+        }
+    });
+}
+
+} // extern "C"

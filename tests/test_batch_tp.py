@@ -1,0 +1,200 @@
+"""Batched, tensor-parallel decode (nut_batch): shard plan and rank logic on
+CPU (gloo, world size 2), the batched step against the oracle on one GPU,
+and tensor parallel against one rank on two GPUs.
+
+The batched step runs B independent sequences through the reference's
+decoder (decode_quantized_token, src/quant_model.cpp:158-206, and the greedy
+head of generate_tokens_cached, src/generate.cpp:197-205) with the
+projections as fp16 tensor-core GEMMs, so its logits are held to the same
+stated bound as the batched prefill."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import nutllm_b200 as nb
+from nutllm_b200 import synthetic as syn
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ATOL, RTOL, MEDIAN = 3e-2, 1e-2, 3e-3  # fp16-operand bound, as for batched prefill
+
+
+def _cfg(**k):
+    base = dict(layers=2, heads=8, dim=256, head_dim=32, ffn_dim=512, vocab_size=1000,
+                max_seq=64, eos_token=1, kv_heads=2)
+    base.update(k)
+    return nb.Config(**base)
+
+
+LLAMA7B = _cfg(layers=32, heads=32, dim=4096, head_dim=128, ffn_dim=11008, vocab_size=32000,
+               max_seq=256, kv_heads=32)
+TINYLLAMA = _cfg(layers=22, heads=32, dim=2048, head_dim=64, ffn_dim=5632, vocab_size=32000,
+                 max_seq=2048, kv_heads=4)
+
+
+# ------------------------------------------------------------------ CPU
+
+
+@pytest.mark.parametrize("cfg,worlds", [(LLAMA7B, (1, 2, 4, 8)), (TINYLLAMA, (1, 2, 4)),
+                                        (_cfg(), (1, 2))])
+def test_shards_cover_the_model_once(cfg, worlds):
+    for world in worlds:
+        shards = [nb.tp_shard(cfg, r, world) for r in range(world)]
+        for key, total, align in (("head", cfg.heads, 1), ("kv", cfg.kv_heads, 1),
+                                  ("ffn", cfg.ffn_dim, 32), ("vocab", cfg.vocab_size, 1)):
+            first = {"head": "head0", "kv": "kv0", "ffn": "ffn0", "vocab": "vocab0"}[key]
+            count = {"head": "heads", "kv": "kv_heads", "ffn": "ffn",
+                     "vocab": "vocab_rows"}[key]
+            at = 0
+            for s in shards:
+                assert s[first] == at and s[first] % align == 0
+                at += s[count]
+            assert at == total
+        # every query head's kv head lives on the same rank
+        g = cfg.heads // cfg.kv_heads
+        for s in shards:
+            for h in range(s["head0"], s["head0"] + s["heads"]):
+                assert s["kv0"] <= h // g < s["kv0"] + s["kv_heads"]
+
+
+def test_uneven_splits_are_rejected():
+    with pytest.raises(ValueError, match="split evenly"):
+        nb.tp_shard(TINYLLAMA, 0, 8)          # 4 kv heads over 8 ranks
+    with pytest.raises(ValueError, match="split evenly"):
+        nb.tp_shard(_cfg(ffn_dim=544), 0, 2)  # 17 blocks of 32 units
+    with pytest.raises(ValueError, match="invalid rank"):
+        nb.tp_shard(_cfg(), 2, 2)
+
+
+def _gloo_worker(rank, world, port, out):
+    """Two CPU ranks run one layer's tensor-parallel split with numpy and
+    combine it the way the device path does: an all-reduce sum of the
+    row-parallel partials and a max all-reduce of the argmax keys."""
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = _cfg()
+    s = nb.tp_shard(cfg, rank, world)
+    rng = np.random.default_rng(5)
+    D, F, V = cfg.dim, cfg.ffn_dim, cfg.vocab_size
+    ctx = rng.standard_normal(D)
+    act = rng.standard_normal(F)
+    wo = rng.standard_normal((D, D))
+    wd = rng.standard_normal((D, F))
+    hd = cfg.head_dim
+    c0, c1 = s["head0"] * hd, (s["head0"] + s["heads"]) * hd
+    f0, f1 = s["ffn0"], s["ffn0"] + s["ffn"]
+    part = wo[:, c0:c1] @ ctx[c0:c1] + wd[:, f0:f1] @ act[f0:f1]
+    t = torch.from_numpy(part)
+    dist.all_reduce(t)
+    full = wo @ ctx + wd @ act
+    # argmax keys over this rank's vocabulary rows, with ties across ranks
+    logits = np.round(rng.standard_normal(V), 1).astype(np.float32)
+    logits[[3, V - 2]] = logits.max() + 1.0  # tie: first index must win
+    v0, v1 = s["vocab0"], s["vocab0"] + s["vocab_rows"]
+    loc = logits[v0:v1]
+    i = int(np.argmax(loc))
+    u = np.float32(loc[i]).view(np.uint32)
+    ordered = (~u if u & 0x80000000 else u | 0x80000000) & 0xFFFFFFFF
+    key = (int(ordered) << 32) | (0xFFFFFFFF - (v0 + i))
+    k = torch.tensor([key - (1 << 63)], dtype=torch.int64)  # signed, order preserved
+    dist.all_reduce(k, op=dist.ReduceOp.MAX)
+    best = 0xFFFFFFFF - ((int(k.item()) + (1 << 63)) & 0xFFFFFFFF)
+    out.put((rank, float(np.max(np.abs(t.numpy() - full))), best, int(np.argmax(logits))))
+    dist.destroy_process_group()
+
+
+def test_tensor_parallel_combine_on_two_cpu_ranks():
+    import multiprocessing as mp
+    import socket
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    procs = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, best, want in res:
+        assert err < 1e-9
+        assert best == want == 3
+
+
+# ------------------------------------------------------------------ GPU
+
+
+def _forced_oracle_logits(orc, w, prompt, ids):
+    """Oracle logits of one sequence fed its prompt and then the given ids
+    (teacher forcing), one row per step."""
+    m = orc.model(w)
+    m.reset()
+    h = None
+    for t in prompt:
+        h = m.decode(int(t))
+    out = []
+    for k in range(len(ids)):
+        lg, _ = m.logits(h)
+        out.append(lg)
+        h = m.decode(int(ids[k]))
+    return np.array(out)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,qtype,cfg", [
+    ("tiny-int8", 0, None), ("gqa-int4", 1, _cfg()), ("gqa-int8", 0, _cfg(vocab_size=999))])
+def test_batched_step_matches_oracle(gpu, orc, name, qtype, cfg):
+    if cfg is None:
+        wl = syn.WORKLOADS["tiny-int8"]
+        cfg = wl.model_config()
+    w = syn.build_model(cfg, qtype, 77, tied=name.startswith("gqa-int8"))
+    B, n, steps = 4, 5, 8
+    prompts = np.stack([syn.prompt_ids(cfg, 100 + b, n) for b in range(B)])
+    tp = nb.TPBatch(B, weights=w)
+    ids, logits, st = tp.generate(prompts, steps, want_logits=True)
+    assert st.generated_tokens == B * steps and st.prefill_tokens == B * n
+    dev = []
+    for b in range(B):
+        want = _forced_oracle_logits(orc, w, prompts[b], ids[b])
+        got = logits[:, b, :]
+        d = np.abs(got - want)
+        assert np.all(d <= ATOL + RTOL * np.abs(want)), (name, b, float(d.max()))
+        dev.append(d)
+        # the chosen ids are the first-index argmax of the returned logits
+        assert ids[b].tolist() == [int(np.argmax(got[k])) for k in range(steps)]
+    assert float(np.median(np.concatenate(dev))) <= MEDIAN
+    tp.close()
+
+
+@pytest.mark.gpu
+def test_batched_errors(gpu):
+    cfg = _cfg()
+    w = syn.build_model(cfg, 1, 3)
+    tp = nb.TPBatch(2, weights=w)
+    with pytest.raises(IndexError, match="token out of range"):
+        tp.generate(np.array([[1, 2], [3, 1000]], np.int32), 2)
+    with pytest.raises(ValueError, match="invalid prompt length"):
+        tp.generate(np.ones((2, 60), np.int32), 10)
+    with pytest.raises(ValueError, match="split evenly"):
+        nb.TPBatch(2, weights=w, world=3, rank=0, nccl_id=bytes(128))
+    tp.close()
+
+
+@pytest.mark.gpu
+def test_tensor_parallel_two_gpus(gpu):
+    if nb.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    r = subprocess.run(
+        [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+         "--master-addr", "127.0.0.1", "--master-port", "29533",
+         os.path.join(ROOT, "tests", "tp_worker.py")],
+        capture_output=True, text=True, timeout=600, cwd=ROOT,
+        env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "tensor parallel matches" in r.stdout
