@@ -21,7 +21,7 @@ __device__ __forceinline__ __half to_half_sat(float v) {
 
 inline int blocks_for(int64_t n, int t) { return int((n + t - 1) / t); }
 
-__global__ void add_rmsnorm_rows_kernel(float *h, const float *part, const float *w, int dim,
+__global__ void add_rmsnorm_rows_kernel(float *h, float *part, int add, const float *w, int dim,
                                         int Kp, __half *out) {
     __shared__ float red[32];
     const int b = blockIdx.x;
@@ -30,8 +30,12 @@ __global__ void add_rmsnorm_rows_kernel(float *h, const float *part, const float
     for (int k = threadIdx.x; k < dim; k += blockDim.x) {
         float v = x[k];
         if (part != nullptr) {
-            v += part[size_t(b) * dim + k];
-            x[k] = v;
+            float *pk = part + size_t(b) * dim + k;
+            if (add) {
+                v += *pk;
+                x[k] = v;
+            }
+            *pk = 0.0f; /* the next split-K GEMM adds into it */
         }
         ss = fmaf(v, v, ss);
     }
@@ -72,8 +76,8 @@ __global__ void rope_kv_batch_kernel(float *qkv, int B, int ldq, const int *pos_
         const float a = p[0], c = p[1];
         const float x0 = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(c, sn[i]));
         const float x1 = __fadd_rn(__fmul_rn(a, sn[i]), __fmul_rn(c, cs[i]));
-        p[0] = x0;
-        p[1] = x1;
+        p[0] = 0.0f; /* consumed: the next split-K GEMM adds into it */
+        p[1] = 0.0f;
         float *kc = kcache + ((seq + h) * max_seq + pos) * hd + 2 * i;
         kc[0] = x0;
         kc[1] = x1;
@@ -82,114 +86,135 @@ __global__ void rope_kv_batch_kernel(float *qkv, int B, int ldq, const int *pos_
     const int e = r2 - kv_heads * half;           /* value element */
     const int h = e / hd, d = e - h * hd;
     vcache[((seq + h) * max_seq + pos) * hd + d] = row[dq + kvd + e];
+    row[dq + kvd + e] = 0.0f;
 }
 
-/* One CTA of kAttWarps warps per (sequence, head).  A cached row of hd
- * floats is read by `lpr` lanes (the largest power of two dividing hd / 4;
- * float4 each, hd / (4 lpr) chunks per lane), so a warp covers 32 / lpr
- * positions per iteration and every row read is coalesced.  Scores go to shared memory, the softmax is
- * CTA-wide, and the context is accumulated per warp over its positions
- * (float4 per lane) and summed across the warps. */
-constexpr int kAttWarps = 4;
+/* One CTA of kAttWarps warps per (sequence, head), one pass over the
+ * positions with a running (maximum, sum, context) per row group: a cached
+ * row of hd floats is read by `lpr` lanes (the largest power of two
+ * dividing hd / 4; float4 each, hd / (4 lpr) chunks per lane), so a warp
+ * covers 32 / lpr positions per step and every row read is coalesced; U
+ * steps' key rows, then their value rows, are in flight together.  The row
+ * groups' states are merged at the end (m = max m_k, l = sum l_k e^(m_k -
+ * m), context = sum c_k e^(m_k - m) / l), which equals the reference's
+ * softmax over all positions up to rounding. */
+constexpr int kAttWarps = 8;
 
+template <int CPL>
 __global__ void __launch_bounds__(kAttWarps * 32)
 attention_batch_kernel(const float *qkv, int B, int ldq, const int *pos_p, const float *kcache,
                        const float *vcache, int layer, int heads, int kv_heads, int hd,
                        int max_seq, int Kp, __half *ctx) {
     extern __shared__ float sm[];
-    float *q = sm;                       /* [hd] */
-    float *part = q + hd;                /* [kAttWarps][hd] */
-    float *w = part + kAttWarps * hd;    /* [max_seq] */
-    __shared__ float red[32];
     const int b = blockIdx.x / heads, h = blockIdx.x - b * heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int npos = *pos_p + 1;
     const int g = h / (heads / kv_heads);
     const size_t base = ((size_t(layer) * B + b) * kv_heads + g) * size_t(max_seq) * hd;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x)
-        q[d] = qkv[size_t(b) * ldq + h * hd + d];
-    __syncthreads();
-    const int chunks = hd / 4;                       /* float4 per row */
-    int lpr = 32;                                    /* lanes per row: the largest */
-    while (chunks % lpr != 0)                        /* power of two dividing chunks */
-        lpr >>= 1;
-    const int cpl = chunks / lpr;                    /* chunks per lane (<= 8) */
-    const int rpi = 32 / lpr;                        /* rows per warp iteration */
+    const int lpr = hd / 4 / CPL;                    /* lanes per row (a power of two) */
+    const int rpi = 32 / lpr;                        /* rows per warp step */
     const int sub = lane / lpr, li = lane - sub * lpr;
+    const int nst = kAttWarps * rpi;                 /* row-group states */
+    float *q = sm;                                   /* [hd] */
+    float *st_c = q + hd;                            /* [nst][hd] */
+    float *st_m = st_c + size_t(nst) * hd;           /* [nst] */
+    float *st_l = st_m + nst;                        /* [nst] */
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float *src = const_cast<float *>(qkv) + size_t(b) * ldq + h * hd + d;
+        q[d] = *src;
+        *src = 0.0f; /* consumed: the next split-K GEMM adds into it */
+    }
+    __syncthreads();
     const float scale = 1.0f / sqrtf(float(hd));
-    const float4 *q4 = reinterpret_cast<const float4 *>(q);
-    float mx = -INFINITY;
-    for (int j0 = warp * rpi; j0 < npos; j0 += kAttWarps * rpi) {
-        const int j = j0 + sub;
-        float a = 0.0f;
-        if (j < npos) {
-            const float4 *kj = reinterpret_cast<const float4 *>(kcache + base + size_t(j) * hd);
-            for (int c = 0; c < cpl; c++) {
-                const float4 k4 = kj[li + c * lpr], x4 = q4[li + c * lpr];
-                a = fmaf(x4.x, k4.x, a);
-                a = fmaf(x4.y, k4.y, a);
-                a = fmaf(x4.z, k4.z, a);
-                a = fmaf(x4.w, k4.w, a);
+    float4 qv[CPL], acc[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        qv[c] = reinterpret_cast<const float4 *>(q)[li + c * lpr];
+        acc[c] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float m = -INFINITY, l = 0.0f;
+    constexpr int U = 4;
+    const int stride = kAttWarps * rpi;
+    for (int j0 = warp * rpi; j0 < npos; j0 += U * stride) {
+        /* the step's key and value rows, all loads issued together (rows
+         * past the end read row 0 and are masked) */
+        float4 kk[U][CPL], vv[U][CPL];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = j0 + u * stride + sub;
+            const size_t off = base + size_t(j < npos ? j : 0) * hd;
+            const float4 *kj = reinterpret_cast<const float4 *>(kcache + off);
+            const float4 *vj = reinterpret_cast<const float4 *>(vcache + off);
+#pragma unroll
+            for (int c = 0; c < CPL; c++) {
+                kk[u][c] = kj[li + c * lpr];
+                vv[u][c] = vj[li + c * lpr];
             }
         }
-        for (int o = lpr >> 1; o > 0; o >>= 1)
-            a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (li == 0 && j < npos) {
-            const float sc = a * scale;
-            w[j] = sc;
-            mx = fmaxf(mx, sc);
+        float sc[U], mn = m;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            float a = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CPL; c++) {
+                a = fmaf(qv[c].x, kk[u][c].x, a);
+                a = fmaf(qv[c].y, kk[u][c].y, a);
+                a = fmaf(qv[c].z, kk[u][c].z, a);
+                a = fmaf(qv[c].w, kk[u][c].w, a);
+            }
+            for (int o = lpr >> 1; o > 0; o >>= 1)
+                a += __shfl_xor_sync(0xffffffffu, a, o);
+            sc[u] = j0 + u * stride + sub < npos ? a * scale : -INFINITY;
+            mn = fmaxf(mn, sc[u]);
         }
-    }
-    mx = block_max(mx, red);
-    float sum = 0.0f;
-    for (int j = threadIdx.x; j < npos; j += blockDim.x) {
-        const float e = expf(w[j] - mx);
-        w[j] = e;
-        sum += e;
-    }
-    sum = block_sum(sum, red); /* its barriers also publish w[] */
-    float4 acc[8];
+        if (mn == -INFINITY)
+            continue; /* no position of this row group in the step */
+        const float corr = expf(m - mn); /* 0 while m is still -inf */
+        l *= corr;
 #pragma unroll
-    for (int c = 0; c < 8; c++)
-        acc[c] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int j0 = warp * rpi; j0 < npos; j0 += kAttWarps * rpi) {
-        const int j = j0 + sub;
-        if (j < npos) {
-            const float e = w[j];
-            const float4 *vj = reinterpret_cast<const float4 *>(vcache + base + size_t(j) * hd);
-#pragma unroll
-            for (int c = 0; c < 8; c++)
-                if (c < cpl) {
-                    const float4 v4 = vj[li + c * lpr];
-                    acc[c].x = fmaf(e, v4.x, acc[c].x);
-                    acc[c].y = fmaf(e, v4.y, acc[c].y);
-                    acc[c].z = fmaf(e, v4.z, acc[c].z);
-                    acc[c].w = fmaf(e, v4.w, acc[c].w);
-                }
+        for (int c = 0; c < CPL; c++) {
+            acc[c].x *= corr;
+            acc[c].y *= corr;
+            acc[c].z *= corr;
+            acc[c].w *= corr;
         }
-    }
-    /* rows handled by different `sub` groups of the warp: fold them */
-    for (int o = 16; o >= lpr; o >>= 1)
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            acc[c].x += __shfl_xor_sync(0xffffffffu, acc[c].x, o);
-            acc[c].y += __shfl_xor_sync(0xffffffffu, acc[c].y, o);
-            acc[c].z += __shfl_xor_sync(0xffffffffu, acc[c].z, o);
-            acc[c].w += __shfl_xor_sync(0xffffffffu, acc[c].w, o);
+        for (int u = 0; u < U; u++) {
+            const float p = expf(sc[u] - mn); /* 0 for masked rows */
+            l += p;
+#pragma unroll
+            for (int c = 0; c < CPL; c++) {
+                acc[c].x = fmaf(p, vv[u][c].x, acc[c].x);
+                acc[c].y = fmaf(p, vv[u][c].y, acc[c].y);
+                acc[c].z = fmaf(p, vv[u][c].z, acc[c].z);
+                acc[c].w = fmaf(p, vv[u][c].w, acc[c].w);
+            }
         }
-    if (sub == 0)
+        m = mn;
+    }
+    const int state = warp * rpi + sub;
+    if (li == 0) {
+        st_m[state] = m;
+        st_l[state] = l;
+    }
 #pragma unroll
-        for (int c = 0; c < 8; c++)
-            if (c < cpl)
-                reinterpret_cast<float4 *>(part + warp * hd)[li + c * lpr] = acc[c];
+    for (int c = 0; c < CPL; c++)
+        reinterpret_cast<float4 *>(st_c + size_t(state) * hd)[li + c * lpr] = acc[c];
     __syncthreads();
-    const float inv = 1.0f / sum;
+    float M = -INFINITY;
+    for (int k = 0; k < nst; k++)
+        M = fmaxf(M, st_m[k]);
     __half *out = ctx + size_t(b) * Kp + h * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float c = 0.0f;
-        for (int k = 0; k < kAttWarps; k++)
-            c += part[k * hd + d];
-        out[d] = to_half_sat(c * inv);
+        float L = 0.0f, c = 0.0f;
+        for (int k = 0; k < nst; k++) {
+            if (st_m[k] == -INFINITY)
+                continue;
+            const float f = expf(st_m[k] - M);
+            L = fmaf(st_l[k], f, L);
+            c = fmaf(st_c[size_t(k) * hd + d], f, c);
+        }
+        out[d] = to_half_sat(c / L);
     }
 }
 
@@ -202,7 +227,8 @@ __global__ void zero_cols_kernel(__half *x, int B, int from, int Kp) {
     x[b * Kp + from + (i - b * tail)] = to_half_sat(0.0f);
 }
 
-__global__ void argmax_keys_kernel(const float *logits, int V, int v0, unsigned long long *keys) {
+__global__ void argmax_keys_kernel(const float *logits, int V, int v0, unsigned long long *keys,
+                                   float *clear) {
     __shared__ unsigned long long best[32];
     const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float *row = logits + size_t(b) * V;
@@ -215,6 +241,9 @@ __global__ void argmax_keys_kernel(const float *logits, int V, int v0, unsigned 
         const unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
         k = c > k ? c : k;
     }
+    if (clear != nullptr) /* consumed: the next split-K GEMM adds into it */
+        for (int i = threadIdx.x; i < V; i += blockDim.x)
+            clear[size_t(b) * V + i] = 0.0f;
     if (lane == 0)
         best[warp] = k;
     __syncthreads();
@@ -296,10 +325,10 @@ __global__ void synth_int4_f16_kernel(uint64_t seed, uint64_t stream, float sigm
 
 } // namespace
 
-cudaError_t add_rmsnorm_rows(float *h, const float *part, const float *w, int B, int dim,
+cudaError_t add_rmsnorm_rows(float *h, float *part, bool add, const float *w, int B, int dim,
                              int Kp, uint16_t *out, cudaStream_t s) {
-    add_rmsnorm_rows_kernel<<<B, 256, 0, s>>>(h, part, w, dim, Kp,
-                                              reinterpret_cast<__half *>(out));
+    add_rmsnorm_rows_kernel<<<B, 1024, 0, s>>>(h, part, add ? 1 : 0, w, dim, Kp,
+                                               reinterpret_cast<__half *>(out));
     count_launches(1);
     return cudaGetLastError();
 }
@@ -316,29 +345,62 @@ cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const floa
     return cudaGetLastError();
 }
 
+template <int CPL>
+cudaError_t launch_attention(const float *qkv, int B, int ldq, const int *pos,
+                             const float *kcache, const float *vcache, int layer, int heads,
+                             int kv_heads, int hd, int max_seq, int Kp, __half *ctx, int lpr,
+                             cudaStream_t s) {
+    const size_t nst = size_t(kAttWarps) * size_t(32 / lpr);
+    const size_t smem = (size_t(hd) * (1 + nst) + 2 * nst) * sizeof(float);
+    auto k = attention_batch_kernel<CPL>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess)
+            return e;
+    }
+    k<<<B * heads, kAttWarps * 32, smem, s>>>(qkv, B, ldq, pos, kcache, vcache, layer, heads,
+                                              kv_heads, hd, max_seq, Kp, ctx);
+    return cudaGetLastError();
+}
+
 cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
                             const float *kcache, const float *vcache, int layer, int heads,
                             int kv_heads, int hd, int max_seq, int Kp, uint16_t *ctx,
                             cudaStream_t s) {
-    /* float4 rows, at most 8 float4 per lane */
+    /* float4 rows over lpr lanes (the largest power of two dividing
+     * hd / 4, at most 32), CPL float4 per lane */
     if (hd % 4 != 0 || hd <= 0)
         return cudaErrorInvalidValue;
     int lpr = 32;
     while ((hd / 4) % lpr != 0)
         lpr >>= 1;
-    if (hd / 4 / lpr > 8)
-        return cudaErrorInvalidValue;
-    const size_t smem = (size_t(hd) * (1 + kAttWarps) + size_t(max_seq)) * sizeof(float);
-    if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(
-            attention_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess)
-            return e;
-    }
+    const int cpl = hd / 4 / lpr;
     __half *c16 = reinterpret_cast<__half *>(ctx);
-    attention_batch_kernel<<<B * heads, kAttWarps * 32, smem, s>>>(
-        qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd, max_seq, Kp, c16);
+    cudaError_t e;
+    switch (cpl) {
+    case 1:
+        e = launch_attention<1>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
+                                max_seq, Kp, c16, lpr, s);
+        break;
+    case 2:
+        e = launch_attention<2>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
+                                max_seq, Kp, c16, lpr, s);
+        break;
+    case 3:
+        e = launch_attention<3>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
+                                max_seq, Kp, c16, lpr, s);
+        break;
+    case 4:
+        e = launch_attention<4>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
+                                max_seq, Kp, c16, lpr, s);
+        break;
+    default:
+        return cudaErrorInvalidValue;
+    }
     count_launches(1);
+    if (e != cudaSuccess)
+        return e;
     if (Kp > heads * hd) {
         const int64_t n = int64_t(B) * (Kp - heads * hd);
         zero_cols_kernel<<<blocks_for(n, 256), 256, 0, s>>>(c16, B, heads * hd, Kp);
@@ -348,8 +410,9 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
 }
 
 cudaError_t argmax_keys(const float *logits, int B, int V, int v0, unsigned long long *keys,
-                        cudaStream_t s) {
-    argmax_keys_kernel<<<B, 256, 0, s>>>(logits, V, v0, keys);
+                        bool clear, cudaStream_t s) {
+    argmax_keys_kernel<<<B, 256, 0, s>>>(logits, V, v0, keys,
+                                         clear ? const_cast<float *>(logits) : nullptr);
     count_launches(1);
     return cudaGetLastError();
 }

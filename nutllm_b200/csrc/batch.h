@@ -11,15 +11,17 @@
 
 namespace nut {
 
-/* h[b] += part[b] (when part is not null), then out[b][k] =
+/* h[b] += part[b] (when part is not null and add is set; part is then
+ * zeroed for the next split-K GEMM that adds into it), then out[b][k] =
  * fp16(rmsnorm(h[b]) * w) for k < dim and 0 for dim <= k < Kp
  * (src/ops.cpp:111-134, eps 1e-5). */
-cudaError_t add_rmsnorm_rows(float *h, const float *part, const float *w, int B, int dim,
+cudaError_t add_rmsnorm_rows(float *h, float *part, bool add, const float *w, int B, int dim,
                              int Kp, uint16_t *out, cudaStream_t s);
 
 /* RoPE (interleaved pairs, src/quant_model.cpp:26-37) of the q and k rows
  * of qkv [B][ldq] (q: heads * hd values, then k and v: kv_heads * hd each)
- * at position *pos, and the k and v rows appended to the batch cache. */
+ * at position *pos, and the k and v rows appended to the batch cache (their
+ * qkv entries are zeroed once cached, for the next split-K GEMM). */
 cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const float *rope_cos,
                           const float *rope_sin, int heads, int kv_heads, int hd,
                           float *kcache, float *vcache, int layer, int max_seq,
@@ -28,7 +30,8 @@ cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const floa
 /* Attention of every (sequence, head) at position *pos over cached
  * positions 0 .. *pos (attention_step, src/quant_model.cpp:68-105: scores
  * q.k / sqrt(hd), softmax, weighted values; GQA head -> kv head by
- * head / (heads / kv_heads)); context fp16 [B][Kp], zero padded. */
+ * head / (heads / kv_heads)); context fp16 [B][Kp], zero padded.  The q
+ * entries of qkv are zeroed once read. */
 cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
                             const float *kcache, const float *vcache, int layer, int heads,
                             int kv_heads, int hd, int max_seq, int Kp, uint16_t *ctx,
@@ -37,9 +40,10 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
 /* Per row b: the first-index argmax of logits[b][0, V) as a 64-bit key
  * (order-preserving value bits << 32 | ~(v0 + index)), so that the maximum
  * key over any split of the vocabulary is the global first-index argmax
- * (std::max_element, src/generate.cpp:28-30). */
+ * (std::max_element, src/generate.cpp:28-30).  With `clear` the logits are
+ * zeroed once read. */
 cudaError_t argmax_keys(const float *logits, int B, int V, int v0, unsigned long long *keys,
-                        cudaStream_t s);
+                        bool clear, cudaStream_t s);
 /* ids[b] = token of keys[b]; also appended to out[b * ld + step] when out
  * is not null. */
 cudaError_t keys_to_ids(const unsigned long long *keys, int B, int32_t *ids, int32_t *out,

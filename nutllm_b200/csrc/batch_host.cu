@@ -274,6 +274,12 @@ void alloc_state(nut_batch &b) {
     b.ostep = dev_alloc<int>(1, "alloc counters");
     b.gemm_error = dev_alloc<int>(1, "alloc error word");
     cuda_check(cudaMemset(b.gemm_error, 0, sizeof(int)), "clear error word");
+    /* GEMM outputs start at zero: each step's GEMMs add into them and their
+     * consumers zero them again */
+    cuda_check(cudaMemset(b.part, 0, B * b.dim * 4), "clear rows");
+    cuda_check(cudaMemset(b.qkv, 0, B * b.nqkv * 4), "clear rows");
+    cuda_check(cudaMemset(b.gu, 0, B * 2 * b.ffn_r * 4), "clear rows");
+    cuda_check(cudaMemset(b.logits, 0, B * b.vocab_r * 4), "clear rows");
     /* RoPE table with the reference's fp32 values (frequency and angle in
      * double, rounded once; src/quant_model.cpp:26-37) */
     const size_t half = size_t(b.hd / 2), S = size_t(b.max_seq);
@@ -417,9 +423,12 @@ void load_synthetic(nut_batch &b, uint64_t seed) {
     cudaFree(cls);
 }
 
+/* y[B][N] += x w^T; y holds zeros (every consumer of a GEMM output zeroes
+ * it once read), so the K dimension may be split over CTAs that add their
+ * partial products. */
 void gemm(nut_batch &b, const uint16_t *a, const uint16_t *w, int N, int K, float *y) {
     cuda_check(nut::gemm_f16(a, b.B, w, N, N, K, y, N, b.gemm_error, nut::kDefaultWaitNs,
-                             b.stream, false),
+                             b.stream, true, 8),
                "batch gemm");
 }
 
@@ -438,8 +447,10 @@ void forward(nut_batch &b) {
     cuda_check(nut::gather_rows(b.emb, b.ids, B, dim, int(b.cfg.vocab_size), b.h, s), "embed");
     for (int l = 0; l < b.layers; l++) {
         const nut_batch::Layer &L = b.L[size_t(l)];
-        cuda_check(nut::add_rmsnorm_rows(b.h, l == 0 ? nullptr : b.part, L.attn_norm, B, dim,
-                                         b.kp_dim, b.x16, s),
+        /* layer 0 starts from the embedding rows: the previous pass's
+         * last Wdown partial is only cleared */
+        cuda_check(nut::add_rmsnorm_rows(b.h, b.part, l > 0, L.attn_norm, B, dim, b.kp_dim,
+                                         b.x16, s),
                    "rmsnorm");
         gemm(b, b.x16, L.qkv, b.nqkv, b.kp_dim, b.qkv);
         cuda_check(nut::rope_kv_batch(b.qkv, B, b.nqkv, b.pos, b.rope_cos, b.rope_sin,
@@ -452,10 +463,11 @@ void forward(nut_batch &b) {
                    "attention");
         gemm(b, b.ctx16, L.wo, dim, b.kp_ctx, b.part);
         all_reduce_sum(b, b.part, size_t(B) * dim);
-        cuda_check(nut::add_rmsnorm_rows(b.h, b.part, L.ffn_norm, B, dim, b.kp_dim, b.x16, s),
+        cuda_check(nut::add_rmsnorm_rows(b.h, b.part, true, L.ffn_norm, B, dim, b.kp_dim,
+                                         b.x16, s),
                    "rmsnorm");
         gemm(b, b.x16, L.gu, 2 * b.ffn_r, b.kp_dim, b.gu);
-        cuda_check(nut::swiglu_rows(b.gu, B, b.ffn_r, b.kp_ffn, b.act16, s), "swiglu");
+        cuda_check(nut::swiglu_rows(b.gu, B, b.ffn_r, b.kp_ffn, b.act16, s, true), "swiglu");
         gemm(b, b.act16, L.down, dim, b.kp_ffn, b.part);
         all_reduce_sum(b, b.part, size_t(B) * dim);
     }
@@ -463,12 +475,14 @@ void forward(nut_batch &b) {
 
 /* Final norm, this rank's classifier rows, and the global first-index
  * argmax into b.ids (and b.out[:, *ostep]). */
-void head(nut_batch &b) {
+void head(nut_batch &b, bool keep_logits) {
     cudaStream_t s = b.stream;
-    cuda_check(nut::add_rmsnorm_rows(b.h, b.part, b.final_norm, b.B, b.dim, b.kp_dim, b.x16, s),
+    cuda_check(nut::add_rmsnorm_rows(b.h, b.part, true, b.final_norm, b.B, b.dim, b.kp_dim,
+                                     b.x16, s),
                "final norm");
     gemm(b, b.x16, b.lm, b.vocab_r, b.kp_dim, b.logits);
-    cuda_check(nut::argmax_keys(b.logits, b.B, b.vocab_r, b.v0, b.keys, s), "argmax");
+    cuda_check(nut::argmax_keys(b.logits, b.B, b.vocab_r, b.v0, b.keys, !keep_logits, s),
+               "argmax");
     if (b.world > 1)
         nccl_check(nccl().all_reduce(b.keys, b.keys, size_t(b.B), ncclUint64, ncclMax, b.comm, s),
                    "argmax all-reduce");
@@ -612,12 +626,15 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
                 cuda_check(nut::advance(b->pos, b->ostep, s), "advance");
                 forward(*b);
             }
-            head(*b);
-            if (logits != nullptr)
+            head(*b, logits != nullptr);
+            if (logits != nullptr) {
                 cuda_check(cudaMemcpyAsync(logits + size_t(k) * b->B * b->vocab_r, b->logits,
                                            size_t(b->B) * b->vocab_r * 4,
                                            cudaMemcpyDeviceToHost, s),
                            "copy logits");
+                cuda_check(cudaMemsetAsync(b->logits, 0, size_t(b->B) * b->vocab_r * 4, s),
+                           "clear logits");
+            }
         }
         cuda_check(cudaEventRecord(b->ev[2], s), "record event");
         if (steps > 0) {

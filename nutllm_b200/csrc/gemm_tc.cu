@@ -144,6 +144,7 @@ struct GemmArgs {
     int accumulate;    /* Y += A B^T instead of Y = A B^T */
     int *error;
     uint64_t limit_ns;
+    int splits;        /* K split over gridDim.z; > 1: Y += A B^T by atomic adds */
 };
 
 template <int BN, int STAGES>
@@ -173,7 +174,10 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     /* blockIdx.x walks the M tiles fastest, so the CTAs that share one B
      * (weight) tile run together and all but the first read it from L2 */
     const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-    const int kb_count = g.K / kBK;
+    /* this CTA's share of the K blocks (split-K over blockIdx.z) */
+    const int kb_total = g.K / kBK;
+    const int kb0 = int(blockIdx.z) * kb_total / g.splits;
+    const int kb_count = (int(blockIdx.z) + 1) * kb_total / g.splits - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -206,8 +210,8 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 }
                 uint8_t *a = tiles + s * S::kStage;
                 mbar_expect_tx(&full[s], uint32_t(S::kStage));
-                tma_load_2d(a, &tmA, kb * kBK, m0, &full[s]);
-                tma_load_2d(a + S::kA, &tmB, kb * kBK, n0, &full[s]);
+                tma_load_2d(a, &tmA, (kb0 + kb) * kBK, m0, &full[s]);
+                tma_load_2d(a + S::kA, &tmB, (kb0 + kb) * kBK, n0, &full[s]);
                 issued = kb + 1;
             }
             /* every issued copy has landed before the CTA can exit */
@@ -250,7 +254,23 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             for (int c = 0; c < BN; c += 16) {
                 float v[16];
                 tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c), v);
-                if (row < g.M) {
+                if (row < g.M && g.splits > 1) {
+                    /* split-K: every split adds its partial product */
+                    float *y = g.Y + size_t(row) * g.ldy + n0 + c;
+                    if (n0 + c + 16 <= g.N && (g.ldy % 4) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            asm volatile(
+                                "red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n"
+                                ::"l"(y + j), "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]),
+                                "f"(v[j + 3])
+                                : "memory");
+                    } else {
+                        for (int j = 0; j < 16; j++)
+                            if (n0 + c + j < g.N)
+                                atomicAdd(y + j, v[j]);
+                    }
+                } else if (row < g.M) {
                     float *y = g.Y + size_t(row) * g.ldy + n0 + c;
                     if (n0 + c + 16 <= g.N && (g.ldy % 4) == 0) {
 #pragma unroll
@@ -386,7 +406,7 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
     if (e != cudaSuccess)
         return e;
-    const dim3 grid((g.M + kBM - 1) / kBM, (g.N + BN - 1) / BN);
+    const dim3 grid((g.M + kBM - 1) / kBM, (g.N + BN - 1) / BN, g.splits);
     k<<<grid, kThreadsG, S::kBytes, stream>>>(a, b, g);
     count_launches(1);
     return cudaGetLastError();
@@ -417,7 +437,7 @@ cudaError_t round_f16(const float *x, int M, int K, int Kp, uint16_t *out, cudaS
 
 cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
                       float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream,
-                      bool accumulate) {
+                      bool accumulate, int max_splits) {
     if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0 ||
         (reinterpret_cast<uintptr_t>(A) & 15) != 0 || (reinterpret_cast<uintptr_t>(B) & 15) != 0)
         return cudaErrorInvalidValue;
@@ -430,10 +450,25 @@ cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_a
     int bn = 256;
     while (bn > 64 && mt * ((N + bn - 1) / bn) < sms)
         bn /= 2;
+    /* split K (at least 4 K blocks per split) so that the CTAs fill their
+     * waves best: one CTA per SM, so a grid of t CTAs runs ceil(t / sms)
+     * waves; the fewest splits within 2 % of the best fill win (each split
+     * adds its partial product atomically) */
+    int splits = 1;
+    const int tiles = mt * ((N + bn - 1) / bn), kbs = K / kBK;
+    double best = 0.0;
+    for (int sp = 1; sp <= max_splits && kbs / sp >= 4; sp++) {
+        const int t = tiles * sp, waves = (t + sms - 1) / sms;
+        const double fill = double(t) / double(waves * sms);
+        if (fill > best + 0.02) {
+            best = fill;
+            splits = sp;
+        }
+    }
     CUtensorMap ma, mb;
     if (!encode_map(&ma, A, M, K, kBM) || !encode_map(&mb, B, N_alloc, K, bn))
         return cudaErrorInvalidValue;
-    const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns};
+    const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, splits};
     if (bn == 256)
         return launch_bn<256, 4>(ma, mb, g, stream);
     if (bn == 128)

@@ -23,10 +23,14 @@ cudaError_t launch_qmatvec_tc(const TileMatrix &m, const float *x, float *y,
 
 /* Prefill GEMM (gemm_tc.cu).  Y[M][N] (row stride ldy, fp32) =
  * A[M][K] B[N][K]^T with fp16 operands (K a multiple of 64, B allocated
- * with N_alloc >= N rows); device-side timeouts land in *error. */
+ * with N_alloc >= N rows); device-side timeouts land in *error.  With
+ * max_splits > 1 the K dimension may be split over up to that many CTAs
+ * per output tile (when the tiles alone fill their waves poorly), each
+ * adding its partial product atomically: Y then receives Y + A B^T, so the
+ * caller zeroes Y first unless it accumulates. */
 cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_alloc, int K,
                      float *Y, int ldy, int *error, uint64_t limit_ns, cudaStream_t stream,
-                     bool accumulate = false);
+                     bool accumulate = false, int max_splits = 1);
 /* Fragment tiles (any tile order) -> fp16 [row_tiles * 16][blocks * 32]. */
 cudaError_t dequant_tiles_f16(const TileMatrix &m, uint16_t *out, cudaStream_t stream);
 /* fp32 [M][K] -> fp16 [M][Kp], zero padded, saturating. */

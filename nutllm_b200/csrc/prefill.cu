@@ -173,7 +173,8 @@ __global__ void zero_tail_kernel(__half *x, int M, int dim, int Kp) {
     x[m * Kp + dim + (i - m * tail)] = to_half_sat(0.0f);
 }
 
-__global__ void swiglu_rows_kernel(const float *gu, int M, int ffn, int Kp, __half *act) {
+__global__ void swiglu_rows_kernel(const float *gu, int M, int ffn, int Kp, __half *act,
+                                   int clear) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= int64_t(M) * Kp)
         return;
@@ -181,10 +182,15 @@ __global__ void swiglu_rows_kernel(const float *gu, int M, int ffn, int Kp, __ha
     const int u = int(i - m * Kp);
     float a = 0.0f;
     if (u < ffn) {
-        const float *row = gu + size_t(m) * 2 * ffn;
+        float *row = const_cast<float *>(gu) + size_t(m) * 2 * ffn;
         const float gte = row[(u / 8) * 16 + (u % 8)];
         const float up = row[(u / 8) * 16 + 8 + (u % 8)];
         a = gte / (1.0f + expf(-gte)) * up;
+        if (clear) { /* each gate/up value has one reader: zero it for the
+                        next GEMM that adds into the rows */
+            row[(u / 8) * 16 + (u % 8)] = 0.0f;
+            row[(u / 8) * 16 + 8 + (u % 8)] = 0.0f;
+        }
     }
     act[i] = to_half_sat(a);
 }
@@ -241,9 +247,10 @@ cudaError_t attention_rows(const float *qkv, int M, int ldq, int start, const fl
     return cudaGetLastError();
 }
 
-cudaError_t swiglu_rows(const float *gu, int M, int ffn, int Kp, uint16_t *act, cudaStream_t s) {
+cudaError_t swiglu_rows(const float *gu, int M, int ffn, int Kp, uint16_t *act, cudaStream_t s,
+                        bool clear_src) {
     swiglu_rows_kernel<<<blocks_for(int64_t(M) * Kp, 256), 256, 0, s>>>(
-        gu, M, ffn, Kp, reinterpret_cast<__half *>(act));
+        gu, M, ffn, Kp, reinterpret_cast<__half *>(act), clear_src ? 1 : 0);
     count_launches(1);
     return cudaGetLastError();
 }

@@ -22,7 +22,9 @@ size_t attention_rows_smem(int hd, int max_seq);
 cudaError_t attention_rows(const float *qkv, int M, int ldq, int start, const float *kcache,
                            const float *vcache, int layer, int heads, int kv_heads, int hd,
                            int dim, int max_seq, int Kp, uint16_t *ctx, cudaStream_t s);
-/* act fp16 [M][Kp] = silu(gate) * up from gu [M][2 ffn] (groups of 8). */
-cudaError_t swiglu_rows(const float *gu, int M, int ffn, int Kp, uint16_t *act, cudaStream_t s);
+/* act fp16 [M][Kp] = silu(gate) * up from gu [M][2 ffn] (groups of 8);
+ * with clear_src the gate/up values are zeroed once read. */
+cudaError_t swiglu_rows(const float *gu, int M, int ffn, int Kp, uint16_t *act, cudaStream_t s,
+                        bool clear_src = false);
 
 } // namespace nut
