@@ -26,6 +26,7 @@
 
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -179,6 +180,12 @@ struct nut_batch {
     int *gemm_error = nullptr;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     uint64_t weight_bytes = 0; /* fp16 weights + fp32 tensors this rank holds */
+    /* one captured prompt pass and one captured decode pass (their
+     * positions and counters live in device memory, so a replay serves
+     * every step); built on first use */
+    cudaGraphExec_t g_prompt = nullptr, g_decode = nullptr;
+    int g_prompt_n = 0;
+    uint64_t g_prompt_kernels = 0, g_decode_kernels = 0;
 
     ~nut_batch() {
         if (stream == nullptr)
@@ -204,6 +211,10 @@ struct nut_batch {
         for (cudaEvent_t e : ev)
             if (e)
                 cudaEventDestroy(e);
+        if (g_prompt)
+            cudaGraphExecDestroy(g_prompt);
+        if (g_decode)
+            cudaGraphExecDestroy(g_decode);
         if (comm)
             nccl().comm_destroy(comm);
         if (stream)
@@ -503,6 +514,52 @@ void check_gemm_error(nut_batch &b) {
     }
 }
 
+/* Captures `body` (work enqueued on b.stream) as an executable graph;
+ * *kernels receives how many of this library's kernels it holds. */
+template <typename F> cudaGraphExec_t capture(nut_batch &b, uint64_t *kernels, F &&body) {
+    cudaGraph_t graph = nullptr;
+    const uint64_t before = nut::launches_so_far();
+    cuda_check(cudaStreamBeginCapture(b.stream, cudaStreamCaptureModeRelaxed), "begin capture");
+    try {
+        body();
+    } catch (...) {
+        cudaStreamEndCapture(b.stream, &graph);
+        if (graph)
+            cudaGraphDestroy(graph);
+        throw;
+    }
+    cuda_check(cudaStreamEndCapture(b.stream, &graph), "end capture");
+    *kernels = nut::launches_so_far() - before;
+    nut::uncount_launches(*kernels); /* captured, not launched */
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    cuda_check(e, "instantiate graph");
+    return exec;
+}
+
+/* The prompt pass (next prompt column, forward, advance) and the decode
+ * pass (advance, forward, head) as graphs. */
+void ensure_graphs(nut_batch &b, int n) {
+    if (b.g_prompt == nullptr || b.g_prompt_n != n) {
+        if (b.g_prompt)
+            cudaGraphExecDestroy(b.g_prompt);
+        b.g_prompt = capture(b, &b.g_prompt_kernels, [&] {
+            cuda_check(nut::prompt_column(b.prompts, b.B, n, b.pstep, b.ids, b.stream),
+                       "prompt");
+            forward(b);
+            cuda_check(nut::advance(b.pos, b.pstep, b.stream), "advance");
+        });
+        b.g_prompt_n = n;
+    }
+    if (b.g_decode == nullptr)
+        b.g_decode = capture(b, &b.g_decode_kernels, [&] {
+            cuda_check(nut::advance(b.pos, b.ostep, b.stream), "advance");
+            forward(b);
+            head(b, false);
+        });
+}
+
 nut_status create(const nut_config *config, const nut_model_view *view, uint64_t seed,
                   int device, int64_t batch, int rank, int world, const uint8_t *nccl_id,
                   nut_batch **out) {
@@ -609,11 +666,20 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
         cuda_check(cudaMemsetAsync(b->pos, 0, sizeof(int), s), "reset position");
         cuda_check(cudaMemsetAsync(b->pstep, 0, sizeof(int), s), "reset position");
         cuda_check(cudaMemsetAsync(b->ostep, 0, sizeof(int), s), "reset position");
-        std::vector<float> lg;
+        /* replayed graphs unless logits are copied out every step */
+        const bool graphs = logits == nullptr && std::getenv("NUTLLM_NO_GRAPHS") == nullptr;
+        if (graphs)
+            ensure_graphs(*b, int(n));
         cuda_check(cudaEventRecord(b->ev[0], s), "record event");
         /* the prompt, one position per pass (its classifier only after the
-         * last prompt token) */
+         * last prompt token); the pass before the last advances the
+         * position, so the last runs at n - 1 */
         for (int64_t t = 0; t < n; t++) {
+            if (graphs && t + 1 < n) {
+                cuda_check(cudaGraphLaunch(b->g_prompt, s), "replay prompt pass");
+                nut::count_launches(unsigned(b->g_prompt_kernels));
+                continue;
+            }
             cuda_check(nut::prompt_column(b->prompts, b->B, int(n), b->pstep, b->ids, s),
                        "prompt");
             forward(*b);
@@ -622,6 +688,11 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
         }
         cuda_check(cudaEventRecord(b->ev[1], s), "record event");
         for (int64_t k = 0; k < steps; k++) {
+            if (graphs && k > 0) {
+                cuda_check(cudaGraphLaunch(b->g_decode, s), "replay decode pass");
+                nut::count_launches(unsigned(b->g_decode_kernels));
+                continue;
+            }
             if (k > 0) {
                 cuda_check(nut::advance(b->pos, b->ostep, s), "advance");
                 forward(*b);

@@ -39,6 +39,8 @@ std::atomic<uint64_t> g_launches{0};
 }
 
 void nut::count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+uint64_t nut::launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
+void nut::uncount_launches(uint64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
 
 namespace {
 

@@ -14,6 +14,10 @@ void set_last_error(const std::string &message);
 /* Adds n to the process-wide count of kernels this library has launched
  * (read through nut_launch_count). */
 void count_launches(unsigned n);
+/* The counter itself, and a correction for kernels that were captured
+ * into a graph rather than launched (their replays count them instead). */
+uint64_t launches_so_far();
+void uncount_launches(uint64_t n);
 
 /* fp32 products in the reference build's order (fp32_ops.cu):
  * C[M][N] = A[M][K] B[K][N] (fused, k-sequential) and y = W x (unfused,

@@ -198,3 +198,21 @@ def test_tensor_parallel_two_gpus(gpu):
         env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "tensor parallel matches" in r.stdout
+
+
+@pytest.mark.gpu
+def test_graph_replay_matches_direct_launches(gpu):
+    """Without logits the prompt and decode passes are replayed CUDA graphs;
+    they choose the same ids as the directly launched passes."""
+    cfg = _cfg()
+    w = syn.build_model(cfg, 1, 91)
+    B, n, steps = 4, 6, 10
+    prompts = np.stack([syn.prompt_ids(cfg, 500 + b, n) for b in range(B)])
+    tp = nb.TPBatch(B, weights=w)
+    direct, _, _ = tp.generate(prompts, steps, want_logits=True)
+    l0 = nb.launch_count()
+    graph1, _, _ = tp.generate(prompts, steps)
+    graph2, _, _ = tp.generate(prompts, steps)
+    assert nb.launch_count() > l0  # replays are counted
+    tp.close()
+    assert graph1.tolist() == graph2.tolist() == direct.tolist()
