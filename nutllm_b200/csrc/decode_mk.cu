@@ -56,7 +56,7 @@
 namespace nut {
 namespace {
 
-constexpr int W = 15;            /* consumer warps (16 per CTA with the producer: 128 registers each) */
+constexpr int W = 8;             /* consumer warps (9 per CTA with the producer) */
 constexpr int NT = W * 32;       /* consumer threads */
 constexpr int THREADS = NT + 32; /* + the producer warp */
 constexpr int kBar = 1;          /* named barrier of the consumer warps */
