@@ -321,6 +321,12 @@ def run_batch_tp(args, rank, world, local):
         nccl_id = box[0]
     tp = nb.TPBatch(B, rank=rank, world=world, nccl_id=nccl_id, config=cfg, seed=SEED,
                     device=local)
+    allreduce = "nccl"
+    if world > 1 and os.environ.get("NUTLLM_TP_ALLREDUCE", "peer") == "peer":
+        handles = [None] * world
+        _pg.all_gather_object(handles, tp.ipc_handle())
+        tp.open_peers(handles)
+        allreduce = "peer"
     rng = np.random.default_rng(SEED)
     prompts = rng.integers(1, cfg.vocab_size, size=(B, n)).astype(np.int32)
     warmup = max(args.warmup, 3)
@@ -368,6 +374,7 @@ def run_batch_tp(args, rank, world, local):
                 "N(0,0.02) embeddings and classifier, uniform prompt ids)",
         "config": {"workload": args.workload, "layers": cfg.layers, "batch": B, "prompt": n,
                    "decode_steps": steps, "parallelism": f"tp{world}",
+                   "all_reduce": allreduce if world > 1 else None,
                    "l2": "inputs larger than L2 (every decode step reads the weights and "
                          "KV cache, several GB, from HBM)",
                    "timing": "CUDA events on the library stream around prefill and decode"},

@@ -250,6 +250,13 @@ void nut_batch_destroy(nut_batch *batch);
  * rows (all of this rank), weight bytes held, world}. */
 nut_status nut_batch_info(const nut_batch *batch, int64_t *info);
 nut_status nut_batch_stream(nut_batch *batch, void **stream);
+/* Peer-memory all-reduce in place of NCCL for the Wo and Wdown sums: each
+ * rank exports an IPC handle of its receive area (size >= 64 bytes per
+ * handle), the ranks exchange them (e.g. an all-gather on the host), and
+ * each opens everyone's handles [world][stride bytes].  Collective, world
+ * <= 8, one process per GPU; the argmax still uses NCCL. */
+nut_status nut_batch_ipc_handle(nut_batch *batch, uint8_t *handle, int64_t size);
+nut_status nut_batch_open_peers(nut_batch *batch, const uint8_t *handles, int64_t stride);
 /* This rank's shard without creating anything (host only): shard[8] =
  * {first head, heads, first kv head, kv heads, first ffn unit, ffn units,
  * first vocabulary row, vocabulary rows}. */

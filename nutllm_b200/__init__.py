@@ -178,6 +178,8 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_batch_destroy", [_P], None)
         _declare(lib, "nut_batch_info", [_P, _PI64])
         _declare(lib, "nut_tp_shard", [C.POINTER(Config), C.c_int, C.c_int, _PI64])
+        _declare(lib, "nut_batch_ipc_handle", [_P, _P, _I64])
+        _declare(lib, "nut_batch_open_peers", [_P, _P, _I64])
         _declare(lib, "nut_batch_stream", [_P, C.POINTER(_P)])
         _declare(lib, "nut_batch_generate", [_P, _P, _I64, _I64, _P, _P,
                                              C.POINTER(GenerationStats)])
@@ -535,6 +537,19 @@ class TPBatch:
             self.config = Config(**config.as_dict())
         self.handle = h
         self.batch, self.rank, self.world = batch, rank, world
+
+    def ipc_handle(self) -> bytes:
+        """This rank's receive-area handle for the peer-memory all-reduce."""
+        buf = (C.c_uint8 * 64)()
+        _check(cuda_lib().nut_batch_ipc_handle(self.handle, buf, 64))
+        return bytes(buf)
+
+    def open_peers(self, handles: list) -> None:
+        """Switches the Wo/Wdown sums from NCCL to the peer-memory all-reduce
+        (handles: every rank's ipc_handle(), in rank order).  Collective."""
+        blob = b"".join(h[:64].ljust(64, b"\0") for h in handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _check(cuda_lib().nut_batch_open_peers(self.handle, buf, 64))
 
     def info(self) -> dict:
         v = (C.c_int64 * 8)()

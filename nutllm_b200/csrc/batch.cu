@@ -454,3 +454,109 @@ cudaError_t synth_int4_f16_dev(uint64_t seed, uint64_t stream, float sigma, int 
 }
 
 } // namespace nut
+
+namespace nut {
+namespace {
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct PeerPtrs {
+    float *recv[8];
+    unsigned *flags[8];
+};
+
+__global__ void __launch_bounds__(256)
+peer_all_reduce_kernel(const float *x, float *out, int n, PeerPtrs pp, int rank, int world,
+                       unsigned *epochs, int *error, uint64_t limit_ns) {
+    const int c = blockIdx.x;
+    const int per = (n / 4 + kArChunks - 1) / kArChunks; /* float4 per chunk */
+    const int f0 = c * per, f1 = min(n / 4, f0 + per);
+    __shared__ unsigned epoch_s;
+    __shared__ int failed;
+    if (threadIdx.x == 0) {
+        epoch_s = epochs[c] + 1;
+        failed = 0;
+    }
+    __syncthreads();
+    const unsigned e = epoch_s;
+    const size_t slot = size_t(e & 1u) * size_t(world) * size_t(n);
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    /* push this rank's chunk into every rank's receive area */
+    for (int i = f0 + int(threadIdx.x); i < f1; i += blockDim.x) {
+        const float4 v = x4[i];
+        for (int q = 0; q < world; q++)
+            reinterpret_cast<float4 *>(pp.recv[q] + slot + size_t(rank) * n)[i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system(); /* the chunk's stores before its flags */
+        for (int q = 0; q < world; q++)
+            st_release_sys(pp.flags[q] + size_t(rank) * kArChunks + c, e);
+    }
+    /* wait for chunk c of every rank (thread q polls rank q's flag) */
+    if (int(threadIdx.x) < world) {
+        const unsigned *f = pp.flags[rank] + size_t(threadIdx.x) * kArChunks + c;
+        if (ld_acquire_sys(f) != e) {
+            const uint64_t t0 = now_ns();
+            while (ld_acquire_sys(f) != e) {
+                if (now_ns() - t0 > limit_ns) {
+                    atomicExch(&failed, 1);
+                    atomicCAS(error, 0, 1);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (!failed) {
+        /* read through L2: the peers wrote these lines over NVLink */
+        const float *mine = pp.recv[rank] + slot;
+        for (int i = f0 + int(threadIdx.x); i < f1; i += blockDim.x) {
+            float4 a = __ldcg(reinterpret_cast<const float4 *>(mine) + i);
+            for (int q = 1; q < world; q++) {
+                const float4 b = __ldcg(reinterpret_cast<const float4 *>(mine + size_t(q) * n) + i);
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+            }
+            reinterpret_cast<float4 *>(out)[i] = a;
+        }
+    }
+    if (threadIdx.x == 0)
+        epochs[c] = e;
+}
+
+} // namespace
+
+cudaError_t peer_all_reduce(const float *x, float *out, int n, float *const *recv,
+                            unsigned *const *flags, int rank, int world, unsigned *epochs,
+                            int *error, uint64_t limit_ns, cudaStream_t s) {
+    if (world < 1 || world > 8 || n % 4 != 0 || rank < 0 || rank >= world)
+        return cudaErrorInvalidValue;
+    PeerPtrs pp{};
+    for (int q = 0; q < world; q++) {
+        pp.recv[q] = recv[q];
+        pp.flags[q] = flags[q];
+    }
+    peer_all_reduce_kernel<<<kArChunks, 256, 0, s>>>(x, out, n, pp, rank, world, epochs, error,
+                                                     limit_ns);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+} // namespace nut

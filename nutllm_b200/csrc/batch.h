@@ -65,3 +65,22 @@ cudaError_t synth_int4_f16_dev(uint64_t seed, uint64_t stream, float sigma, int 
                                int ld, uint16_t *out, cudaStream_t s);
 
 } // namespace nut
+
+namespace nut {
+
+/* One-shot all-reduce (sum, fp32) of n floats over `world` ranks through
+ * peer memory (NVLink), one call per rank, every rank with the same n and
+ * the same sequence of calls.  Rank r's receive area recv[r] is
+ * [2][world][n] floats (double-buffered by call parity) and its flags
+ * [world][chunks] words; recv and flags hold every rank's pointers (IPC
+ * mappings of the peers', this rank's own).  CTA c pushes chunk c of x into
+ * every rank's area with plain stores, fences at system scope, raises its
+ * flag on every rank, waits (bounded by limit_ns; *error = 1 on timeout)
+ * for chunk c of every rank and writes their sum, in rank order, to out.
+ * epochs [chunks] counts this rank's calls per chunk. */
+constexpr int kArChunks = 128;
+cudaError_t peer_all_reduce(const float *x, float *out, int n, float *const *recv,
+                            unsigned *const *flags, int rank, int world, unsigned *epochs,
+                            int *error, uint64_t limit_ns, cudaStream_t s);
+
+} // namespace nut

@@ -178,6 +178,16 @@ struct nut_batch {
     int32_t *ids = nullptr, *out = nullptr, *prompts = nullptr;
     int *pos = nullptr, *pstep = nullptr, *ostep = nullptr; /* device counters */
     int *gemm_error = nullptr;
+    /* peer-memory all-reduce: this rank's area ([2][world][B dim] floats,
+     * then [world][kArChunks] flags), the peers' areas (IPC mappings), the
+     * per-chunk call counters and the error word */
+    uint8_t *peer_area = nullptr;
+    std::vector<void *> peer_open;
+    float *recv_ptrs[8] = {};
+    unsigned *flag_ptrs[8] = {};
+    unsigned *ar_epochs = nullptr;
+    int *ar_error = nullptr;
+    bool peers = false;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     uint64_t weight_bytes = 0; /* fp16 weights + fp32 tensors this rank holds */
     /* one captured prompt pass and one captured decode pass (their
@@ -200,6 +210,11 @@ struct nut_batch {
                             (void *)l.attn_norm, (void *)l.ffn_norm})
                 if (p)
                     cudaFree(p);
+        for (void *p : peer_open)
+            cudaIpcCloseMemHandle(p);
+        for (void *p : {(void *)peer_area, (void *)ar_epochs, (void *)ar_error})
+            if (p)
+                cudaFree(p);
         for (void *p : {(void *)emb, (void *)final_norm, (void *)rope_cos, (void *)rope_sin,
                         (void *)lm, (void *)kcache, (void *)vcache, (void *)h, (void *)part,
                         (void *)qkv, (void *)gu, (void *)logits, (void *)x16, (void *)ctx16,
@@ -444,9 +459,21 @@ void gemm(nut_batch &b, const uint16_t *a, const uint16_t *w, int N, int K, floa
 }
 
 void all_reduce_sum(nut_batch &b, float *x, size_t n) {
-    if (b.world > 1)
+    if (b.world == 1)
+        return;
+    if (b.peers)
+        cuda_check(nut::peer_all_reduce(x, x, int(n), b.recv_ptrs, b.flag_ptrs, b.rank,
+                                        b.world, b.ar_epochs, b.ar_error, nut::kDefaultWaitNs,
+                                        b.stream),
+                   "peer all-reduce");
+    else
         nccl_check(nccl().all_reduce(x, x, n, ncclFloat32, ncclSum, b.comm, b.stream),
                    "all-reduce");
+}
+
+size_t peer_area_bytes(const nut_batch &b) {
+    return size_t(2) * b.world * size_t(b.B) * b.dim * 4 +
+           size_t(b.world) * nut::kArChunks * 4;
 }
 
 /* One forward pass of the batch: token ids in b.ids at position *b.pos,
@@ -501,11 +528,17 @@ void head(nut_batch &b, bool keep_logits) {
 }
 
 void check_gemm_error(nut_batch &b) {
-    int code = 0;
+    int code = 0, ar = 0;
     cuda_check(cudaMemcpyAsync(&code, b.gemm_error, sizeof code, cudaMemcpyDeviceToHost,
                                b.stream),
                "read error word");
+    if (b.peers)
+        cuda_check(cudaMemcpyAsync(&ar, b.ar_error, sizeof ar, cudaMemcpyDeviceToHost,
+                                   b.stream),
+                   "read error word");
     cuda_check(cudaStreamSynchronize(b.stream), "synchronize");
+    if (ar != 0)
+        raise(NUT_DEVICE_TIMEOUT, "tensor parallel: a peer all-reduce wait gave up");
     if (code != 0) {
         cudaMemsetAsync(b.gemm_error, 0, sizeof(int), b.stream);
         cudaStreamSynchronize(b.stream);
@@ -626,6 +659,64 @@ nut_status nut_tp_shard(const nut_config *config, int rank, int world, int64_t *
         const int64_t v[8] = {int64_t(rank) * b.heads_r, b.heads_r, int64_t(rank) * b.kvh_r,
                               b.kvh_r, int64_t(rank) * b.ffn_r, b.ffn_r, b.v0, b.vocab_r};
         std::memcpy(shard, v, sizeof v);
+    });
+}
+
+nut_status nut_batch_ipc_handle(nut_batch *b, uint8_t *handle, int64_t size) {
+    return guarded([&] {
+        if (b == nullptr || handle == nullptr || size < int64_t(sizeof(cudaIpcMemHandle_t)))
+            raise(NUT_INVALID_ARGUMENT, "tensor parallel: handle buffer too small");
+        DeviceScope scope(b->device);
+        if (b->peer_area == nullptr) {
+            const size_t bytes = peer_area_bytes(*b);
+            b->peer_area = dev_alloc<uint8_t>(bytes, "alloc peer area");
+            cuda_check(cudaMemset(b->peer_area, 0, bytes), "clear peer area");
+            b->ar_epochs = dev_alloc<unsigned>(nut::kArChunks, "alloc epochs");
+            cuda_check(cudaMemset(b->ar_epochs, 0, nut::kArChunks * 4), "clear epochs");
+            b->ar_error = dev_alloc<int>(1, "alloc error word");
+            cuda_check(cudaMemset(b->ar_error, 0, sizeof(int)), "clear error word");
+            cuda_check(cudaDeviceSynchronize(), "clear peer area");
+        }
+        cudaIpcMemHandle_t h;
+        cuda_check(cudaIpcGetMemHandle(&h, b->peer_area), "ipc handle");
+        std::memcpy(handle, &h, sizeof h);
+    });
+}
+
+nut_status nut_batch_open_peers(nut_batch *b, const uint8_t *handles, int64_t stride) {
+    return guarded([&] {
+        if (b == nullptr || handles == nullptr || stride < int64_t(sizeof(cudaIpcMemHandle_t)))
+            raise(NUT_INVALID_ARGUMENT, "tensor parallel: invalid handles");
+        if (b->peer_area == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "tensor parallel: export this rank's handle first");
+        if (b->world > 8)
+            raise(NUT_INVALID_ARGUMENT, "tensor parallel: peer all-reduce takes at most 8 ranks");
+        DeviceScope scope(b->device);
+        const size_t recv_bytes = size_t(2) * b->world * size_t(b->B) * b->dim * 4;
+        for (int q = 0; q < b->world; q++) {
+            uint8_t *base = b->peer_area;
+            if (q != b->rank) {
+                cudaIpcMemHandle_t h;
+                std::memcpy(&h, handles + size_t(q) * size_t(stride), sizeof h);
+                void *p = nullptr;
+                cuda_check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess),
+                           "open peer memory");
+                b->peer_open.push_back(p);
+                base = static_cast<uint8_t *>(p);
+            }
+            b->recv_ptrs[q] = reinterpret_cast<float *>(base);
+            b->flag_ptrs[q] = reinterpret_cast<unsigned *>(base + recv_bytes);
+        }
+        b->peers = true;
+        /* graphs captured before hold NCCL calls: capture again */
+        if (b->g_prompt) {
+            cudaGraphExecDestroy(b->g_prompt);
+            b->g_prompt = nullptr;
+        }
+        if (b->g_decode) {
+            cudaGraphExecDestroy(b->g_decode);
+            b->g_decode = nullptr;
+        }
     });
 }
 

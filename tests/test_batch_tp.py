@@ -197,7 +197,7 @@ def test_tensor_parallel_two_gpus(gpu):
         capture_output=True, text=True, timeout=600, cwd=ROOT,
         env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "tensor parallel matches" in r.stdout
+    assert "tensor parallel matches" in r.stdout and "peer all-reduce matches" in r.stdout
 
 
 @pytest.mark.gpu

@@ -33,6 +33,15 @@ def main():
     ids, logits, _ = tp.generate(prompts, steps, want_logits=True)
     parts = [None] * world
     dist.all_gather_object(parts, (tp.info()["vocab0"], logits))
+    # the same run with the Wo / Wdown sums through peer memory, with and
+    # without graph replay
+    handles = [None] * world
+    dist.all_gather_object(handles, tp.ipc_handle())
+    tp.open_peers(handles)
+    ids_p, logits_p, _ = tp.generate(prompts, steps, want_logits=True)
+    ids_g, _, _ = tp.generate(prompts, steps)
+    parts_p = [None] * world
+    dist.all_gather_object(parts_p, (tp.info()["vocab0"], logits_p))
     tp.close()
     if rank == 0:
         full = np.concatenate([p[1] for p in sorted(parts, key=lambda x: x[0])], axis=2)
@@ -43,6 +52,12 @@ def main():
         assert np.all(d <= 1e-3 + 1e-3 * np.abs(logits1)), float(d.max())
         assert ids.tolist() == [[int(np.argmax(full[k, b])) for k in range(steps)]
                                 for b in range(B)]
+        full_p = np.concatenate([p[1] for p in sorted(parts_p, key=lambda x: x[0])], axis=2)
+        dp = np.abs(full_p - logits1)
+        assert np.all(dp <= 1e-3 + 1e-3 * np.abs(logits1)), float(dp.max())
+        assert ids_p.tolist() == ids_g.tolist() == [
+            [int(np.argmax(full_p[k, b])) for k in range(steps)] for b in range(B)]
+        print(f"peer all-reduce matches: max |diff| {float(dp.max()):.2e}")
         print(f"tensor parallel matches: max |diff| {float(d.max()):.2e}, "
               f"ids equal to one rank: {ids.tolist() == ids1.tolist()}")
     dist.barrier()
