@@ -322,7 +322,9 @@ def run_batch_tp(args, rank, world, local):
     tp = nb.TPBatch(B, rank=rank, world=world, nccl_id=nccl_id, config=cfg, seed=SEED,
                     device=local)
     allreduce = "nccl"
-    if world > 1 and os.environ.get("NUTLLM_TP_ALLREDUCE", "peer") == "peer":
+    # NCCL (NVLS where it is available) by default; the one-shot peer-memory
+    # all-reduce measured slower at 4 and 8 ranks
+    if world > 1 and os.environ.get("NUTLLM_TP_ALLREDUCE", "nccl") == "peer":
         handles = [None] * world
         _pg.all_gather_object(handles, tp.ipc_handle())
         tp.open_peers(handles)
