@@ -307,6 +307,37 @@ def tp_decode_bytes(cfg, batch, prompt, steps, world):
     return (lin + cls + kv) / world + norms
 
 
+def cpu_estimate_tp(spec, reps=3):
+    """The reference's CPU decode of the 7B shape at batch 1 (its own
+    kernels, all host threads), bounded: one layer's projections timed with
+    matvec_quantized_threaded (Wq, Wk, Wv, Wo, Wgate, Wup, Wdown shapes) times
+    the layer count, plus the fp32 classifier with matvec_threaded.  Attention
+    and norms (under 2 % of a token's bytes at these lengths) are not timed."""
+    import oracle
+    threads = os.cpu_count() or 1
+    if not oracle.reference_available():
+        return None, threads, "oracle/_ref not built"
+    cfg = spec["cfg"]
+    d, f, L, V = cfg["dim"], cfg["ffn_dim"], cfg["layers"], cfg["vocab_size"]
+    kvd = cfg["kv_heads"] * cfg["head_dim"]
+    r = oracle.Reference()
+    rng = np.random.default_rng(SEED)
+    per_layer = 0.0
+    shapes = {(d, d): 2, (kvd, d): 2, (f, d): 2, (d, f): 1}
+    for (rows, cols), count in shapes.items():
+        w = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02)
+        data, scales = r.quantize(w, 1)
+        x = rng.standard_normal(cols, dtype=np.float32)
+        sec, _ = r.qmatvec_time(1, rows, cols, data, scales, x, threads, reps)
+        per_layer += count * sec
+    cls = rng.standard_normal((V, d), dtype=np.float32) * 0.02
+    head = r.matvec_time(cls, rng.standard_normal(d, dtype=np.float32), threads, reps)
+    token = L * per_layer + head
+    sample = (f"batch 1: one layer's quantised projections ({reps} timed calls each) "
+              f"x {L} layers + the fp32 classifier, reference kernels, {threads} threads")
+    return 1.0 / token, threads, sample
+
+
 def run_batch_tp(args, rank, world, local):
     import torch
     import nutllm_b200 as nb
@@ -355,6 +386,11 @@ def run_batch_tp(args, rank, world, local):
     tp.close()
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_estimate_tp(spec)
+        cpu = {"value": round(v, 3) if v else None, "unit": "decode tok/s (batch 1)",
+               "cores": cores, "kind": "reference", "sample": sample}
     value = B * steps * args.steps / dec_s
     step_s = dec_s / (args.steps * steps)
     peak, src = measured_peaks()
@@ -391,7 +427,7 @@ def run_batch_tp(args, rank, world, local):
                      "frac": round(ach / peak, 4), "peak_source": src,
                      "algorithmic_bytes_per_step_per_rank": int(per_rank),
                      "weight_bytes_held_per_rank": info["weight_bytes"], "traffic": None},
-        "cpu_baseline": None,
+        "cpu_baseline": cpu,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -625,8 +661,33 @@ def cpu_baseline(wl, c):
 # ------------------------------------------------------------- reference
 
 
+def run_reference_tp(args, world):
+    spec = TP_WORKLOADS[args.workload]
+    # one set of matrices, each matvec timed over `steps` calls
+    value, cores, sample = cpu_estimate_tp(spec, reps=max(args.steps, 1))
+    if value is None:
+        print(json.dumps({"impl": "reference", "unavailable": sample}))
+        return
+    print(json.dumps({
+        "impl": "reference",
+        "metric": f"decode tok/s (Llama-2-7B INT4 shape, batch {spec['batch']}, tensor parallel)",
+        "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 / value, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int4xfp32", "data": "synthetic",
+        "config": {"workload": args.workload, "batch": 1,
+                   "note": "the reference generates one sequence at a time"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": cores,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
+        return
+    if args.workload in TP_WORKLOADS:
+        run_reference_tp(args, world)
         return
     import oracle
     from nutllm_b200 import synthetic as syn
