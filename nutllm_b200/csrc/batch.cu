@@ -11,6 +11,7 @@
 #include "batch.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "kernels_tc.h"
 
 namespace nut {
 namespace {
@@ -323,7 +324,60 @@ __global__ void synth_int4_f16_kernel(uint64_t seed, uint64_t stream, float sigm
     out[i] = __float2half_rn(float(q) * s);
 }
 
+/* One thread per packed 32-bit word of nibbles (8 consecutive k, in the
+ * packed order k0 k2 k4 k6 k1 k3 k5 k7, each q + 8 with q = hash % 15 - 7)
+ * or per scale byte (scales as in synth_int4_f16_kernel). */
+__global__ void synth_q4_packed_kernel(uint64_t seed, uint64_t stream, float sigma, int rows,
+                                       int cols, int kbs, uint8_t *out) {
+    constexpr int kWords = kQ4Rows * 8, kScaleBytes = kQ4Rows * 4;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int tiles = (rows + kQ4Rows - 1) / kQ4Rows;
+    if (i >= int64_t(tiles) * kbs * (kWords + kScaleBytes))
+        return;
+    const int64_t stage = i / (kWords + kScaleBytes);
+    const int off = int(i - stage * (kWords + kScaleBytes));
+    const int nt = int(stage / kbs), kb = int(stage - int64_t(nt) * kbs);
+    uint8_t *st = out + stage * kQ4StageBytes;
+    const float unit = sigma * 2.5f / 7.0f;
+    if (off < kWords) {
+        const int r = off / 8, wd = off % 8, row = nt * kQ4Rows + r;
+        const int k0 = kb * 64 + wd * 8;
+        uint32_t word = 0x88888888u; /* q = 0 */
+        if (row < rows && k0 + 8 <= cols) {
+            word = 0;
+            for (int k = 0; k < 8; k++) {
+                const uint32_t q8 =
+                    uint32_t(element_hash(seed, stream, uint64_t(row) * cols + k0 + k) % 15u) + 1u;
+                const int slot = (k & 1) ? 4 + k / 2 : k / 2;
+                word |= q8 << (4 * slot); /* q + 8 with q in [-7, 7] */
+            }
+        }
+        reinterpret_cast<uint32_t *>(st)[off] = word;
+    } else {
+        const int sb = off - kWords;
+        const int j = sb / 2, byte = sb % 2;
+        const int r = j / 2, h = j % 2, row = nt * kQ4Rows + r, blk = kb * 2 + h;
+        uint16_t bits = 0;
+        if (row < rows && (blk + 1) * 32 <= cols) {
+            const uint64_t hs = element_hash(seed, stream ^ 0x5CA1Eull, uint64_t(row) * cols + blk);
+            bits = __half_as_ushort(__float2half_rn(
+                unit * (0.75f + 0.5f * float(uint32_t(hs >> 40)) * (1.0f / 16777216.0f))));
+        }
+        st[kQ4Rows * 32 + sb] = byte == 0 ? uint8_t(bits & 0xFF) : uint8_t(bits >> 8);
+    }
+}
+
 } // namespace
+
+cudaError_t synth_q4_packed_dev(uint64_t seed, uint64_t stream, float sigma, int rows,
+                                int cols, int K, uint8_t *out, cudaStream_t s) {
+    const int kbs = K / 64, tiles = (rows + kQ4Rows - 1) / kQ4Rows;
+    const int64_t n = int64_t(tiles) * kbs * (kQ4Rows * 8 + kQ4Rows * 4);
+    synth_q4_packed_kernel<<<blocks_for(n, 256), 256, 0, s>>>(seed, stream, sigma, rows, cols,
+                                                              kbs, out);
+    count_launches(1);
+    return cudaGetLastError();
+}
 
 cudaError_t add_rmsnorm_rows(float *h, float *part, bool add, const float *w, int B, int dim,
                              int Kp, uint16_t *out, cudaStream_t s) {

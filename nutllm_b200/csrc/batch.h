@@ -63,6 +63,11 @@ cudaError_t synth_normal_dev(uint64_t seed, uint64_t stream, float sigma, float 
                              cudaStream_t s);
 cudaError_t synth_int4_f16_dev(uint64_t seed, uint64_t stream, float sigma, int rows, int cols,
                                int ld, uint16_t *out, cudaStream_t s);
+/* The same random INT4 block-32 matrix [rows][cols] written directly in the
+ * packed layout of gemm_q4 (K = cols rounded up to 64, zero past cols and
+ * rows). */
+cudaError_t synth_q4_packed_dev(uint64_t seed, uint64_t stream, float sigma, int rows,
+                                int cols, int K, uint8_t *out, cudaStream_t s);
 
 } // namespace nut
 

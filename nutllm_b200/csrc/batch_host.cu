@@ -165,9 +165,11 @@ struct nut_batch {
     cudaStream_t stream = nullptr;
     ncclComm_t comm = nullptr;
     struct Layer {
-        uint16_t *qkv = nullptr, *wo = nullptr, *gu = nullptr, *down = nullptr;
+        uint16_t *qkv = nullptr, *wo = nullptr, *gu = nullptr, *down = nullptr; /* fp16 */
+        uint8_t *qkv4 = nullptr, *wo4 = nullptr, *gu4 = nullptr, *down4 = nullptr; /* INT4 */
         float *attn_norm = nullptr, *ffn_norm = nullptr;
     };
+    bool q4 = false; /* projections as packed INT4 (gemm_q4) rather than fp16 copies */
     std::vector<Layer> L;
     float *emb = nullptr, *final_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     uint16_t *lm = nullptr;
@@ -207,6 +209,7 @@ struct nut_batch {
             cudaStreamSynchronize(stream);
         for (Layer &l : L)
             for (void *p : {(void *)l.qkv, (void *)l.wo, (void *)l.gu, (void *)l.down,
+                            (void *)l.qkv4, (void *)l.wo4, (void *)l.gu4, (void *)l.down4,
                             (void *)l.attn_norm, (void *)l.ffn_norm})
                 if (p)
                     cudaFree(p);
@@ -339,8 +342,18 @@ float *upload_f32(const float *src, size_t n, uint64_t &bytes) {
     return p;
 }
 
+/* INT4 projections stay packed and are dequantised inside the GEMM
+ * pipeline when NUTLLM_BATCH_Q4=1.  Off by default: that pipeline is
+ * latency-bound at its 64-row stages (~0.58 us per 64-wide K block against
+ * ~0.35 us for the fp16 copies), so the fp16 copies are faster today in
+ * spite of 3.6x the weight bytes. */
+bool use_q4() {
+    const char *v = std::getenv("NUTLLM_BATCH_Q4");
+    return v != nullptr && v[0] == '1';
+}
+
 /* This rank's shard of a host model (the reference's storage), dequantised
- * to fp16 on the host. */
+ * to fp16 on the host (or packed INT4, see use_q4). */
 void load_view(nut_batch &b, const nut_model_view &v) {
     const nut_config &c = b.cfg;
     if (v.n_layers != c.layers || v.layers == nullptr || v.embeddings == nullptr ||
@@ -349,6 +362,30 @@ void load_view(nut_batch &b, const nut_model_view &v) {
     const int dim = b.dim, hd = b.hd;
     const int q0 = b.rank * b.heads_r * hd, k0 = b.rank * b.kvh_r * hd;
     const int kvd_r = b.kvh_r * hd, f0 = b.rank * b.ffn_r;
+    /* packed INT4 needs whole quant blocks in every slice */
+    b.q4 = v.quant_type == NUT_QUANT_INT4 && use_q4() && dim % 32 == 0 &&
+           (b.heads_r * hd) % 32 == 0;
+    /* the listed (matrix, row) pairs, columns [c0, c0 + n), as contiguous
+     * INT4 storage packed for gemm_q4 */
+    auto pack_rows = [&](const std::vector<std::pair<const nut_qmatrix_view *, int>> &rows,
+                         int c0, int n, int K) {
+        std::vector<uint8_t> data(rows.size() * size_t(n / 2));
+        std::vector<uint16_t> sc(rows.size() * size_t(n / 32));
+        for (size_t r = 0; r < rows.size(); r++) {
+            const nut_qmatrix_view &m = *rows[r].first;
+            const int64_t src = rows[r].second;
+            std::memcpy(data.data() + r * (n / 2), m.data + (src * m.cols + c0) / 2, n / 2);
+            std::memcpy(sc.data() + r * (n / 32), m.scales + (src * m.cols + c0) / 32,
+                        (n / 32) * 2);
+        }
+        std::vector<uint8_t> packed(nut::q4_packed_bytes(int(rows.size()), K));
+        nut::pack_q4(data.data(), sc.data(), int(rows.size()), n, K, packed.data());
+        uint8_t *p = dev_alloc<uint8_t>(packed.size(), "alloc packed weights");
+        cuda_check(cudaMemcpy(p, packed.data(), packed.size(), cudaMemcpyHostToDevice),
+                   "copy packed weights");
+        b.weight_bytes += packed.size();
+        return p;
+    };
     for (int l = 0; l < b.layers; l++) {
         const nut_layer_view &lv = v.layers[l];
         for (const nut_qmatrix_view *m : {&lv.query, &lv.key, &lv.value, &lv.output, &lv.gate,
@@ -356,6 +393,34 @@ void load_view(nut_batch &b, const nut_model_view &v) {
             if (m->data == nullptr || m->scales == nullptr || m->block_size != 32 ||
                 m->type != v.quant_type)
                 raise(NUT_INVALID_ARGUMENT, "model: invalid matrix view");
+        if (b.q4) {
+            nut_batch::Layer &d = b.L[size_t(l)];
+            std::vector<std::pair<const nut_qmatrix_view *, int>> rows;
+            for (int r = 0; r < b.heads_r * hd; r++)
+                rows.push_back({&lv.query, q0 + r});
+            for (int r = 0; r < kvd_r; r++)
+                rows.push_back({&lv.key, k0 + r});
+            for (int r = 0; r < kvd_r; r++)
+                rows.push_back({&lv.value, k0 + r});
+            d.qkv4 = pack_rows(rows, 0, dim, b.kp_dim);
+            rows.clear();
+            for (int r = 0; r < dim; r++)
+                rows.push_back({&lv.output, r});
+            d.wo4 = pack_rows(rows, q0, b.heads_r * hd, b.kp_ctx);
+            rows.clear();
+            for (int r = 0; r < 2 * b.ffn_r; r++) {
+                const int group = r / 16, within = r % 16;
+                rows.push_back({within >= 8 ? &lv.up : &lv.gate, f0 + group * 8 + within % 8});
+            }
+            d.gu4 = pack_rows(rows, 0, dim, b.kp_dim);
+            rows.clear();
+            for (int r = 0; r < dim; r++)
+                rows.push_back({&lv.down, r});
+            d.down4 = pack_rows(rows, f0, b.ffn_r, b.kp_ffn);
+            d.attn_norm = upload_f32(lv.attention_norm, size_t(dim), b.weight_bytes);
+            d.ffn_norm = upload_f32(lv.ffn_norm, size_t(dim), b.weight_bytes);
+            continue;
+        }
         std::vector<uint16_t> qkv(size_t(b.nqkv) * b.kp_dim, 0);
         for (int r = 0; r < b.nqkv; r++) {
             const nut_qmatrix_view *m;
@@ -423,9 +488,26 @@ void load_synthetic(nut_batch &b, uint64_t seed) {
         b.weight_bytes += size_t(rows) * ld * 2;
         return p;
     };
+    auto make4 = [&](int rows, int cols, int K, uint64_t id) {
+        const size_t bytes = nut::q4_packed_bytes(rows, K);
+        uint8_t *p = dev_alloc<uint8_t>(bytes, "alloc packed weights");
+        cuda_check(nut::synth_q4_packed_dev(seed, id, sigma, rows, cols, K, p, s), "synth");
+        b.weight_bytes += bytes;
+        return p;
+    };
+    b.q4 = use_q4();
     std::vector<float> ones(size_t(dim), 1.0f);
     for (int l = 0; l < b.layers; l++) {
         nut_batch::Layer &d = b.L[size_t(l)];
+        if (b.q4) {
+            d.qkv4 = make4(b.nqkv, dim, b.kp_dim, stream_id(l, 0));
+            d.wo4 = make4(dim, b.heads_r * b.hd, b.kp_ctx, stream_id(l, 1));
+            d.gu4 = make4(2 * b.ffn_r, dim, b.kp_dim, stream_id(l, 2));
+            d.down4 = make4(dim, b.ffn_r, b.kp_ffn, stream_id(l, 3));
+            d.attn_norm = upload_f32(ones.data(), size_t(dim), b.weight_bytes);
+            d.ffn_norm = upload_f32(ones.data(), size_t(dim), b.weight_bytes);
+            continue;
+        }
         d.qkv = make(b.nqkv, dim, b.kp_dim, stream_id(l, 0));
         d.wo = make(dim, b.heads_r * b.hd, b.kp_ctx, stream_id(l, 1));
         d.gu = make(2 * b.ffn_r, dim, b.kp_dim, stream_id(l, 2));
@@ -456,6 +538,17 @@ void gemm(nut_batch &b, const uint16_t *a, const uint16_t *w, int N, int K, floa
     cuda_check(nut::gemm_f16(a, b.B, w, N, N, K, y, N, b.gemm_error, nut::kDefaultWaitNs,
                              b.stream, true, 8),
                "batch gemm");
+}
+
+/* A projection: packed INT4 weights through gemm_q4, or the fp16 copy. */
+void proj(nut_batch &b, const uint16_t *a, const uint16_t *w16, const uint8_t *w4, int N, int K,
+          float *y) {
+    if (b.q4)
+        cuda_check(nut::gemm_q4(a, b.B, w4, N, K, y, N, b.gemm_error, nut::kDefaultWaitNs,
+                                b.stream, true, 8),
+                   "batch gemm");
+    else
+        gemm(b, a, w16, N, K, y);
 }
 
 void all_reduce_sum(nut_batch &b, float *x, size_t n) {
@@ -490,7 +583,7 @@ void forward(nut_batch &b) {
         cuda_check(nut::add_rmsnorm_rows(b.h, b.part, l > 0, L.attn_norm, B, dim, b.kp_dim,
                                          b.x16, s),
                    "rmsnorm");
-        gemm(b, b.x16, L.qkv, b.nqkv, b.kp_dim, b.qkv);
+        proj(b, b.x16, L.qkv, L.qkv4, b.nqkv, b.kp_dim, b.qkv);
         cuda_check(nut::rope_kv_batch(b.qkv, B, b.nqkv, b.pos, b.rope_cos, b.rope_sin,
                                       b.heads_r, b.kvh_r, b.hd, b.kcache, b.vcache, l,
                                       b.max_seq, s),
@@ -499,14 +592,14 @@ void forward(nut_batch &b) {
                                         b.heads_r, b.kvh_r, b.hd, b.max_seq, b.kp_ctx, b.ctx16,
                                         s),
                    "attention");
-        gemm(b, b.ctx16, L.wo, dim, b.kp_ctx, b.part);
+        proj(b, b.ctx16, L.wo, L.wo4, dim, b.kp_ctx, b.part);
         all_reduce_sum(b, b.part, size_t(B) * dim);
         cuda_check(nut::add_rmsnorm_rows(b.h, b.part, true, L.ffn_norm, B, dim, b.kp_dim,
                                          b.x16, s),
                    "rmsnorm");
-        gemm(b, b.x16, L.gu, 2 * b.ffn_r, b.kp_dim, b.gu);
+        proj(b, b.x16, L.gu, L.gu4, 2 * b.ffn_r, b.kp_dim, b.gu);
         cuda_check(nut::swiglu_rows(b.gu, B, b.ffn_r, b.kp_ffn, b.act16, s, true), "swiglu");
-        gemm(b, b.act16, L.down, dim, b.kp_ffn, b.part);
+        proj(b, b.act16, L.down, L.down4, dim, b.kp_ffn, b.part);
         all_reduce_sum(b, b.part, size_t(B) * dim);
     }
 }

@@ -397,6 +397,235 @@ bool encode_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols_e
     return r == CUDA_SUCCESS;
 }
 
+/* ---- INT4 weights dequantised in the pipeline ----------------------
+
+   Y[M][N] (+)= X[M][K] W[N][K]^T with W kept as INT4 block-32 weights in a
+   packed layout: for every 64-row tile n and 64-wide K block kb, 64 rows of
+   32 bytes (the row's 64 nibbles) then 64 x 2 fp16 scale bits (kQ4Stage
+   bytes in all, one contiguous bulk copy).  Each 32-bit word holds 8
+   consecutive k in the nibble order k0 k2 k4 k6 k1 k3 k5 k7 (bits 0-3 =
+   k0, ..., 28-31 = k7), offset by 8 (q + 8, 0..15), so that
+   ((w >> 4j) & 0x000F000F) | 0x64006400 is the half2 (1024 + q_2j + 8,
+   1024 + q_2j+1 + 8): one subtraction of 1032 gives the exact pair and one
+   half2 multiply by the block scale gives q * scale rounded once to fp16,
+   the value dequant_tiles_f16 produces.  Per stage:
+     warp 4 (one lane)  TMA load of the fp16 X tile (128 x 64) and a bulk copy
+                        of the W stage into a staging area, both completing on
+                        the stage's "full" barrier
+     warps 0-3          dequantise the staged stage: thread t expands row t/2,
+                        quant block t%2 (32 nibbles), to fp16 q * scale (the
+                        rounding of dequant_tiles_f16), written in the 128-byte
+                        swizzle the MMA descriptor reads; a proxy fence makes
+                        the stores visible to the tensor core, then one arrive
+                        per warp on the stage's "ready" barrier
+     warp 5             waits "full" and "ready", issues the MMAs, commits
+                        to "empty"
+   and warps 0-3 run the usual epilogue after the last stage. */
+constexpr int kQ4N = kQ4Rows;                     /* weight rows per tile */
+constexpr int kQ4Bytes = kQ4N * 32;               /* nibbles per stage */
+constexpr int kQ4Stage = kQ4StageBytes;           /* + scales */
+static_assert(kQ4Stage == kQ4Bytes + kQ4N * 2 * 2, "packed INT4 stage layout");
+
+template <int STAGES>
+struct Q4Smem {
+    static constexpr int kA = kBM * kBK * 2;  /* 16 KB */
+    static constexpr int kB = kQ4N * kBK * 2; /* 8 KB */
+    static constexpr int kTile = kA + kB;     /* 1024-byte multiple */
+    static constexpr size_t kBytes =
+        size_t(STAGES) * (kTile + kQ4Stage) + 1024 /* align */ + 512;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreadsG, 1)
+gemm_q4_kernel(const __grid_constant__ CUtensorMap tmA, const uint8_t *wq, const GemmArgs g) {
+    using S = Q4Smem<STAGES>;
+    constexpr int BN = kQ4N;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *tiles = smem;                                 /* [STAGES][A | B] */
+    uint8_t *staging = smem + STAGES * S::kTile;           /* [STAGES][kQ4Stage] */
+    uint64_t *full = reinterpret_cast<uint64_t *>(staging + STAGES * kQ4Stage);
+    uint64_t *ready = full + STAGES;
+    uint64_t *empty = ready + STAGES;
+    uint64_t *accum = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kBM, nt = blockIdx.y, n0 = nt * BN;
+    const int kb_total = g.K / kBK;
+    const int kb0 = int(blockIdx.z) * kb_total / g.splits;
+    const int kb_count = (int(blockIdx.z) + 1) * kb_total / g.splits - kb0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], kEpiWarps);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kEpiWarps + 1)
+        tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kEpiWarps) {
+        /* producer */
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < kb_count; kb++) {
+                const int s = kb % STAGES;
+                const uint32_t par = uint32_t((kb / STAGES) & 1);
+                if (kb >= STAGES &&
+                    (*abort_flag || !mbar_wait(&empty[s], par ^ 1u, g.limit_ns))) {
+                    atomicCAS(g.error, 0, kGemmErrEmpty);
+                    *abort_flag = 1;
+                    break;
+                }
+                uint8_t *a = tiles + s * S::kTile;
+                mbar_expect_tx(&full[s], uint32_t(S::kA + kQ4Stage));
+                tma_load_2d(a, &tmA, (kb0 + kb) * kBK, m0, &full[s]);
+                bulk_g2s(staging + s * kQ4Stage,
+                         wq + (size_t(nt) * kb_total + size_t(kb0 + kb)) * kQ4Stage,
+                         uint32_t(kQ4Stage), &full[s]);
+                issued = kb + 1;
+            }
+            for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
+                mbar_wait(&full[kb % STAGES], uint32_t((kb / STAGES) & 1), g.limit_ns);
+        }
+    } else if (warp == kEpiWarps + 1) {
+        /* MMA issuer */
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(kBM, BN);
+            for (int kb = 0; kb < kb_count; kb++) {
+                const int s = kb % STAGES;
+                const uint32_t par = uint32_t((kb / STAGES) & 1);
+                if (*abort_flag || !mbar_wait(&full[s], par, g.limit_ns) ||
+                    !mbar_wait(&ready[s], par, g.limit_ns)) {
+                    atomicCAS(g.error, 0, kGemmErrFull);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(tiles + s * S::kTile), b = a + S::kA;
+#pragma unroll
+                for (int k = 0; k < kBK / 16; k++)
+                    umma_f16(tmem, smem_desc_sw128(a + k * 32), smem_desc_sw128(b + k * 32),
+                             idesc, (kb | k) != 0);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(accum);
+        }
+        __syncwarp();
+    } else {
+        /* dequantisers: thread t owns row t / 2, quant block t % 2 */
+        const int t = threadIdx.x, r = t >> 1, h = t & 1;
+        for (int kb = 0; kb < kb_count; kb++) {
+            const int s = kb % STAGES;
+            const uint32_t par = uint32_t((kb / STAGES) & 1);
+            bool ok = !*abort_flag && mbar_wait(&full[s], par, g.limit_ns);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicCAS(g.error, 0, kGemmErrFull);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            const uint8_t *st = staging + s * kQ4Stage;
+            const uint4 q = *reinterpret_cast<const uint4 *>(st + r * 32 + h * 16);
+            const uint16_t sbits = reinterpret_cast<const uint16_t *>(st + kQ4Bytes)[r * 2 + h];
+            const __half2 sc2 = __halves2half2(__ushort_as_half(sbits), __ushort_as_half(sbits));
+            const __half2 bias = __halves2half2(__ushort_as_half(0x6408),
+                                                __ushort_as_half(0x6408)); /* 1032 */
+            uint8_t *brow = tiles + s * S::kTile + S::kA + r * 128;
+            const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                /* 8 values k = 32 h + 8 c .. + 7 from one 32-bit word */
+                const uint32_t w = words[c];
+                uint32_t packed[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t bits = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+                    const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&bits),
+                                                      bias),
+                                              sc2);
+                    packed[j] = *reinterpret_cast<const uint32_t *>(&v);
+                }
+                const int chunk = (4 * h + c) ^ (r & 7);
+                *reinterpret_cast<uint4 *>(brow + chunk * 16) =
+                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&ready[s]);
+        }
+        /* epilogue: warp w owns TMEM lanes (rows) 32 w .. 32 w + 31 */
+        bool ok = mbar_wait(accum, 0u, g.limit_ns);
+        if (!ok)
+            atomicCAS(g.error, 0, kGemmErrAccum);
+        ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+        tc_fence_after();
+        const int row = m0 + warp * 32 + lane;
+        if (ok) {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float v[16];
+                tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c), v);
+                if (row >= g.M)
+                    continue;
+                float *y = g.Y + size_t(row) * g.ldy + n0 + c;
+                const bool vec = n0 + c + 16 <= g.N && (g.ldy % 4) == 0;
+                if (g.splits > 1 && vec) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4)
+                        asm volatile(
+                            "red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n"
+                            ::"l"(y + j), "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]),
+                            "f"(v[j + 3])
+                            : "memory");
+                } else if (g.splits > 1) {
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c + j < g.N)
+                            atomicAdd(y + j, v[j]);
+                } else if (vec) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        if (g.accumulate) {
+                            const float4 p = *reinterpret_cast<const float4 *>(y + j);
+                            o.x += p.x, o.y += p.y, o.z += p.z, o.w += p.w;
+                        }
+                        *reinterpret_cast<float4 *>(y + j) = o;
+                    }
+                } else {
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c + j < g.N)
+                            y[j] = g.accumulate ? y[j] + v[j] : v[j];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
 template <int BN, int STAGES>
 cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs &g,
                       cudaStream_t stream) {
@@ -408,6 +637,21 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs
         return e;
     const dim3 grid((g.M + kBM - 1) / kBM, (g.N + BN - 1) / BN, g.splits);
     k<<<grid, kThreadsG, S::kBytes, stream>>>(a, b, g);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+template <int STAGES>
+cudaError_t launch_q4(const CUtensorMap &a, const uint8_t *wq, const GemmArgs &g,
+                      cudaStream_t stream) {
+    using S = Q4Smem<STAGES>;
+    auto k = gemm_q4_kernel<STAGES>;
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
+    if (e != cudaSuccess)
+        return e;
+    const dim3 grid((g.M + kBM - 1) / kBM, (g.N + kQ4N - 1) / kQ4N, g.splits);
+    k<<<grid, kThreadsG, S::kBytes, stream>>>(a, wq, g);
     count_launches(1);
     return cudaGetLastError();
 }
@@ -474,6 +718,80 @@ cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_a
     if (bn == 128)
         return launch_bn<128, 6>(ma, mb, g, stream);
     return launch_bn<64, 8>(ma, mb, g, stream);
+}
+
+size_t q4_packed_bytes(int N, int K) {
+    return size_t((N + kQ4N - 1) / kQ4N) * size_t(K / kBK) * size_t(kQ4Stage);
+}
+
+void pack_q4(const uint8_t *data, const uint16_t *scales, int N, int K_src, int K,
+             uint8_t *out) {
+    const int tiles = (N + kQ4N - 1) / kQ4N, kbs = K / kBK;
+    for (int nt = 0; nt < tiles; nt++)
+        for (int kb = 0; kb < kbs; kb++) {
+            uint8_t *st = out + (size_t(nt) * kbs + kb) * kQ4Stage;
+            uint16_t *ss = reinterpret_cast<uint16_t *>(st + kQ4Bytes);
+            for (int r = 0; r < kQ4N; r++) {
+                const int row = nt * kQ4N + r;
+                for (int h = 0; h < 2; h++) {
+                    const int blk = kb * 2 + h; /* quant block within the row */
+                    const bool in = row < N && (blk + 1) * 32 <= K_src;
+                    uint8_t *dst = st + r * 32 + h * 16;
+                    if (in) {
+                        /* reference order: element k in byte k / 2, even k in
+                         * the low nibble; packed: per word of 8 values the
+                         * order k0 k2 k4 k6 k1 k3 k5 k7, offset by 8 */
+                        const uint8_t *src = data + size_t(row) * (K_src / 2) + blk * 16;
+                        for (int wd = 0; wd < 4; wd++) {
+                            uint32_t word = 0;
+                            for (int k = 0; k < 8; k++) {
+                                const uint8_t byte = src[wd * 4 + k / 2];
+                                const uint32_t nib = ((k & 1) ? byte >> 4 : byte) & 0xFu;
+                                const uint32_t off = (nib ^ 8u) & 0xFu; /* q + 8 */
+                                const int slot = (k & 1) ? 4 + k / 2 : k / 2;
+                                word |= off << (4 * slot);
+                            }
+                            for (int i = 0; i < 4; i++)
+                                dst[wd * 4 + i] = uint8_t(word >> (8 * i));
+                        }
+                        ss[r * 2 + h] = scales[size_t(row) * (K_src / 32) + blk];
+                    } else {
+                        /* q = 0 (offset 8) with a zero scale */
+                        for (int i = 0; i < 16; i++)
+                            dst[i] = 0x88;
+                        ss[r * 2 + h] = 0;
+                    }
+                }
+            }
+        }
+}
+
+cudaError_t gemm_q4(const uint16_t *A, int M, const uint8_t *Wq, int N, int K, float *Y, int ldy,
+                    int *error, uint64_t limit_ns, cudaStream_t stream, bool accumulate,
+                    int max_splits) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0 ||
+        (reinterpret_cast<uintptr_t>(A) & 15) != 0 || (reinterpret_cast<uintptr_t>(Wq) & 15) != 0)
+        return cudaErrorInvalidValue;
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int mt = (M + kBM - 1) / kBM;
+    int splits = 1;
+    const int tiles = mt * ((N + kQ4N - 1) / kQ4N), kbs = K / kBK;
+    double best = 0.0;
+    for (int sp = 1; sp <= max_splits && kbs / sp >= 4; sp++) {
+        const int t = tiles * sp, waves = (t + sms - 1) / sms;
+        const double fill = double(t) / double(waves * sms);
+        if (fill > best + 0.02) {
+            best = fill;
+            splits = sp;
+        }
+    }
+    CUtensorMap ma;
+    if (!encode_map(&ma, A, M, K, kBM))
+        return cudaErrorInvalidValue;
+    const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, splits};
+    return launch_q4<8>(ma, Wq, g, stream);
 }
 
 } // namespace nut

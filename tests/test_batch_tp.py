@@ -216,3 +216,27 @@ def test_graph_replay_matches_direct_launches(gpu):
     assert nb.launch_count() > l0  # replays are counted
     tp.close()
     assert graph1.tolist() == graph2.tolist() == direct.tolist()
+
+
+@pytest.mark.gpu
+def test_int4_pipeline_gemm_matches_fp16_copies(gpu, monkeypatch):
+    """INT4 weights dequantised inside the GEMM pipeline give the logits of
+    the fp16 weight copies (the same q * scale values in the same K order;
+    only the split-K addition order differs)."""
+    cfg = _cfg()
+    w = syn.build_model(cfg, 1, 123)
+    B, n, steps = 4, 5, 6
+    prompts = np.stack([syn.prompt_ids(cfg, 700 + b, n) for b in range(B)])
+    monkeypatch.setenv("NUTLLM_BATCH_Q4", "1")
+    q4 = nb.TPBatch(B, weights=w)
+    ids4, lg4, _ = q4.generate(prompts, steps, want_logits=True)
+    bytes4 = q4.info()["weight_bytes"]
+    q4.close()
+    monkeypatch.setenv("NUTLLM_BATCH_Q4", "0")
+    f16 = nb.TPBatch(B, weights=w)
+    ids16, lg16, _ = f16.generate(prompts, steps, want_logits=True)
+    bytes16 = f16.info()["weight_bytes"]
+    f16.close()
+    assert np.allclose(lg4, lg16, rtol=1e-5, atol=1e-6), float(np.abs(lg4 - lg16).max())
+    assert ids4.tolist() == ids16.tolist()
+    assert bytes4 < bytes16
