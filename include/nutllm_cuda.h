@@ -257,6 +257,10 @@ nut_status nut_batch_stream(nut_batch *batch, void **stream);
  * <= 8, one process per GPU; the argmax still uses NCCL. */
 nut_status nut_batch_ipc_handle(nut_batch *batch, uint8_t *handle, int64_t size);
 nut_status nut_batch_open_peers(nut_batch *batch, const uint8_t *handles, int64_t stride);
+/* Prompts of at least min_tokens tokens (default 16; 0 = never) are
+ * prefilled as GEMMs over chunks of whole sequences (causal attention per
+ * sequence) instead of one position per pass. */
+nut_status nut_batch_set_prefill_threshold(nut_batch *batch, int64_t min_tokens);
 /* This rank's shard without creating anything (host only): shard[8] =
  * {first head, heads, first kv head, kv heads, first ffn unit, ffn units,
  * first vocabulary row, vocabulary rows}. */

@@ -179,6 +179,7 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_batch_info", [_P, _PI64])
         _declare(lib, "nut_tp_shard", [C.POINTER(Config), C.c_int, C.c_int, _PI64])
         _declare(lib, "nut_batch_ipc_handle", [_P, _P, _I64])
+        _declare(lib, "nut_batch_set_prefill_threshold", [_P, _I64])
         _declare(lib, "nut_batch_open_peers", [_P, _P, _I64])
         _declare(lib, "nut_batch_stream", [_P, C.POINTER(_P)])
         _declare(lib, "nut_batch_generate", [_P, _P, _I64, _I64, _P, _P,
@@ -537,6 +538,11 @@ class TPBatch:
             self.config = Config(**config.as_dict())
         self.handle = h
         self.batch, self.rank, self.world = batch, rank, world
+
+    def set_prefill_threshold(self, min_tokens: int) -> None:
+        """Prompts of at least min_tokens tokens (0 = never) are prefilled as
+        GEMMs over whole sequences rather than one position per pass."""
+        _check(cuda_lib().nut_batch_set_prefill_threshold(self.handle, int(min_tokens)))
 
     def ipc_handle(self) -> bytes:
         """This rank's receive-area handle for the peer-memory all-reduce."""

@@ -48,20 +48,23 @@ __global__ void add_rmsnorm_rows_kernel(float *h, float *part, int add, const fl
 }
 
 /* One thread per (sequence b, rotation pair or value element). */
-__global__ void rope_kv_batch_kernel(float *qkv, int B, int ldq, const int *pos_p,
+__global__ void rope_kv_batch_kernel(float *qkv, int rows, int B, int ldq, const int *pos_p,
                                      const float *rope_cos, const float *rope_sin, int heads,
                                      int kv_heads, int hd, float *kcache, float *vcache,
-                                     int layer, int max_seq) {
+                                     int layer, int max_seq, int pf_n, int seq0) {
     const int half = hd / 2, dq = heads * hd, kvd = kv_heads * hd;
     const int per_row = heads * half + kv_heads * half + kvd;
     const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (gid >= int64_t(B) * per_row)
+    if (gid >= int64_t(rows) * per_row)
         return;
-    const int pos = *pos_p;
     const int b = int(gid / per_row), r = int(gid - int64_t(b) * per_row);
+    /* decode: row b is sequence b at *pos; prefill: row b is position
+     * b % pf_n of sequence seq0 + b / pf_n */
+    const int pos = pf_n > 0 ? b % pf_n : *pos_p;
+    const int sq = pf_n > 0 ? seq0 + b / pf_n : b;
     float *row = qkv + size_t(b) * ldq;
     const float *cs = rope_cos + size_t(pos) * half, *sn = rope_sin + size_t(pos) * half;
-    const size_t seq = (size_t(layer) * B + b) * kv_heads;
+    const size_t seq = (size_t(layer) * B + sq) * kv_heads;
     if (r < heads * half) {                       /* query pair */
         const int h = r / half, i = r - h * half;
         float *p = row + h * hd + 2 * i;
@@ -105,13 +108,16 @@ template <int CPL>
 __global__ void __launch_bounds__(kAttWarps * 32)
 attention_batch_kernel(const float *qkv, int B, int ldq, const int *pos_p, const float *kcache,
                        const float *vcache, int layer, int heads, int kv_heads, int hd,
-                       int max_seq, int Kp, __half *ctx) {
+                       int max_seq, int Kp, __half *ctx, int pf_n, int seq0) {
     extern __shared__ float sm[];
+    /* decode: row b is sequence b at *pos; prefill: row b is position
+     * b % pf_n of sequence seq0 + b / pf_n (causal: positions 0..that) */
     const int b = blockIdx.x / heads, h = blockIdx.x - b * heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int npos = *pos_p + 1;
+    const int npos = (pf_n > 0 ? b % pf_n : *pos_p) + 1;
+    const int sq = pf_n > 0 ? seq0 + b / pf_n : b;
     const int g = h / (heads / kv_heads);
-    const size_t base = ((size_t(layer) * B + b) * kv_heads + g) * size_t(max_seq) * hd;
+    const size_t base = ((size_t(layer) * B + sq) * kv_heads + g) * size_t(max_seq) * hd;
     const int lpr = hd / 4 / CPL;                    /* lanes per row (a power of two) */
     const int rpi = 32 / lpr;                        /* rows per warp step */
     const int sub = lane / lpr, li = lane - sub * lpr;
@@ -390,20 +396,23 @@ cudaError_t add_rmsnorm_rows(float *h, float *part, bool add, const float *w, in
 cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const float *rope_cos,
                           const float *rope_sin, int heads, int kv_heads, int hd,
                           float *kcache, float *vcache, int layer, int max_seq,
-                          cudaStream_t s) {
-    const int64_t n = int64_t(B) * (heads * (hd / 2) + kv_heads * (hd / 2) + kv_heads * hd);
-    rope_kv_batch_kernel<<<blocks_for(n, 256), 256, 0, s>>>(qkv, B, ldq, pos, rope_cos,
+                          cudaStream_t s, int rows, int pf_n, int seq0) {
+    if (rows <= 0)
+        rows = B;
+    const int64_t n = int64_t(rows) * (heads * (hd / 2) + kv_heads * (hd / 2) + kv_heads * hd);
+    rope_kv_batch_kernel<<<blocks_for(n, 256), 256, 0, s>>>(qkv, rows, B, ldq, pos, rope_cos,
                                                             rope_sin, heads, kv_heads, hd,
-                                                            kcache, vcache, layer, max_seq);
+                                                            kcache, vcache, layer, max_seq, pf_n,
+                                                            seq0);
     count_launches(1);
     return cudaGetLastError();
 }
 
 template <int CPL>
-cudaError_t launch_attention(const float *qkv, int B, int ldq, const int *pos,
+cudaError_t launch_attention(const float *qkv, int rows, int B, int ldq, const int *pos,
                              const float *kcache, const float *vcache, int layer, int heads,
                              int kv_heads, int hd, int max_seq, int Kp, __half *ctx, int lpr,
-                             cudaStream_t s) {
+                             int pf_n, int seq0, cudaStream_t s) {
     const size_t nst = size_t(kAttWarps) * size_t(32 / lpr);
     const size_t smem = (size_t(hd) * (1 + nst) + 2 * nst) * sizeof(float);
     auto k = attention_batch_kernel<CPL>;
@@ -413,15 +422,17 @@ cudaError_t launch_attention(const float *qkv, int B, int ldq, const int *pos,
         if (e != cudaSuccess)
             return e;
     }
-    k<<<B * heads, kAttWarps * 32, smem, s>>>(qkv, B, ldq, pos, kcache, vcache, layer, heads,
-                                              kv_heads, hd, max_seq, Kp, ctx);
+    k<<<rows * heads, kAttWarps * 32, smem, s>>>(qkv, B, ldq, pos, kcache, vcache, layer, heads,
+                                                 kv_heads, hd, max_seq, Kp, ctx, pf_n, seq0);
     return cudaGetLastError();
 }
 
 cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
                             const float *kcache, const float *vcache, int layer, int heads,
                             int kv_heads, int hd, int max_seq, int Kp, uint16_t *ctx,
-                            cudaStream_t s) {
+                            cudaStream_t s, int rows, int pf_n, int seq0) {
+    if (rows <= 0)
+        rows = B;
     /* float4 rows over lpr lanes (the largest power of two dividing
      * hd / 4, at most 32), CPL float4 per lane */
     if (hd % 4 != 0 || hd <= 0)
@@ -434,20 +445,20 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
     cudaError_t e;
     switch (cpl) {
     case 1:
-        e = launch_attention<1>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
-                                max_seq, Kp, c16, lpr, s);
+        e = launch_attention<1>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
+                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
         break;
     case 2:
-        e = launch_attention<2>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
-                                max_seq, Kp, c16, lpr, s);
+        e = launch_attention<2>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
+                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
         break;
     case 3:
-        e = launch_attention<3>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
-                                max_seq, Kp, c16, lpr, s);
+        e = launch_attention<3>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
+                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
         break;
     case 4:
-        e = launch_attention<4>(qkv, B, ldq, pos, kcache, vcache, layer, heads, kv_heads, hd,
-                                max_seq, Kp, c16, lpr, s);
+        e = launch_attention<4>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
+                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
         break;
     default:
         return cudaErrorInvalidValue;
@@ -456,8 +467,8 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
     if (e != cudaSuccess)
         return e;
     if (Kp > heads * hd) {
-        const int64_t n = int64_t(B) * (Kp - heads * hd);
-        zero_cols_kernel<<<blocks_for(n, 256), 256, 0, s>>>(c16, B, heads * hd, Kp);
+        const int64_t n = int64_t(rows) * (Kp - heads * hd);
+        zero_cols_kernel<<<blocks_for(n, 256), 256, 0, s>>>(c16, rows, heads * hd, Kp);
         count_launches(1);
     }
     return cudaGetLastError();

@@ -24,6 +24,7 @@
  */
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdlib>
@@ -180,6 +181,11 @@ struct nut_batch {
     int32_t *ids = nullptr, *out = nullptr, *prompts = nullptr;
     int *pos = nullptr, *pstep = nullptr, *ostep = nullptr; /* device counters */
     int *gemm_error = nullptr;
+    /* prefill rows (chunks of whole sequences, made on first use) */
+    int pf_rows = 0;
+    float *pf_h = nullptr, *pf_part = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr;
+    uint16_t *pf_x16 = nullptr, *pf_ctx16 = nullptr, *pf_act16 = nullptr;
+    int prefill_min = 16; /* prompts of at least this many tokens: GEMM prefill */
     /* peer-memory all-reduce: this rank's area ([2][world][B dim] floats,
      * then [world][kArChunks] flags), the peers' areas (IPC mappings), the
      * per-chunk call counters and the error word */
@@ -213,6 +219,10 @@ struct nut_batch {
                             (void *)l.attn_norm, (void *)l.ffn_norm})
                 if (p)
                     cudaFree(p);
+        for (void *p : {(void *)pf_h, (void *)pf_part, (void *)pf_qkv, (void *)pf_gu,
+                        (void *)pf_x16, (void *)pf_ctx16, (void *)pf_act16})
+            if (p)
+                cudaFree(p);
         for (void *p : peer_open)
             cudaIpcCloseMemHandle(p);
         for (void *p : {(void *)peer_area, (void *)ar_epochs, (void *)ar_error})
@@ -534,21 +544,22 @@ void load_synthetic(nut_batch &b, uint64_t seed) {
 /* y[B][N] += x w^T; y holds zeros (every consumer of a GEMM output zeroes
  * it once read), so the K dimension may be split over CTAs that add their
  * partial products. */
-void gemm(nut_batch &b, const uint16_t *a, const uint16_t *w, int N, int K, float *y) {
-    cuda_check(nut::gemm_f16(a, b.B, w, N, N, K, y, N, b.gemm_error, nut::kDefaultWaitNs,
-                             b.stream, true, 8),
+void gemm(nut_batch &b, const uint16_t *a, const uint16_t *w, int N, int K, float *y,
+          int M = 0) {
+    cuda_check(nut::gemm_f16(a, M > 0 ? M : b.B, w, N, N, K, y, N, b.gemm_error,
+                             nut::kDefaultWaitNs, b.stream, true, 8),
                "batch gemm");
 }
 
 /* A projection: packed INT4 weights through gemm_q4, or the fp16 copy. */
 void proj(nut_batch &b, const uint16_t *a, const uint16_t *w16, const uint8_t *w4, int N, int K,
-          float *y) {
+          float *y, int M = 0) {
     if (b.q4)
-        cuda_check(nut::gemm_q4(a, b.B, w4, N, K, y, N, b.gemm_error, nut::kDefaultWaitNs,
-                                b.stream, true, 8),
+        cuda_check(nut::gemm_q4(a, M > 0 ? M : b.B, w4, N, K, y, N, b.gemm_error,
+                                nut::kDefaultWaitNs, b.stream, true, 8),
                    "batch gemm");
     else
-        gemm(b, a, w16, N, K, y);
+        gemm(b, a, w16, N, K, y, M);
 }
 
 void all_reduce_sum(nut_batch &b, float *x, size_t n) {
@@ -602,6 +613,93 @@ void forward(nut_batch &b) {
         proj(b, b.act16, L.down, L.down4, dim, b.kp_ffn, b.part);
         all_reduce_sum(b, b.part, size_t(B) * dim);
     }
+}
+
+/* The prompts [B][n] through every layer as GEMMs over the rows of up to
+ * kPrefillRows tokens (whole sequences per chunk): the same operations as
+ * n passes of forward(), with RoPE, the KV append and causal attention per
+ * sequence.  Leaves each sequence's last hidden row in b.h (and its last
+ * Wdown partial, summed over the ranks, in b.part), the cache holding
+ * positions 0 .. n - 1 and *pos = n - 1, as the n-th pass would. */
+constexpr int kPrefillRows = 2048;
+
+void prefill(nut_batch &b, int n) {
+    cudaStream_t s = b.stream;
+    const int dim = b.dim, chunk = std::max(1, std::min(b.B, kPrefillRows / n));
+    const int rows = chunk * n;
+    if (b.pf_rows < rows) {
+        cuda_check(cudaStreamSynchronize(s), "synchronize");
+        for (void *p : {(void *)b.pf_h, (void *)b.pf_part, (void *)b.pf_qkv, (void *)b.pf_gu,
+                        (void *)b.pf_x16, (void *)b.pf_ctx16, (void *)b.pf_act16})
+            if (p)
+                cudaFree(p);
+        const size_t R = size_t(rows);
+        b.pf_h = dev_alloc<float>(R * dim, "alloc prefill rows");
+        b.pf_part = dev_alloc<float>(R * dim, "alloc prefill rows");
+        b.pf_qkv = dev_alloc<float>(R * b.nqkv, "alloc prefill rows");
+        b.pf_gu = dev_alloc<float>(R * 2 * b.ffn_r, "alloc prefill rows");
+        b.pf_x16 = dev_alloc<uint16_t>(R * b.kp_dim, "alloc prefill rows");
+        b.pf_ctx16 = dev_alloc<uint16_t>(R * b.kp_ctx, "alloc prefill rows");
+        b.pf_act16 = dev_alloc<uint16_t>(R * b.kp_ffn, "alloc prefill rows");
+        /* GEMM outputs start at zero; their consumers zero them again */
+        cuda_check(cudaMemsetAsync(b.pf_part, 0, R * dim * 4, s), "clear rows");
+        cuda_check(cudaMemsetAsync(b.pf_qkv, 0, R * b.nqkv * 4, s), "clear rows");
+        cuda_check(cudaMemsetAsync(b.pf_gu, 0, R * 2 * b.ffn_r * 4, s), "clear rows");
+        b.pf_rows = rows;
+    }
+    for (int s0 = 0; s0 < b.B; s0 += chunk) {
+        const int cs = std::min(chunk, b.B - s0), M = cs * n;
+        cuda_check(nut::gather_rows(b.emb, b.prompts + size_t(s0) * n, M, dim,
+                                    int(b.cfg.vocab_size), b.pf_h, s),
+                   "embed");
+        for (int l = 0; l < b.layers; l++) {
+            const nut_batch::Layer &L = b.L[size_t(l)];
+            cuda_check(nut::add_rmsnorm_rows(b.pf_h, b.pf_part, l > 0, L.attn_norm, M, dim,
+                                             b.kp_dim, b.pf_x16, s),
+                       "rmsnorm");
+            proj(b, b.pf_x16, L.qkv, L.qkv4, b.nqkv, b.kp_dim, b.pf_qkv, M);
+            cuda_check(nut::rope_kv_batch(b.pf_qkv, b.B, b.nqkv, b.pos, b.rope_cos, b.rope_sin,
+                                          b.heads_r, b.kvh_r, b.hd, b.kcache, b.vcache, l,
+                                          b.max_seq, s, M, n, s0),
+                       "rope");
+            cuda_check(nut::attention_batch(b.pf_qkv, b.B, b.nqkv, b.pos, b.kcache, b.vcache, l,
+                                            b.heads_r, b.kvh_r, b.hd, b.max_seq, b.kp_ctx,
+                                            b.pf_ctx16, s, M, n, s0),
+                       "attention");
+            proj(b, b.pf_ctx16, L.wo, L.wo4, dim, b.kp_ctx, b.pf_part, M);
+            if (b.world > 1)
+                nccl_check(nccl().all_reduce(b.pf_part, b.pf_part, size_t(M) * dim, ncclFloat32,
+                                             ncclSum, b.comm, s),
+                           "all-reduce");
+            cuda_check(nut::add_rmsnorm_rows(b.pf_h, b.pf_part, true, L.ffn_norm, M, dim,
+                                             b.kp_dim, b.pf_x16, s),
+                       "rmsnorm");
+            proj(b, b.pf_x16, L.gu, L.gu4, 2 * b.ffn_r, b.kp_dim, b.pf_gu, M);
+            cuda_check(nut::swiglu_rows(b.pf_gu, M, b.ffn_r, b.kp_ffn, b.pf_act16, s, true),
+                       "swiglu");
+            proj(b, b.pf_act16, L.down, L.down4, dim, b.kp_ffn, b.pf_part, M);
+            if (b.world > 1)
+                nccl_check(nccl().all_reduce(b.pf_part, b.pf_part, size_t(M) * dim, ncclFloat32,
+                                             ncclSum, b.comm, s),
+                           "all-reduce");
+        }
+        /* each sequence's last row: hidden and its pending Wdown partial */
+        const size_t pitch = size_t(n) * dim * 4, row = size_t(dim) * 4;
+        cuda_check(cudaMemcpy2DAsync(b.h + size_t(s0) * dim, row,
+                                     b.pf_h + size_t(n - 1) * dim, pitch, row, cs,
+                                     cudaMemcpyDeviceToDevice, s),
+                   "copy last rows");
+        cuda_check(cudaMemcpy2DAsync(b.part + size_t(s0) * dim, row,
+                                     b.pf_part + size_t(n - 1) * dim, pitch, row, cs,
+                                     cudaMemcpyDeviceToDevice, s),
+                   "copy last rows");
+        /* the partials of the other rows are never added: clear them all */
+        cuda_check(cudaMemsetAsync(b.pf_part, 0, size_t(M) * dim * 4, s), "clear rows");
+    }
+    const int last = n - 1;
+    cuda_check(cudaMemcpyAsync(b.pos, &last, sizeof last, cudaMemcpyHostToDevice, s),
+               "set position");
+    cuda_check(cudaStreamSynchronize(s), "prefill"); /* `last` lives on this stack */
 }
 
 /* Final norm, this rank's classifier rows, and the global first-index
@@ -813,6 +911,14 @@ nut_status nut_batch_open_peers(nut_batch *b, const uint8_t *handles, int64_t st
     });
 }
 
+nut_status nut_batch_set_prefill_threshold(nut_batch *b, int64_t min_tokens) {
+    return guarded([&] {
+        if (b == nullptr || min_tokens < 0)
+            raise(NUT_INVALID_ARGUMENT, "batch: invalid argument");
+        b->prefill_min = int(std::min<int64_t>(min_tokens, 1 << 30));
+    });
+}
+
 nut_status nut_batch_info(const nut_batch *b, int64_t *info) {
     return guarded([&] {
         if (b == nullptr || info == nullptr)
@@ -855,10 +961,13 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
         if (graphs)
             ensure_graphs(*b, int(n));
         cuda_check(cudaEventRecord(b->ev[0], s), "record event");
-        /* the prompt, one position per pass (its classifier only after the
-         * last prompt token); the pass before the last advances the
-         * position, so the last runs at n - 1 */
-        for (int64_t t = 0; t < n; t++) {
+        /* the prompt: as GEMMs over whole sequences, or one position per
+         * pass (its classifier only after the last prompt token; the pass
+         * before the last advances the position, so the last runs at n - 1) */
+        const bool gemm_prefill = n >= b->prefill_min && b->prefill_min > 0;
+        if (gemm_prefill)
+            prefill(*b, int(n));
+        for (int64_t t = 0; t < n && !gemm_prefill; t++) {
             if (graphs && t + 1 < n) {
                 cuda_check(cudaGraphLaunch(b->g_prompt, s), "replay prompt pass");
                 nut::count_launches(unsigned(b->g_prompt_kernels));

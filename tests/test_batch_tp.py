@@ -240,3 +240,30 @@ def test_int4_pipeline_gemm_matches_fp16_copies(gpu, monkeypatch):
     assert np.allclose(lg4, lg16, rtol=1e-5, atol=1e-6), float(np.abs(lg4 - lg16).max())
     assert ids4.tolist() == ids16.tolist()
     assert bytes4 < bytes16
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype", [0, 1])
+def test_gemm_prefill_matches_oracle(gpu, orc, qtype):
+    """Prompts of >= 16 tokens are prefilled as GEMMs over whole sequences
+    (causal attention per sequence): the logits of every step stay within
+    the fp16-operand bound of the oracle, and match the per-pass prefill."""
+    cfg = _cfg()
+    w = syn.build_model(cfg, qtype, 31)
+    B, n, steps = 5, 21, 5
+    prompts = np.stack([syn.prompt_ids(cfg, 900 + b, n) for b in range(B)])
+    tp = nb.TPBatch(B, weights=w)
+    ids, logits, st = tp.generate(prompts, steps, want_logits=True)
+    tp.set_prefill_threshold(0)
+    ids_pp, logits_pp, _ = tp.generate(prompts, steps, want_logits=True)
+    tp.close()
+    assert st.prefill_tokens == B * n
+    dev = []
+    for b in range(B):
+        want = _forced_oracle_logits(orc, w, prompts[b], ids[b])
+        d = np.abs(logits[:, b, :] - want)
+        assert np.all(d <= ATOL + RTOL * np.abs(want)), (b, float(d.max()))
+        dev.append(d)
+    assert float(np.median(np.concatenate(dev))) <= MEDIAN
+    assert np.allclose(logits, logits_pp, rtol=1e-3, atol=1e-4)
+    assert ids.tolist() == ids_pp.tolist()
