@@ -48,6 +48,16 @@ int nut_host_llama2c_generate(const char *path, int32_t type, const int32_t *pro
 int nut_host_llama2c_inspect(const char *path, int32_t type, int64_t *config,
                              int32_t *tied, uint64_t *storage_bytes, uint64_t *digest);
 
+/* Llama2Tokenizer (reference include/llama2.hpp:11-25): loads `path` with
+ * `vocab` entries and encodes text (bos / eos flags) into ids (room for
+ * `cap`; *n_out = count), or decodes ids into text (room for `cap` bytes,
+ * not NUL-terminated; *len_out = length). */
+int nut_host_tokenizer_encode(const char *path, int64_t vocab, const char *text,
+                              int64_t text_len, int32_t bos, int32_t eos, int32_t *ids,
+                              int64_t cap, int64_t *n_out);
+int nut_host_tokenizer_decode(const char *path, int64_t vocab, const int32_t *ids, int64_t n,
+                              char *out, int64_t cap, int64_t *len_out);
+
 /* The generation token choice (choose_token, reference
  * src/generate.cpp:25-73) over `steps` rows of logits [steps][vocab] with
  * one std::mt19937(seed) shared by the steps, as one generation uses it. */

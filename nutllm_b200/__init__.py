@@ -212,6 +212,10 @@ def host_lib() -> C.CDLL:
                   C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)])
         _declare(lib, "nut_host_choose_tokens",
                  [_P, _I64, _I64, C.c_float, C.c_float, C.c_uint32, _P])
+        _declare(lib, "nut_host_tokenizer_encode",
+                 [C.c_char_p, _I64, C.c_char_p, _I64, C.c_int32, C.c_int32, _P, _I64, _PI64])
+        _declare(lib, "nut_host_tokenizer_decode",
+                 [C.c_char_p, _I64, _P, _I64, C.c_char_p, _I64, _PI64])
         _host = lib
     return _host
 
@@ -327,6 +331,31 @@ def llama2c_inspect(path: str, qtype: int) -> tuple[list, bool, int, int]:
     _check(lib.nut_host_llama2c_inspect(os.fsencode(path), qtype, cfg, C.byref(tied),
                                         C.byref(nbytes), C.byref(digest)), lib)
     return list(cfg), bool(tied.value), nbytes.value, digest.value
+
+
+def tokenizer_encode(path: str, vocab: int, text: str, bos: bool = True,
+                     eos: bool = False) -> list:
+    """Llama2Tokenizer::load(path, vocab).encode(text, bos, eos)."""
+    lib = host_lib()
+    raw = text.encode("utf-8")
+    cap = len(raw) + 3
+    ids = np.zeros(cap, np.int32)
+    n = C.c_int64(0)
+    _check(lib.nut_host_tokenizer_encode(os.fsencode(path), vocab, raw, len(raw), int(bos),
+                                         int(eos), _ptr(ids), cap, C.byref(n)), lib)
+    return ids[:n.value].tolist()
+
+
+def tokenizer_decode(path: str, vocab: int, ids) -> bytes:
+    """Llama2Tokenizer::load(path, vocab).decode(ids), as raw bytes."""
+    lib = host_lib()
+    a = np.ascontiguousarray(ids, np.int32)
+    cap = 64 * max(len(a), 1)
+    buf = C.create_string_buffer(cap)
+    n = C.c_int64(0)
+    _check(lib.nut_host_tokenizer_decode(os.fsencode(path), vocab, _ptr(a), len(a), buf, cap,
+                                         C.byref(n)), lib)
+    return buf.raw[:n.value]
 
 
 def choose_tokens(logits: np.ndarray, temperature: float, top_p: float,

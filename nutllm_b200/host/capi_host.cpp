@@ -167,4 +167,36 @@ int nut_host_choose_tokens(const float *logits, int64_t steps, int64_t vocab,
     });
 }
 
+int nut_host_tokenizer_encode(const char *path, int64_t vocab, const char *text,
+                              int64_t text_len, int32_t bos, int32_t eos, int32_t *ids,
+                              int64_t cap, int64_t *n_out) {
+    return guarded([&] {
+        if (path == nullptr || (text == nullptr && text_len > 0) || n_out == nullptr ||
+            vocab < 0 || text_len < 0)
+            throw std::invalid_argument("llama2 tokenizer: invalid argument");
+        const Llama2Tokenizer t = Llama2Tokenizer::load(path, size_t(vocab));
+        const std::vector<int> out =
+            t.encode(std::string(text, size_t(text_len)), bos != 0, eos != 0);
+        if (int64_t(out.size()) > cap || (cap > 0 && ids == nullptr))
+            throw std::length_error("llama2 tokenizer: output buffer too small");
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = int64_t(out.size());
+    });
+}
+
+int nut_host_tokenizer_decode(const char *path, int64_t vocab, const int32_t *ids, int64_t n,
+                              char *out, int64_t cap, int64_t *len_out) {
+    return guarded([&] {
+        if (path == nullptr || (ids == nullptr && n > 0) || len_out == nullptr || vocab < 0 ||
+            n < 0)
+            throw std::invalid_argument("llama2 tokenizer: invalid argument");
+        const Llama2Tokenizer t = Llama2Tokenizer::load(path, size_t(vocab));
+        const std::string text = t.decode(std::vector<int>(ids, ids + n));
+        if (int64_t(text.size()) > cap || (cap > 0 && out == nullptr))
+            throw std::length_error("llama2 tokenizer: output buffer too small");
+        std::memcpy(out, text.data(), text.size());
+        *len_out = int64_t(text.size());
+    });
+}
+
 } // extern "C"

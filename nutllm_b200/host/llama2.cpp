@@ -7,6 +7,8 @@
 #include "llama2.hpp"
 
 #include <algorithm>
+#include <cmath>
+#include <cstddef>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -228,4 +230,137 @@ QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, Quan
                                   std::move(down[l]), std::move(att_norms[l]),
                                   std::move(ffn_norms[l]));
     return model;
+}
+
+/* ---- tokenizer -------------------------------------------------------- */
+
+Llama2Tokenizer Llama2Tokenizer::load(const std::string &path, size_t vocab_size) {
+    if (vocab_size == 0 || vocab_size > size_t(std::numeric_limits<int>::max()))
+        throw std::invalid_argument("llama2 tokenizer: invalid vocabulary");
+    std::ifstream in(path, std::ios::binary);
+    if (!in)
+        throw std::runtime_error("llama2 tokenizer: cannot open " + path);
+    uint32_t max_len = 0;
+    in.read(reinterpret_cast<char *>(&max_len), sizeof max_len);
+    if (!in || max_len == 0)
+        throw std::runtime_error("llama2 tokenizer: invalid header");
+    Llama2Tokenizer t;
+    t.max_length_ = max_len;
+    t.pieces_.reserve(vocab_size);
+    t.scores_.reserve(vocab_size);
+    for (size_t id = 0; id < vocab_size; id++) {
+        float score = 0.0f;
+        int32_t len = 0;
+        in.read(reinterpret_cast<char *>(&score), sizeof score);
+        in.read(reinterpret_cast<char *>(&len), sizeof len);
+        if (!in || !std::isfinite(score) || len <= 0 || size_t(len) > t.max_length_)
+            throw std::runtime_error("llama2 tokenizer: malformed vocabulary entry");
+        std::string piece(size_t(len), '\0');
+        in.read(&piece[0], len);
+        if (!in)
+            throw std::runtime_error("llama2 tokenizer: truncated token");
+        t.scores_.push_back(score);
+        t.pieces_.push_back(std::move(piece));
+    }
+    if (in.peek() != std::char_traits<char>::eof())
+        throw std::runtime_error("llama2 tokenizer: trailing data");
+    t.ids_.reserve(t.pieces_.size());
+    for (size_t id = 0; id < t.pieces_.size(); id++)
+        t.ids_.emplace(t.pieces_[id], int(id)); /* keeps the first id of a piece */
+    return t;
+}
+
+int Llama2Tokenizer::find(const std::string &piece) const {
+    const auto it = ids_.find(piece);
+    return it == ids_.end() ? -1 : it->second;
+}
+
+std::vector<int> Llama2Tokenizer::encode(const std::string &text, bool bos, bool eos) const {
+    std::vector<int> out;
+    out.reserve(text.size() + 3);
+    if (bos)
+        out.push_back(1);
+    if (!text.empty()) {
+        const int space = find(" ");
+        if (space < 0)
+            throw std::runtime_error("llama2 tokenizer: dummy prefix token missing");
+        out.push_back(space);
+    }
+    /* one token per UTF-8 character: a lead byte and up to three
+     * continuation bytes (10xxxxxx) */
+    size_t i = 0;
+    while (i < text.size()) {
+        size_t j = i + 1;
+        while (j < text.size() && j - i < 4 &&
+               (static_cast<unsigned char>(text[j]) & 0xC0u) == 0x80u)
+            j++;
+        const std::string ch = text.substr(i, j - i);
+        const int id = find(ch);
+        if (id >= 0) {
+            out.push_back(id);
+        } else {
+            for (unsigned char c : ch) {
+                if (size_t(c) + 3 >= pieces_.size())
+                    throw std::runtime_error("llama2 tokenizer: byte fallback unavailable");
+                out.push_back(int(c) + 3);
+            }
+        }
+        i = j;
+    }
+    /* merge the best-scoring adjacent pair until none forms a token */
+    for (;;) {
+        size_t at = out.size();
+        int merged = -1;
+        float best = -std::numeric_limits<float>::infinity();
+        for (size_t k = 0; k + 1 < out.size(); k++) {
+            const int id = find(pieces_[size_t(out[k])] + pieces_[size_t(out[k + 1])]);
+            if (id >= 0 && scores_[size_t(id)] > best) {
+                best = scores_[size_t(id)];
+                at = k;
+                merged = id;
+            }
+        }
+        if (at == out.size())
+            break;
+        out[at] = merged;
+        out.erase(out.begin() + std::ptrdiff_t(at) + 1);
+    }
+    if (eos)
+        out.push_back(2);
+    return out;
+}
+
+std::string Llama2Tokenizer::decode(const std::vector<int> &tokens) const {
+    auto hex = [](char c) -> int {
+        if (c >= '0' && c <= '9')
+            return c - '0';
+        if (c >= 'a' && c <= 'f')
+            return c - 'a' + 10;
+        if (c >= 'A' && c <= 'F')
+            return c - 'A' + 10;
+        return -1;
+    };
+    std::string text;
+    size_t k = 0;
+    int prev = -1;
+    if (!tokens.empty() && tokens[0] == 1) {
+        prev = 1;
+        k = 1;
+    }
+    for (; k < tokens.size(); k++) {
+        const int id = tokens[k];
+        if (id < 0 || size_t(id) >= pieces_.size())
+            throw std::out_of_range("llama2 tokenizer: token id out of range");
+        std::string piece = pieces_[size_t(id)];
+        if (prev == 1 && !piece.empty() && piece[0] == ' ')
+            piece.erase(0, 1);
+        if (piece.size() == 6 && piece.compare(0, 3, "<0x") == 0 && piece[5] == '>') {
+            const int hi = hex(piece[3]), lo = hex(piece[4]);
+            if (hi >= 0 && lo >= 0)
+                piece.assign(1, char((hi << 4) | lo));
+        }
+        text += piece;
+        prev = id;
+    }
+    return text;
 }

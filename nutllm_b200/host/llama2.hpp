@@ -14,8 +14,39 @@
  * are [out][in] as stored; eos is token 1.  Each projection is quantised
  * per block of 32 on the host exactly as QuantizedMatrix::quantize does. */
 #include <string>
+#include <unordered_map>
+#include <vector>
 
 #include "quant.hpp"
 #include "quant_model.hpp"
 
 QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, QuantType type);
+
+/* The llama2.c tokenizer (include/llama2.hpp:11-25, src/llama2.cpp:414-543),
+ * host text I/O around the token loop.
+ *
+ * File: uint32 maximum token length, then per id a float score, an int32
+ * byte length and the bytes.  encode: BOS (1) if asked, the " " token when
+ * the text is non-empty, one token per UTF-8 character (or, for a character
+ * with no token, one byte-fallback id byte + 3 per byte), then repeatedly
+ * the adjacent pair whose concatenation is a token with the highest score
+ * (the first such pair on ties) is merged, then EOS (2) if asked.  decode:
+ * skips a leading BOS, drops one leading space of the piece after a BOS,
+ * and turns "<0xHH>" pieces into that byte.  Errors keep the reference's
+ * classes and messages. */
+class Llama2Tokenizer {
+public:
+    static Llama2Tokenizer load(const std::string &path, size_t vocab_size);
+
+    std::vector<int> encode(const std::string &text, bool bos = true, bool eos = false) const;
+    std::string decode(const std::vector<int> &tokens) const;
+    size_t vocabulary_size() const { return pieces_.size(); }
+
+private:
+    int find(const std::string &piece) const;
+
+    std::vector<std::string> pieces_;
+    std::vector<float> scores_;
+    std::unordered_map<std::string, int> ids_; /* first id of each piece */
+    size_t max_length_ = 0;
+};

@@ -286,6 +286,10 @@ class Reference:
                                             C.POINTER(C.c_uint64)]
         lib.ref_llama2c_encode.argtypes = [C.c_char_p, S, C.c_char_p, C.c_int, _P, S,
                                            C.POINTER(S)]
+        lib.ref_llama2c_encode2.argtypes = [C.c_char_p, S, C.c_char_p, S, C.c_int, C.c_int,
+                                            _P, S, C.POINTER(S)]
+        lib.ref_llama2c_decode.argtypes = [C.c_char_p, S, _P, S, C.c_char_p, S,
+                                           C.POINTER(S)]
         self.lib = lib
 
     def _check(self, status):
@@ -399,6 +403,23 @@ class Reference:
         self._check(self.lib.ref_llama2c_inspect(path.encode(), qtype, cfg, C.byref(tied),
                                                  C.byref(nbytes), C.byref(digest)))
         return list(cfg), bool(tied.value), nbytes.value, digest.value
+
+    def tokenizer_encode(self, path: str, vocab: int, text: bytes, bos: bool, eos: bool):
+        ids = np.zeros(len(text) + 3, np.int32)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_llama2c_encode2(path.encode(), vocab, text, len(text),
+                                                 int(bos), int(eos), _ptr(ids), ids.size,
+                                                 C.byref(n)))
+        return ids[:n.value].tolist()
+
+    def tokenizer_decode(self, path: str, vocab: int, ids) -> bytes:
+        a = np.ascontiguousarray(ids, np.int32)
+        cap = 64 * max(len(a), 1)
+        buf = C.create_string_buffer(cap)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_llama2c_decode(path.encode(), vocab, _ptr(a), len(a), buf,
+                                                cap, C.byref(n)))
+        return buf.raw[:n.value]
 
     def llama2c_encode(self, tokenizer_path: str, vocab: int, text: str, bos: bool = True):
         ids = np.zeros(4 * len(text.encode()) + 8, np.int32)

@@ -434,6 +434,34 @@ int ref_llama2c_inspect(const char *path, int type, int64_t *config,
     });
 }
 
+/* Llama2Tokenizer::load(path, vocab).encode(text, bos, eos). */
+int ref_llama2c_encode2(const char *tokenizer_path, size_t vocab, const char *text,
+                        size_t text_len, int bos, int eos, int *ids, size_t capacity,
+                        size_t *n_out) {
+    return guarded([&] {
+        const Llama2Tokenizer tok = Llama2Tokenizer::load(tokenizer_path, vocab);
+        const std::vector<int> out =
+            tok.encode(std::string(text, text_len), bos != 0, eos != 0);
+        if (out.size() > capacity)
+            throw std::length_error("ref harness: encode capacity");
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = out.size();
+    });
+}
+
+/* Llama2Tokenizer::load(path, vocab).decode(ids) into out (not terminated). */
+int ref_llama2c_decode(const char *tokenizer_path, size_t vocab, const int *ids,
+                       size_t n, char *out, size_t capacity, size_t *len_out) {
+    return guarded([&] {
+        const Llama2Tokenizer tok = Llama2Tokenizer::load(tokenizer_path, vocab);
+        const std::string text = tok.decode(std::vector<int>(ids, ids + n));
+        if (text.size() > capacity)
+            throw std::length_error("ref harness: decode capacity");
+        std::memcpy(out, text.data(), text.size());
+        *len_out = text.size();
+    });
+}
+
 /* Llama2Tokenizer::load(path, vocab).encode(text, bos, false). */
 int ref_llama2c_encode(const char *tokenizer_path, size_t vocab,
                        const char *text, int bos, int *ids, size_t capacity,

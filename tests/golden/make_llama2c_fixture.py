@@ -99,11 +99,69 @@ def prompt_of(name: str) -> np.ndarray:
     return rng.integers(2, abs(c["vocab"]), size=c["n_prompt"]).astype(np.int32)
 
 
+TOKENIZER_GOLDEN = os.path.join(HERE, "tokenizer_golden.npz")
+
+# texts the tokenizer goldens cover (utf-8): merges, ties, byte fallback for
+# characters without a token (2-, 3- and 4-byte sequences), empty text
+TOKENIZER_TEXTS = ["the cat", "Hi!", "caf\u00e9 au lait", "thing and then", "",
+                   "\u017e\u20ac\U0001d11e", "  spaces  ", "the the the", "ATHENA"]
+
+
+def tokenizer_bytes(seed: int = 5) -> tuple[bytes, int]:
+    """A llama2.c tokenizer file (the layout Llama2Tokenizer::load reads,
+    src/llama2.cpp:414-453): ids 0-2 special, 3-258 the byte pieces
+    <0x00>..<0xFF>, then single characters and seeded merge pieces with
+    seeded scores, one duplicated piece (the first id must win) and two
+    pieces with equal scores (the first position must win)."""
+    rng = np.random.default_rng(seed)
+    pieces = ["<unk>", "\n<s>\n", "\n</s>\n"] + [f"<0x{b:02X}>" for b in range(256)]
+    chars = [" "] + list("abcdefghijklmnopqrstuvwxyz") + list("ATHEN") + list("!.,") + ["\u00e9"]
+    merges = ["th", "he", "the", " t", " th", " the", "in", "ing", "an", "and", " a", "ca",
+              "caf", "caf\u00e9", "at", " c", " ca", " cat", "en", "then", " l", "la",
+              "lait", "ai", "it", "  ", "ATH", "EN", "ENA", "th"]  # "th" twice
+    pieces += chars + merges
+    scores = [0.0] * 259 + list(rng.uniform(-10, -5, len(chars))) + \
+        list(rng.uniform(-5, 0, len(merges)))
+    scores[pieces.index("en")] = scores[pieces.index("an")]  # a tie
+    out = [np.array([max(len(p.encode()) for p in pieces)], np.uint32).tobytes()]
+    for p, sc in zip(pieces, scores):
+        b = p.encode()
+        out.append(np.array([sc], np.float32).tobytes())
+        out.append(np.array([len(b)], np.int32).tobytes())
+        out.append(b)
+    return b"".join(out), len(pieces)
+
+
+def write_tokenizer(path: str) -> tuple[str, int]:
+    data, vocab = tokenizer_bytes()
+    with open(path, "wb") as f:
+        f.write(data)
+    return path, vocab
+
+
+def make_tokenizer_goldens(ref) -> None:
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        path, vocab = write_tokenizer(os.path.join(tmp, "tok.bin"))
+        out["sha256"] = np.frombuffer(hashlib.sha256(open(path, "rb").read()).digest(), np.uint8)
+        out["vocab"] = np.array(vocab)
+        for i, text in enumerate(TOKENIZER_TEXTS):
+            raw = text.encode("utf-8")
+            for bos, eos in ((1, 0), (0, 0), (1, 1)):
+                ids = ref.tokenizer_encode(path, vocab, raw, bool(bos), bool(eos))
+                out[f"t{i}/ids{bos}{eos}"] = np.array(ids, np.int32)
+                back = ref.tokenizer_decode(path, vocab, ids if not eos else ids[:-1])
+                out[f"t{i}/text{bos}{eos}"] = np.frombuffer(back, np.uint8)
+    np.savez_compressed(TOKENIZER_GOLDEN, **out)
+    print("wrote", TOKENIZER_GOLDEN)
+
+
 def main() -> None:
     sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
     from oracle import Reference
 
     ref = Reference()
+    make_tokenizer_goldens(ref)
     out = {}
     with tempfile.TemporaryDirectory() as tmp:
         for name in CONFIGS:

@@ -227,3 +227,57 @@ def test_host_api_selftest(gpu, checkpoints, name, qname):
                        text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "FAIL" not in r.stdout and "all host API checks passed" in r.stdout
+
+
+# ------------------------------------------------------------------ tokenizer
+
+TG = np.load(golden_path("tokenizer_golden.npz"))
+
+
+@pytest.fixture(scope="module")
+def tokenizer_file(tmp_path_factory):
+    path, vocab = fx.write_tokenizer(str(tmp_path_factory.mktemp("tok") / "tok.bin"))
+    assert np.array_equal(np.frombuffer(hashlib.sha256(open(path, "rb").read()).digest(),
+                                        np.uint8), TG["sha256"])
+    return path, vocab
+
+
+@pytest.mark.parametrize("i", range(len(fx.TOKENIZER_TEXTS)))
+def test_tokenizer_matches_reference(tokenizer_file, i):
+    """Llama2Tokenizer encode (BOS / no BOS / BOS+EOS) and decode give the
+    reference's ids and bytes: merges by score with first-position ties, the
+    first id of a duplicated piece, byte fallback for characters without a
+    token, the dummy-prefix space and its removal after BOS."""
+    path, vocab = tokenizer_file
+    text = fx.TOKENIZER_TEXTS[i]
+    for bos, eos in ((1, 0), (0, 0), (1, 1)):
+        ids = nb.tokenizer_encode(path, vocab, text, bool(bos), bool(eos))
+        assert ids == TG[f"t{i}/ids{bos}{eos}"].tolist()
+        back = nb.tokenizer_decode(path, vocab, ids if not eos else ids[:-1])
+        assert back == bytes(TG[f"t{i}/text{bos}{eos}"])
+
+
+def test_tokenizer_errors(tmp_path, tokenizer_file):
+    path, vocab = tokenizer_file
+    with pytest.raises(RuntimeError, match="llama2 tokenizer: cannot open"):
+        nb.tokenizer_encode(str(tmp_path / "absent.bin"), vocab, "a")
+    with pytest.raises(RuntimeError, match="llama2 tokenizer: trailing data"):
+        nb.tokenizer_encode(path, vocab - 1, "a")
+    with pytest.raises(RuntimeError, match="malformed vocabulary entry|truncated token"):
+        nb.tokenizer_encode(path, vocab + 1, "a")
+    with pytest.raises(ValueError, match="llama2 tokenizer: invalid vocabulary"):
+        nb.tokenizer_encode(path, 0, "a")
+    with pytest.raises(IndexError, match="llama2 tokenizer: token id out of range"):
+        nb.tokenizer_decode(path, vocab, [5, vocab])
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_FIXTURES),
+                    reason="reference fixtures are only present where the reference is")
+def test_tokenizer_reference_fixture():
+    """The reference's known answer: "H" encodes to the prompt whose greedy
+    continuation {4, 5} decodes to "Hi!" (src/loader_selftest.cpp:82-116)."""
+    tok = os.path.join(REF_FIXTURES, "tiny-llama2.tokenizer")
+    ids = nb.tokenizer_encode(tok, 6, "H")
+    if oracle.reference_available():
+        assert ids == oracle.Reference().llama2c_encode(tok, 6, "H").tolist()
+    assert nb.tokenizer_decode(tok, 6, ids + [4, 5]) == b"Hi!"
