@@ -71,6 +71,25 @@ typedef struct nut_model_view {
     int64_t n_layers;
 } nut_model_view;
 
+/* fp32 ModelWeights / LayerWeights (include/loader.hpp, include/model.hpp:
+ * 26-38) for the `--quant fp32` path: every projection fp32 and [out][in]
+ * (the llama2.c storage; the reference's own ModelWeights holds them
+ * transposed, [in][out]). */
+typedef struct nut_layer_f32_view {
+    const float *query, *key, *value, *output, *gate, *up, *down;
+    const float *attention_norm, *ffn_norm; /* [dim] each */
+} nut_layer_f32_view;
+
+typedef struct nut_model_f32_view {
+    nut_config config;
+    int32_t tied_embeddings;
+    const float *embeddings; /* [vocab][dim] */
+    const float *final_norm; /* [dim] */
+    const float *lm_head;    /* [vocab][dim], ignored when tied */
+    const nut_layer_f32_view *layers;
+    int64_t n_layers;
+} nut_model_f32_view;
+
 /* GenerationStats (include/generate.hpp:19-24), device-event timed. */
 typedef struct nut_generation_stats {
     int64_t prefill_tokens, generated_tokens;
@@ -139,6 +158,12 @@ nut_status nut_matvec_f32(const float *matrix, const float *vector, float *outpu
 /* Copies a QuantizedModelWeights image to `device` (layout private to the
  * library).  Fails with NUT_INVALID_ARGUMENT for an invalid config or a
  * layer whose shape does not match it (src/quant_model.cpp:161-166). */
+/* decode_token / prefill_tokens over fp32 weights (src/kvcache.cpp:237-284)
+ * as a nut_model: the KV cache, decode, prefill, logits and greedy
+ * generation calls below take it like a quantised model (one position per
+ * pass; fp32 matvecs with the reference's matvec_threaded order; the fp32
+ * reference projects with linear_threaded, so parity is by tolerance). */
+nut_status nut_model_create_f32(const nut_model_f32_view *view, int device, nut_model **out);
 nut_status nut_model_create(const nut_model_view *view, int device,
                             nut_model **out);
 nut_status nut_model_destroy(nut_model *model);

@@ -27,7 +27,9 @@ int nut_host_scale_to_half(float value, uint16_t *bits);
 
 /* load_llama2c_quantized_model + generate_tokens_cached (reference
  * include/llama2.hpp:27-29, include/generate.hpp:29-36): loads a llama2.c
- * checkpoint, quantises it (type 0 INT8, 1 INT4) and generates up to
+ * checkpoint, quantises it (type 0 INT8, 1 INT4; type 2 keeps fp32
+ * weights: load_llama2c_model and the ModelWeights overload of
+ * generate_tokens_cached, src/generate.cpp:128-172) and generates up to
  * max_tokens ids after the prompt on the current device, stopping at eos
  * (token 1) like the reference.  temperature <= 0 is greedy; otherwise
  * top-p sampling with std::mt19937(seed).  ids has room for max_tokens;
@@ -43,8 +45,9 @@ int nut_host_llama2c_generate(const char *path, int32_t type, const int32_t *pro
  * vocab_size, max_seq, eos_token, kv_heads), whether the classifier is the
  * embedding table, storage_bytes(), and a 64-bit FNV-1a digest of every
  * loaded byte in this order: embeddings; per layer the data then scales of
- * query, key, value, output, gate, up, down, then the attention and ffn
- * norms; the final norm; the classifier when it is separate. */
+ * query, key, value, output, gate, up, down (type 2: the fp32 [in][out]
+ * matrices), then the attention and ffn norms; the final norm; the
+ * classifier when it is separate. */
 int nut_host_llama2c_inspect(const char *path, int32_t type, int64_t *config,
                              int32_t *tied, uint64_t *storage_bytes, uint64_t *digest);
 

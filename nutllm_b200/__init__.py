@@ -29,6 +29,9 @@ HOST_LIB = os.path.join(LIB_DIR, "libnutllm.so")
 
 INT8 = 0
 INT4 = 1
+# loader type of the llama2.c entries that keeps fp32 weights
+# (load_llama2c_model and the ModelWeights overload of generation)
+FP32 = 2
 
 NUT_OK = 0
 NUT_INVALID_ARGUMENT = 1
@@ -103,6 +106,19 @@ class ModelView(C.Structure):
                 ("layers", C.POINTER(LayerView)), ("n_layers", C.c_int64)]
 
 
+class LayerF32View(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "query", "key", "value", "output", "gate", "up", "down", "attention_norm",
+        "ffn_norm")]
+
+
+class ModelF32View(C.Structure):
+    _fields_ = [("config", Config), ("tied_embeddings", C.c_int32),
+                ("embeddings", C.c_void_p), ("final_norm", C.c_void_p),
+                ("lm_head", C.c_void_p), ("layers", C.POINTER(LayerF32View)),
+                ("n_layers", C.c_int64)]
+
+
 class GenerationStats(C.Structure):
     """GenerationStats (reference include/generate.hpp:19-24)."""
 
@@ -151,6 +167,8 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_matvec_f32", [_P, _P, _P, _I64, _I64, _P])
         _declare(lib, "nut_model_create", [C.POINTER(ModelView), C.c_int,
                                            C.POINTER(_P)])
+        _declare(lib, "nut_model_create_f32", [C.POINTER(ModelF32View), C.c_int,
+                                               C.POINTER(_P)])
         _declare(lib, "nut_model_destroy", [_P])
         _declare(lib, "nut_model_storage_bytes", [_P, C.POINTER(C.c_uint64)])
         _declare(lib, "nut_model_stream", [_P, C.POINTER(_P)])
@@ -306,9 +324,10 @@ def synth_tokens(seed: int, stream: int, n: int, lo: int, hi: int) -> np.ndarray
 def llama2c_generate(path: str, qtype: int, prompt, max_tokens: int,
                      temperature: float = 0.0, top_p: float = 1.0,
                      seed: int = 1) -> tuple[np.ndarray, GenerationStats]:
-    """load_llama2c_quantized_model + generate_tokens_cached through the C++
-    host API (reference include/llama2.hpp:27-29, include/generate.hpp:29-36):
-    stops at eos (token 1) or a full context like the reference."""
+    """load_llama2c_quantized_model (qtype INT8 / INT4) or load_llama2c_model
+    (qtype FP32) + generate_tokens_cached through the C++ host API (reference
+    include/llama2.hpp:27-29, include/generate.hpp:29-36): stops at eos
+    (token 1) or a full context like the reference."""
     lib = host_lib()
     p = np.ascontiguousarray(prompt, np.int32)
     ids = np.zeros(max(max_tokens, 1), np.int32)
@@ -627,7 +646,8 @@ class TPBatch:
 
 
 class DeviceModel:
-    """A QuantizedModelWeights image on one GPU (nut_model)."""
+    """A QuantizedModelWeights image (or, through DeviceModel.fp32, a
+    ModelWeights image) on one GPU (nut_model)."""
 
     def __init__(self, weights: ModelWeights, device: int = 0):
         self.config = Config(**weights.config.as_dict())
@@ -637,6 +657,43 @@ class DeviceModel:
         _check(cuda_lib().nut_model_create(C.byref(view), device, C.byref(h)))
         del keep
         self.handle = h
+
+    @classmethod
+    def fp32(cls, config: Config, embeddings: np.ndarray, layers: Sequence[dict],
+             final_norm: np.ndarray, lm_head: np.ndarray = None,
+             device: int = 0) -> "DeviceModel":
+        """An fp32-weight model (the reference's ModelWeights) on one GPU
+        (nut_model_create_f32).  Each layer is a dict of fp32 arrays: query,
+        key, value, output, gate, up, down as [out][in] (the llama2.c
+        storage), attention_norm and ffn_norm; lm_head None ties the
+        classifier to the embeddings."""
+        self = cls.__new__(cls)
+        self.config = Config(**config.as_dict())
+        self.device = device
+        keep = []
+
+        def arr(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return a.ctypes.data
+
+        lv = (LayerF32View * len(layers))()
+        for i, lw in enumerate(layers):
+            for name in ("query", "key", "value", "output", "gate", "up", "down",
+                         "attention_norm", "ffn_norm"):
+                setattr(lv[i], name, arr(lw[name]))
+        view = ModelF32View()
+        view.config = self.config
+        view.tied_embeddings = int(lm_head is None)
+        view.embeddings = arr(embeddings)
+        view.final_norm = arr(final_norm)
+        view.lm_head = None if lm_head is None else arr(lm_head)
+        view.layers = C.cast(lv, C.POINTER(LayerF32View))
+        view.n_layers = len(layers)
+        h = C.c_void_p()
+        _check(cuda_lib().nut_model_create_f32(C.byref(view), device, C.byref(h)))
+        self.handle = h
+        return self
 
     def storage_bytes(self) -> int:
         out = C.c_uint64(0)

@@ -306,6 +306,8 @@ struct nut_qmatrix {
 struct DevLayer {
     nut::DevQMatrix q, k, v, o, gate, up, down;
     float *attention_norm = nullptr, *ffn_norm = nullptr;
+    /* fp32-weight models: q, k, v, o, gate, up, down as fp32 [out][in] */
+    float *f[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
 struct nut_model {
@@ -314,6 +316,7 @@ struct nut_model {
     int64_t kv_heads = 0;
     int type = 0;
     bool tied = false;
+    bool f32 = false; /* fp32 projections (ModelWeights), per-phase path only */
     float *embeddings = nullptr, *final_norm = nullptr, *lm_head = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr; /* [max_seq][hd/2] */
     std::vector<DevLayer> layers;
@@ -350,6 +353,8 @@ struct nut_model {
             release(l.q), release(l.k), release(l.v), release(l.o);
             release(l.gate), release(l.up), release(l.down);
             dev_free(l.attention_norm), dev_free(l.ffn_norm);
+            for (float *p : l.f)
+                dev_free(p);
         }
         dev_free(embeddings), dev_free(final_norm), dev_free(lm_head);
         dev_free(rope_cos), dev_free(rope_sin);
@@ -364,6 +369,7 @@ struct nut_kv {
     float *hidden = nullptr;                 /* [dim] last hidden */
     float *q = nullptr, *k = nullptr, *v = nullptr, *ctx = nullptr;
     float *gate = nullptr, *up = nullptr, *logits = nullptr;
+    float *x = nullptr, *tmp = nullptr; /* [dim] fp32-weight path scratch */
     unsigned long long *argmax_key = nullptr;
     int32_t *ids = nullptr; /* [max_seq] generated ids */
     bool has_hidden = false;
@@ -398,6 +404,7 @@ struct nut_kv {
             cudaStreamSynchronize(model->stream);
         dev_free(keys), dev_free(values), dev_free(hidden), dev_free(q);
         dev_free(k), dev_free(v), dev_free(ctx), dev_free(gate), dev_free(up);
+        dev_free(x), dev_free(tmp);
         dev_free(logits), dev_free(argmax_key), dev_free(ids);
         dev_free(tagged), dev_free(mk_keys), dev_free(mk_done), dev_free(mk_prompt);
         dev_free(mk_acc), dev_free(mk_cnt);
@@ -427,6 +434,38 @@ void enqueue_decode(nut_model *m, nut_kv *kv, int token, int id_index) {
     nut::launch_embed(m->embeddings, dim, int(c.vocab_size), token,
                       kv->argmax_key,
                       token < 0 ? kv->ids + id_index : nullptr, kv->hidden, s);
+    if (m->f32) {
+        /* decode_token over fp32 weights (src/kvcache.cpp:265-284,
+         * decoder_layer_step :143-171) */
+        const int kvd = KVH * hd, ffn = int(c.ffn_dim);
+        auto mv = [&](const float *w, const float *xin, float *y, int rows, int cols) {
+            cuda_check(nut::matvec_f32(w, xin, y, rows, cols, s), "fp32 projection");
+        };
+        for (int l = 0; l < int(c.layers); l++) {
+            const DevLayer &w = m->layers[size_t(l)];
+            cuda_check(nut::rmsnorm_vec(kv->hidden, w.attention_norm, kv->x, dim, s),
+                       "rmsnorm");
+            mv(w.f[0], kv->x, kv->q, dim, dim);
+            mv(w.f[1], kv->x, kv->k, kvd, dim);
+            mv(w.f[2], kv->x, kv->v, kvd, dim);
+            nut::launch_rope_store(kv->q, kv->k, kv->v, kv->keys, kv->values, m->rope_cos,
+                                   m->rope_sin, pos, l, H, KVH, hd, S, s);
+            nut::launch_attention(kv->q, kv->keys, kv->values, kv->ctx, pos, l, H, KVH, hd, S,
+                                  s);
+            mv(w.f[3], kv->ctx, kv->tmp, dim, dim);
+            cuda_check(nut::add_vec(kv->hidden, kv->tmp, dim, s), "residual");
+            cuda_check(nut::rmsnorm_vec(kv->hidden, w.ffn_norm, kv->x, dim, s), "rmsnorm");
+            mv(w.f[4], kv->x, kv->gate, ffn, dim);
+            mv(w.f[5], kv->x, kv->up, ffn, dim);
+            nut::launch_swiglu(kv->gate, kv->up, ffn, s);
+            mv(w.f[6], kv->gate, kv->tmp, dim, ffn);
+            cuda_check(nut::add_vec(kv->hidden, kv->tmp, dim, s), "residual");
+        }
+        cuda_check(cudaGetLastError(), "decode launch");
+        kv->length++;
+        kv->has_hidden = true;
+        return;
+    }
     for (int l = 0; l < int(c.layers); l++) {
         const DevLayer &w = m->layers[size_t(l)];
         nut::QSegs qkv{};
@@ -478,15 +517,22 @@ void enqueue_logits(nut_model *m, nut_kv *kv) {
     cuda_check(cudaGetLastError(), "lm_head launch");
 }
 
+const char *token_range_message(const nut_model *m) {
+    return m->f32 ? "kv cache: token id out of range" : "quantized decode: token out of range";
+}
+
 void check_decode_args(nut_model *m, nut_kv *kv, int64_t token) {
     if (m == nullptr || kv == nullptr)
         raise(NUT_INVALID_ARGUMENT, "quantized decode: null handle");
     if (kv->model != m)
         raise(NUT_INVALID_ARGUMENT, "quantized decode: cache configuration mismatch");
+    /* the fp32 path keeps decode_token's messages (src/kvcache.cpp:35-41,
+     * 265-276) */
     if (token < 0 || token >= m->cfg.vocab_size)
-        raise(NUT_OUT_OF_RANGE, "quantized decode: token out of range");
+        raise(NUT_OUT_OF_RANGE, token_range_message(m));
     if (kv->length >= m->cfg.max_seq)
-        raise(NUT_LENGTH_ERROR, "quantized decode: context is full");
+        raise(NUT_LENGTH_ERROR,
+              m->f32 ? "kv cache: context is full" : "quantized decode: context is full");
 }
 
 void sync(nut_model *m) { cuda_check(cudaStreamSynchronize(m->stream), "synchronize"); }
@@ -709,6 +755,27 @@ void prefill_batched(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n)
     check_device_error(m->gemm_error, s);
     kv->length = n;
     kv->has_hidden = true;
+}
+
+/* RoPE table with the reference's exact fp32 values: frequency
+ * 10000^(-pair/d) and cos/sin in double, rounded to fp32
+ * (src/quant_model.cpp:26-37). */
+void upload_rope(nut_model *m) {
+    const nut_config &c = m->cfg;
+    const size_t half = size_t(c.head_dim / 2), S = size_t(c.max_seq);
+    std::vector<float> cs(S * half), sn(S * half);
+    for (size_t p = 0; p < S; p++)
+        for (size_t j = 0; j < half; j++) {
+            const double f = std::pow(10000.0, -double(2 * j) / double(c.head_dim));
+            cs[p * half + j] = float(std::cos(double(p) * f));
+            sn[p * half + j] = float(std::sin(double(p) * f));
+        }
+    m->rope_cos = dev_alloc<float>(S * half, "alloc rope");
+    m->rope_sin = dev_alloc<float>(S * half, "alloc rope");
+    cuda_check(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice),
+               "copy rope");
+    cuda_check(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice),
+               "copy rope");
 }
 
 bool use_batched_prefill(const nut_model *m, int64_t n) {
@@ -1025,26 +1092,64 @@ nut_status nut_model_create(const nut_model_view *view, int device,
             bytes += 2 * dim * 4;
         }
         m->storage_bytes = bytes;
-        /* RoPE table with the reference's exact fp32 values: frequency
-         * 10000^(-pair/d) and cos/sin in double, rounded to fp32
-         * (src/quant_model.cpp:26-37). */
-        const size_t half = size_t(c.head_dim / 2), S = size_t(c.max_seq);
-        std::vector<float> cs(S * half), sn(S * half);
-        for (size_t p = 0; p < S; p++)
-            for (size_t j = 0; j < half; j++) {
-                const double f =
-                    std::pow(10000.0, -double(2 * j) / double(c.head_dim));
-                cs[p * half + j] = float(std::cos(double(p) * f));
-                sn[p * half + j] = float(std::sin(double(p) * f));
-            }
-        m->rope_cos = dev_alloc<float>(S * half, "alloc rope");
-        m->rope_sin = dev_alloc<float>(S * half, "alloc rope");
-        cuda_check(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4,
-                              cudaMemcpyHostToDevice),
-                   "copy rope");
-        cuda_check(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4,
-                              cudaMemcpyHostToDevice),
-                   "copy rope");
+        upload_rope(m.get());
+        settle_uploads();
+        *out = m.release();
+    });
+}
+
+nut_status nut_model_create_f32(const nut_model_f32_view *view, int device, nut_model **out) {
+    return guarded([&] {
+        if (view == nullptr || out == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "model: null argument");
+        const nut_config &c = view->config;
+        validate_config(c);
+        if (view->n_layers != c.layers || view->layers == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "kv cache: layer count mismatch");
+        if (view->embeddings == nullptr || view->final_norm == nullptr ||
+            (!view->tied_embeddings && view->lm_head == nullptr))
+            raise(NUT_INVALID_ARGUMENT, "model: null fp32 tensor");
+        DeviceScope scope(device);
+        auto m = std::make_unique<nut_model>();
+        m->device = device;
+        m->cfg = c;
+        m->kv_heads = c.kv_heads == 0 ? c.heads : c.kv_heads;
+        m->type = -1;
+        m->f32 = true;
+        m->tied = view->tied_embeddings != 0;
+        m->prefill_min = 0; /* the fp32 path has no GEMM prefill */
+        cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking),
+                   "create stream");
+        const size_t dim = size_t(c.dim), V = size_t(c.vocab_size), ffn = size_t(c.ffn_dim);
+        const size_t kvd = size_t(m->kv_heads * c.head_dim);
+        uint64_t bytes = 0;
+        auto up = [&](const float *src, size_t n, const char *what) {
+            if (src == nullptr)
+                raise(NUT_INVALID_ARGUMENT, "model: null fp32 tensor");
+            float *p = dev_alloc<float>(n, what);
+            cuda_check(cudaMemcpy(p, src, n * 4, cudaMemcpyHostToDevice), what);
+            bytes += n * 4;
+            return p;
+        };
+        m->embeddings = up(view->embeddings, V * dim, "copy embeddings");
+        m->final_norm = up(view->final_norm, dim, "copy final norm");
+        if (!m->tied)
+            m->lm_head = up(view->lm_head, V * dim, "copy lm_head");
+        for (int64_t l = 0; l < c.layers; l++) {
+            const nut_layer_f32_view &lv = view->layers[l];
+            m->layers.emplace_back();
+            DevLayer &d = m->layers.back();
+            const float *src[7] = {lv.query, lv.key, lv.value, lv.output, lv.gate, lv.up,
+                                   lv.down};
+            const size_t n[7] = {dim * dim, kvd * dim, kvd * dim, dim * dim, ffn * dim,
+                                 ffn * dim, dim * ffn};
+            for (int j = 0; j < 7; j++)
+                d.f[j] = up(src[j], n[j], "copy fp32 weights");
+            d.attention_norm = up(lv.attention_norm, dim, "copy norm");
+            d.ffn_norm = up(lv.ffn_norm, dim, "copy norm");
+        }
+        m->storage_bytes = bytes;
+        upload_rope(m.get());
         settle_uploads();
         *out = m.release();
     });
@@ -1107,6 +1212,8 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
         cuda_check(cudaMemset(kv->values, 0, n * 4), "clear values");
         const size_t kvd = size_t(model->kv_heads * c.head_dim);
         kv->hidden = dev_alloc<float>(size_t(c.dim), "alloc hidden");
+        kv->x = dev_alloc<float>(size_t(c.dim), "alloc scratch");
+        kv->tmp = dev_alloc<float>(size_t(c.dim), "alloc scratch");
         kv->q = dev_alloc<float>(size_t(c.dim), "alloc q");
         kv->k = dev_alloc<float>(kvd, "alloc k");
         kv->v = dev_alloc<float>(kvd, "alloc v");
@@ -1259,7 +1366,7 @@ nut_status nut_prefill(nut_model *model, nut_kv *kv, const int32_t *tokens,
         DeviceScope scope(model->device);
         for (int64_t i = 0; i < n; i++)
             if (tokens[i] < 0 || tokens[i] >= model->cfg.vocab_size)
-                raise(NUT_OUT_OF_RANGE, "quantized decode: token out of range");
+                raise(NUT_OUT_OF_RANGE, token_range_message(model));
         if (use_batched_prefill(model, n)) {
             prefill_batched(model, kv, tokens, n);
         } else if (model->mk) {
@@ -1317,7 +1424,7 @@ nut_status nut_generate_greedy(nut_model *model, nut_kv *kv,
             raise(NUT_INVALID_ARGUMENT, "generation: invalid output");
         for (int64_t i = 0; i < n; i++)
             if (prompt[i] < 0 || prompt[i] >= c.vocab_size)
-                raise(NUT_OUT_OF_RANGE, "quantized decode: token out of range");
+                raise(NUT_OUT_OF_RANGE, token_range_message(model));
         DeviceScope scope(model->device);
         cudaStream_t s = model->stream;
         kv->length = 0;

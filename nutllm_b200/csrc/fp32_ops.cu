@@ -196,3 +196,51 @@ cudaError_t matvec_f32(const float *W, const float *x, float *y, int rows, int c
 }
 
 } // namespace nut
+
+/* ---- fp32-weight decode helpers ------------------------------------- */
+
+namespace nut {
+namespace {
+
+/* out = x * (1 / sqrt(mean(x^2) + eps)) * w, one CTA (src/ops.cpp:111-134;
+ * the sum of squares is reduced in a different order than the reference's
+ * eight lanes, within the parity tolerance). */
+__global__ void rmsnorm_vec_kernel(const float *x, const float *w, float *out, int n) {
+    __shared__ float red[32];
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        ss = fmaf(x[k], x[k], ss);
+    for (int o = 16; o > 0; o >>= 1)
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.0f;
+    for (int i = 0; i < int(blockDim.x >> 5); i++)
+        total += red[i];
+    const float scale = 1.0f / sqrtf(total / float(n) + 1e-5f);
+    for (int k = threadIdx.x; k < n; k += blockDim.x)
+        out[k] = x[k] * scale * w[k];
+}
+
+__global__ void add_vec_kernel(float *h, const float *y, int n) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k < n)
+        h[k] += y[k];
+}
+
+} // namespace
+
+cudaError_t rmsnorm_vec(const float *x, const float *w, float *out, int n, cudaStream_t s) {
+    rmsnorm_vec_kernel<<<1, 1024, 0, s>>>(x, w, out, n);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t add_vec(float *h, const float *y, int n, cudaStream_t s) {
+    add_vec_kernel<<<(n + 255) / 256, 256, 0, s>>>(h, y, n);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+} // namespace nut

@@ -24,6 +24,10 @@ void uncount_launches(uint64_t n);
  * column-sequential). */
 cudaError_t matmul_f32(const float *A, const float *B, float *C, int M, int K, int N,
                        cudaStream_t s);
+/* fp32-weight decode helpers (fp32_ops.cu): one-vector rmsnorm
+ * (eps 1e-5) and h += y. */
+cudaError_t rmsnorm_vec(const float *x, const float *w, float *out, int n, cudaStream_t s);
+cudaError_t add_vec(float *h, const float *y, int n, cudaStream_t s);
 cudaError_t matvec_f32(const float *W, const float *x, float *y, int rows, int cols,
                        cudaStream_t s);
 

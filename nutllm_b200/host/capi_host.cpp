@@ -44,6 +44,23 @@ QuantType quant_type(int32_t type) {
     return type == 0 ? QuantType::int8 : QuantType::int4;
 }
 
+/* The loader type that selects load_llama2c_model (fp32 weights). */
+constexpr int32_t kFp32 = 2;
+
+void describe(const ModelConfig &c, bool is_tied, size_t bytes, int64_t *config, int32_t *tied,
+              uint64_t *storage_bytes) {
+    if (config != nullptr) {
+        const size_t v[9] = {c.layers,     c.heads,   c.dim,       c.head_dim, c.ffn_dim,
+                             c.vocab_size, c.max_seq, c.eos_token, c.kv_heads};
+        for (int i = 0; i < 9; i++)
+            config[i] = int64_t(v[i]);
+    }
+    if (tied != nullptr)
+        *tied = is_tied ? 1 : 0;
+    if (storage_bytes != nullptr)
+        *storage_bytes = uint64_t(bytes);
+}
+
 /* 64-bit FNV-1a over a byte stream. */
 struct Fnv1a {
     uint64_t h = 0xcbf29ce484222325ull;
@@ -92,15 +109,18 @@ int nut_host_llama2c_generate(const char *path, int32_t type, const int32_t *pro
         if (path == nullptr || prompt == nullptr || n_out == nullptr || max_tokens < 0 ||
             (max_tokens > 0 && ids == nullptr) || n < 0)
             throw std::invalid_argument("generation: invalid argument");
-        const QuantizedModelWeights model = load_llama2c_quantized_model(path, quant_type(type));
         SamplingConfig sampling;
         sampling.max_tokens = size_t(max_tokens);
         sampling.temperature = temperature;
         sampling.top_p = top_p;
         sampling.seed = seed;
         GenerationStats st;
+        const std::vector<int> tokens(prompt, prompt + n);
         const std::vector<int> out =
-            generate_tokens_cached(model, std::vector<int>(prompt, prompt + n), sampling, &st);
+            type == kFp32 ? generate_tokens_cached(load_llama2c_model(path), tokens, sampling, &st)
+                          : generate_tokens_cached(
+                                load_llama2c_quantized_model(path, quant_type(type)), tokens,
+                                sampling, &st);
         std::copy(out.begin(), out.end(), ids);
         *n_out = int64_t(out.size());
         if (stats != nullptr) {
@@ -117,18 +137,29 @@ int nut_host_llama2c_inspect(const char *path, int32_t type, int64_t *config,
     return guarded([&] {
         if (path == nullptr)
             throw std::invalid_argument("llama2 checkpoint: null path");
-        const QuantizedModelWeights m = load_llama2c_quantized_model(path, quant_type(type));
-        const ModelConfig &c = m.config;
-        if (config != nullptr) {
-            const size_t v[9] = {c.layers,     c.heads,   c.dim,       c.head_dim, c.ffn_dim,
-                                 c.vocab_size, c.max_seq, c.eos_token, c.kv_heads};
-            for (int i = 0; i < 9; i++)
-                config[i] = int64_t(v[i]);
+        if (type == kFp32) {
+            const ModelWeights m = load_llama2c_model(path);
+            describe(m.config, m.tied_embeddings, m.storage_bytes(), config, tied,
+                     storage_bytes);
+            if (digest != nullptr) {
+                Fnv1a f;
+                f.add(m.embeddings.data(), m.embeddings.size() * sizeof(float));
+                for (const LayerWeights &l : m.layers) {
+                    for (const Matrix *q :
+                         {&l.query, &l.key, &l.value, &l.output, &l.gate, &l.up, &l.down})
+                        f.add(q->data(), q->size() * sizeof(float));
+                    f.add(l.attention_norm);
+                    f.add(l.ffn_norm);
+                }
+                f.add(m.final_norm);
+                if (!m.tied_embeddings)
+                    f.add(m.lm_head.data(), m.lm_head.size() * sizeof(float));
+                *digest = f.h;
+            }
+            return;
         }
-        if (tied != nullptr)
-            *tied = m.tied_embeddings ? 1 : 0;
-        if (storage_bytes != nullptr)
-            *storage_bytes = uint64_t(m.storage_bytes());
+        const QuantizedModelWeights m = load_llama2c_quantized_model(path, quant_type(type));
+        describe(m.config, m.tied_embeddings, m.storage_bytes(), config, tied, storage_bytes);
         if (digest != nullptr) {
             Fnv1a f;
             f.add(m.embeddings.data(), m.embeddings.size() * sizeof(float));

@@ -1,4 +1,4 @@
-/* generate_tokens_cached for quantised models over the C ABI, and the
+/* generate_tokens_cached for quantised and fp32 models over the C ABI, and the
  * host token sampler.  The sampler keeps the reference's arithmetic
  * (src/generate.cpp:25-73) step for step, because a seeded draw only picks
  * the same token when every intermediate value is the same:
@@ -19,6 +19,7 @@
 
 #include "device.hpp"
 #include "kvcache.hpp"
+#include "loader.hpp"
 #include "quant_model.hpp"
 
 size_t choose_token(const std::vector<float> &logits, const SamplingConfig &sampling,
@@ -75,11 +76,10 @@ double seconds_since(std::chrono::steady_clock::time_point start) {
     return std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
 }
 
-std::vector<int> generate_greedy(const QuantizedModelWeights &model,
-                                 const std::vector<int> &prompt,
+/* Both model kinds run the loop through one nut_model. */
+std::vector<int> generate_greedy(nut_model *m, const std::vector<int> &prompt,
                                  const SamplingConfig &sampling, KVCache &cache,
                                  GenerationStats *stats) {
-    nut_model *m = model.device();
     nut_kv *kv = cache.device(m);
     const std::vector<int32_t> ids32(prompt.begin(), prompt.end());
     std::vector<int32_t> out(std::max<size_t>(sampling.max_tokens, 1));
@@ -97,24 +97,26 @@ std::vector<int> generate_greedy(const QuantizedModelWeights &model,
     return std::vector<int>(out.begin(), out.begin() + produced);
 }
 
-std::vector<int> generate_sampled(const QuantizedModelWeights &model,
+/* `prefill` fills the cache from the prompt (the model kind's own prefill
+ * and messages). */
+template <typename Prefill>
+std::vector<int> generate_sampled(nut_model *m, const ModelConfig &config,
                                   const std::vector<int> &prompt,
                                   const SamplingConfig &sampling, KVCache &cache,
-                                  GenerationStats *stats) {
+                                  GenerationStats *stats, Prefill &&prefill) {
     const auto prefill_start = std::chrono::steady_clock::now();
-    prefill_quantized(model, prompt, cache, sampling.threads);
+    prefill();
     const double prefill_seconds = seconds_since(prefill_start);
 
-    nut_model *m = model.device();
     nut_kv *kv = cache.device(m);
-    std::vector<float> logits(model.config.vocab_size);
+    std::vector<float> logits(config.vocab_size);
     std::vector<int> generated;
     std::mt19937 rng(sampling.seed);
     const auto decode_start = std::chrono::steady_clock::now();
     while (generated.size() < sampling.max_tokens && cache.length() < cache.capacity()) {
         nutdev::check(nut_logits(m, kv, logits.data(), nullptr));
         const size_t token = choose_token(logits, sampling, rng);
-        if (token == model.config.eos_token)
+        if (token == config.eos_token)
             break;
         generated.push_back(int(token));
         nutdev::check(nut_decode_token(m, kv, int32_t(token), nullptr));
@@ -128,19 +130,39 @@ std::vector<int> generate_sampled(const QuantizedModelWeights &model,
     return generated;
 }
 
+void check_generation(const ModelConfig &config, const std::vector<int> &prompt,
+                      const SamplingConfig &sampling) {
+    config.validate();
+    if (prompt.empty() || prompt.size() > config.max_seq)
+        throw std::invalid_argument("generation: invalid prompt length");
+    if (sampling.threads == 0)
+        throw std::invalid_argument("generation: zero threads");
+}
+
 } // namespace
 
 std::vector<int> generate_tokens_cached(const QuantizedModelWeights &model,
                                         const std::vector<int> &prompt,
                                         const SamplingConfig &sampling,
                                         GenerationStats *stats) {
-    model.config.validate();
-    if (prompt.empty() || prompt.size() > model.config.max_seq)
-        throw std::invalid_argument("generation: invalid prompt length");
-    if (sampling.threads == 0)
-        throw std::invalid_argument("generation: zero threads");
+    check_generation(model.config, prompt, sampling);
     KVCache cache(model.config);
     if (sampling.temperature <= 0.0f)
-        return generate_greedy(model, prompt, sampling, cache, stats);
-    return generate_sampled(model, prompt, sampling, cache, stats);
+        return generate_greedy(model.device(), prompt, sampling, cache, stats);
+    return generate_sampled(model.device(), model.config, prompt, sampling, cache, stats,
+                            [&] { prefill_quantized(model, prompt, cache, sampling.threads); });
+}
+
+/* The fp32 overload (src/generate.cpp:128-172): prefill_tokens, then per
+ * step final norm + classifier, choice, decode_token. */
+std::vector<int> generate_tokens_cached(const ModelWeights &model,
+                                        const std::vector<int> &prompt,
+                                        const SamplingConfig &sampling,
+                                        GenerationStats *stats) {
+    check_generation(model.config, prompt, sampling);
+    KVCache cache(model.config);
+    if (sampling.temperature <= 0.0f)
+        return generate_greedy(model.device(), prompt, sampling, cache, stats);
+    return generate_sampled(model.device(), model.config, prompt, sampling, cache, stats,
+                            [&] { prefill_tokens(model, prompt, cache, sampling.threads); });
 }

@@ -1,7 +1,7 @@
 #pragma once
 /* Generation — host side of the drop-in for the reference's
- * include/generate.hpp:11-36 (quantised overload of generate_tokens_cached,
- * src/generate.cpp:174-216).
+ * include/generate.hpp:11-36 (both overloads of generate_tokens_cached,
+ * src/generate.cpp:128-216).
  *
  * temperature <= 0 (greedy) runs the whole loop on the device
  * (nut_generate_greedy: prefill, then final norm + classifier + argmax and
@@ -16,6 +16,7 @@
 #include <vector>
 
 struct QuantizedModelWeights;
+struct ModelWeights;
 
 struct SamplingConfig {
     size_t max_tokens = 32;
@@ -33,6 +34,11 @@ struct GenerationStats {
 };
 
 std::vector<int> generate_tokens_cached(const QuantizedModelWeights &model,
+                                        const std::vector<int> &prompt,
+                                        const SamplingConfig &sampling,
+                                        GenerationStats *stats = nullptr);
+/* The fp32-weight overload (src/generate.cpp:128-172), same loop. */
+std::vector<int> generate_tokens_cached(const ModelWeights &model,
                                         const std::vector<int> &prompt,
                                         const SamplingConfig &sampling,
                                         GenerationStats *stats = nullptr);

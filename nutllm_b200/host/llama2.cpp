@@ -200,7 +200,45 @@ std::vector<std::vector<float>> read_norms(Checkpoint &file, size_t first, size_
     return norms;
 }
 
+/* One stored [out][in] projection of a layer into the reference's
+ * [in][out] Matrix (transpose_external, src/llama2.cpp:300-337). */
+void read_transposed(Checkpoint &file, size_t first, Matrix &dst, std::vector<float> &raw) {
+    const size_t in = dst.rows(), out = dst.cols();
+    raw.resize(in * out);
+    file.read(raw.data(), first, raw.size());
+    for (size_t o = 0; o < out; o++)
+        for (size_t i = 0; i < in; i++)
+            dst.data()[i * out + o] = raw[o * in + i];
+}
+
 } // namespace
+
+ModelWeights load_llama2c_model(const std::string &path) {
+    Checkpoint file(path);
+    const Sections s = parse(file);
+    const ModelConfig &c = s.config;
+    ModelWeights model(c, !s.shared_classifier);
+    model.tied_embeddings = s.shared_classifier;
+    file.read(model.embeddings.data(), s.embeddings, c.vocab_size * c.dim);
+    file.read(model.final_norm.data(), s.final_norm, c.dim);
+    if (!s.shared_classifier)
+        file.read(model.lm_head.data(), s.classifier, c.vocab_size * c.dim);
+    const size_t att = c.dim * c.dim, kv = c.dim * c.kv_dim(), ff = c.dim * c.ffn_dim;
+    std::vector<float> raw;
+    for (size_t l = 0; l < c.layers; l++) {
+        LayerWeights &d = model.layers[l];
+        file.read(d.attention_norm.data(), s.attention_norms + l * c.dim, c.dim);
+        file.read(d.ffn_norm.data(), s.ffn_norms + l * c.dim, c.dim);
+        read_transposed(file, s.wq + l * att, d.query, raw);
+        read_transposed(file, s.wk + l * kv, d.key, raw);
+        read_transposed(file, s.wv + l * kv, d.value, raw);
+        read_transposed(file, s.wo + l * att, d.output, raw);
+        read_transposed(file, s.w1 + l * ff, d.gate, raw);
+        read_transposed(file, s.w2 + l * ff, d.down, raw);
+        read_transposed(file, s.w3 + l * ff, d.up, raw);
+    }
+    return model;
+}
 
 QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, QuantType type) {
     Checkpoint file(path);

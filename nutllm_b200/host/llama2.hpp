@@ -1,7 +1,7 @@
 #pragma once
-/* llama2.c checkpoint loader — host side of the drop-in for the reference's
- * load_llama2c_quantized_model (include/llama2.hpp:27-29,
- * src/llama2.cpp:199-298,339-412).
+/* llama2.c checkpoint loaders — host side of the drop-in for the reference's
+ * load_llama2c_model and load_llama2c_quantized_model (include/llama2.hpp:
+ * 27-29, src/llama2.cpp:199-412).
  *
  * File format (llama2.c "legacy" export): seven int32 — dim, ffn_dim,
  * layers, heads, kv_heads, vocab (negative: separate classifier follows),
@@ -17,10 +17,14 @@
 #include <unordered_map>
 #include <vector>
 
+#include "loader.hpp"
 #include "quant.hpp"
 #include "quant_model.hpp"
 
 QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, QuantType type);
+/* The fp32 loader (src/llama2.cpp:300-337): the same file into ModelWeights,
+ * projections transposed to the reference's [in][out] storage. */
+ModelWeights load_llama2c_model(const std::string &path);
 
 /* The llama2.c tokenizer (include/llama2.hpp:11-25, src/llama2.cpp:414-543),
  * host text I/O around the token loop.

@@ -165,8 +165,17 @@ class Oracle:
                                                temperature, top_p, seed, _ptr(out)))
         return out
 
+    def rope(self, values: np.ndarray, position: int) -> np.ndarray:
+        """rotate_vector of one head (src/kvcache.cpp:48-59), in place."""
+        assert values.dtype == np.float32 and values.flags.c_contiguous
+        self.lib.orc_rope(_ptr(values), values.size, position)
+        return values
+
     def model(self, weights) -> "OracleModel":
         return OracleModel(self, weights)
+
+    def fp32_model(self, tensors: dict) -> "Fp32Model":
+        return Fp32Model(self, tensors)
 
 
 class OracleModel:
@@ -240,6 +249,109 @@ class OracleModel:
             C.byref(self._model), C.byref(self.kv), _ptr(p), p.size, max_tokens,
             temperature, top_p, seed, _ptr(ids), C.byref(n)))
         return ids[:n.value]
+
+
+class Fp32Model:
+    """The fp32-weight decoder (ModelWeights) of a llama2.c checkpoint,
+    restated from decode_token / decoder_layer_step / attention_step
+    (src/kvcache.cpp:35-171,265-284) and generate_tokens_cached
+    (src/generate.cpp:128-172) over read_llama2c's tensors.
+
+    Projections follow linear_threaded (src/threading.cpp:200-214: for an
+    [in][out] matrix, each output is an in-order chain of multiply-adds),
+    which is matmul_threaded of one row, so they run through orc_matmul_f32
+    on the transposed ([in][out]) matrices; the classifier follows
+    matvec_threaded.  Attention keeps the reference's double dot products and
+    weighted sums.  The prompt runs one position at a time (the reference's
+    prefill_tokens computes the same rows as whole-matrix products, equal up
+    to rounding order); ids are pinned against the reference's goldens."""
+
+    def __init__(self, oracle: Oracle, t: dict):
+        self.o = oracle
+        c = t["config"]
+        self.c = c
+        self.kvh = c["kv_heads"] or c["heads"]
+        T = lambda a: np.ascontiguousarray(np.swapaxes(a, -1, -2))  # noqa: E731
+        self.wq, self.wk, self.wv, self.wo = T(t["wq"]), T(t["wk"]), T(t["wv"]), T(t["wo"])
+        self.gate, self.down, self.up = T(t["w1"]), T(t["w2"]), T(t["w3"])
+        self.att_norm, self.ffn_norm = t["attention_norm"], t["ffn_norm"]
+        self.emb = np.ascontiguousarray(t["embeddings"])
+        self.final_norm = np.ascontiguousarray(t["final_norm"])
+        self.cls = self.emb if t["tied"] else np.ascontiguousarray(t["classifier"])
+        hd, S = c["head_dim"], c["max_seq"]
+        self.keys = np.zeros((c["layers"], self.kvh, S, hd), np.float32)
+        self.values = np.zeros_like(self.keys)
+        self.length = 0
+
+    def _linear(self, x, w):
+        return self.o.matmul_f32(x[None, :], w)[0]
+
+    def decode(self, token: int) -> np.ndarray:
+        c, o = self.c, self.o
+        if not 0 <= token < c["vocab_size"]:
+            raise IndexError("kv cache: token id out of range")
+        if self.length >= c["max_seq"]:
+            raise OverflowError("kv cache: context is full")
+        pos, hd, H = self.length, c["head_dim"], c["heads"]
+        h = self.emb[token].copy()
+        scale = np.float32(1.0) / np.sqrt(np.float32(hd))
+        group = H // self.kvh
+        for l in range(c["layers"]):
+            x = o.rmsnorm(h, self.att_norm[l])
+            q = self._linear(x, self.wq[l])
+            k = self._linear(x, self.wk[l])
+            v = self._linear(x, self.wv[l])
+            for hh in range(H):
+                seg = np.ascontiguousarray(q[hh * hd:(hh + 1) * hd])
+                q[hh * hd:(hh + 1) * hd] = o.rope(seg, pos)
+            for hh in range(self.kvh):
+                seg = np.ascontiguousarray(k[hh * hd:(hh + 1) * hd])
+                self.keys[l, hh, pos] = o.rope(seg, pos)
+                self.values[l, hh, pos] = v[hh * hd:(hh + 1) * hd]
+            ctx = np.zeros(c["dim"], np.float32)
+            for hh in range(H):
+                K = self.keys[l, hh // group, :pos + 1].astype(np.float64)
+                V = self.values[l, hh // group, :pos + 1].astype(np.float64)
+                qh = q[hh * hd:(hh + 1) * hd].astype(np.float64)
+                sc = (K @ qh).astype(np.float32) * scale
+                e = np.exp(sc - sc.max()).astype(np.float32)
+                total = np.float32(e.astype(np.float64).sum())
+                wts = (e / total).astype(np.float64)
+                ctx[hh * hd:(hh + 1) * hd] = (wts @ V).astype(np.float32)
+            h = (h + self._linear(ctx, self.wo[l])).astype(np.float32)
+            x = o.rmsnorm(h, self.ffn_norm[l])
+            g = self._linear(x, self.gate[l])
+            u = self._linear(x, self.up[l])
+            act = (g / (np.float32(1) + np.exp(-g)) * u).astype(np.float32)
+            h = (h + self._linear(act, self.down[l])).astype(np.float32)
+        self.length += 1
+        return h
+
+    def logits(self, hidden: np.ndarray) -> np.ndarray:
+        return self.o.matvec_f32(self.cls, self.o.rmsnorm(hidden, self.final_norm))
+
+    def generate_cached(self, prompt, max_tokens: int, temperature: float = 0.0,
+                        top_p: float = 1.0, seed: int = 1):
+        """(ids, logits per step): eos stop (token 1) and context limit; a
+        sampled run replays one seeded generator over the rows so far."""
+        c = self.c
+        if len(prompt) == 0 or len(prompt) > c["max_seq"]:
+            raise ValueError("generation: invalid prompt length")
+        self.length = 0
+        for t in prompt:
+            h = self.decode(int(t))
+        ids, rows = [], []
+        while len(ids) < max_tokens and self.length < c["max_seq"]:
+            rows.append(self.logits(h))
+            if temperature <= 0:
+                tok = int(np.argmax(rows[-1]))
+            else:
+                tok = int(self.o.choose_tokens(np.stack(rows), temperature, top_p, seed)[-1])
+            if tok == c["eos_token"]:
+                break
+            ids.append(tok)
+            h = self.decode(tok)
+        return np.array(ids, np.int32), rows
 
 
 # ------------------------------------------------------------- reference
@@ -385,7 +497,8 @@ class Reference:
 
     def llama2c_generate(self, path: str, qtype: int, prompt, max_tokens: int,
                          temperature: float = 0.0, top_p: float = 1.0, seed: int = 1):
-        """load_llama2c_quantized_model + generate_tokens_cached (eos stop)."""
+        """load_llama2c_quantized_model (qtype 0 / 1) or load_llama2c_model
+        (qtype 2) + generate_tokens_cached (eos stop)."""
         p = np.ascontiguousarray(prompt, np.int32)
         ids = np.zeros(max(max_tokens, 1), np.int32)
         n = C.c_size_t(0)

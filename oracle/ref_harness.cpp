@@ -377,15 +377,18 @@ int ref_llama2c_generate(const char *path, int type, const int *prompt,
                          size_t n, size_t max_tokens, float temperature,
                          float top_p, unsigned seed, int *ids, size_t *n_out) {
     return guarded([&] {
-        QuantizedModelWeights model =
-            load_llama2c_quantized_model(path, to_type(type));
         SamplingConfig sampling;
         sampling.max_tokens = max_tokens;
         sampling.temperature = temperature;
         sampling.top_p = top_p;
         sampling.seed = seed;
-        const std::vector<int> out = generate_tokens_cached(
-            model, std::vector<int>(prompt, prompt + n), sampling);
+        const std::vector<int> tokens(prompt, prompt + n);
+        /* type 2: the fp32 loader and the ModelWeights overload */
+        const std::vector<int> out =
+            type == 2 ? generate_tokens_cached(load_llama2c_model(path), tokens, sampling)
+                      : generate_tokens_cached(
+                            load_llama2c_quantized_model(path, to_type(type)), tokens,
+                            sampling);
         std::copy(out.begin(), out.end(), ids);
         *n_out = out.size();
     });
@@ -398,16 +401,6 @@ int ref_llama2c_generate(const char *path, int type, const int *prompt,
 int ref_llama2c_inspect(const char *path, int type, int64_t *config,
                         int *tied, uint64_t *storage_bytes, uint64_t *digest) {
     return guarded([&] {
-        const QuantizedModelWeights m =
-            load_llama2c_quantized_model(path, to_type(type));
-        const ModelConfig &c = m.config;
-        const size_t v[9] = {c.layers,     c.heads,   c.dim,
-                             c.head_dim,   c.ffn_dim, c.vocab_size,
-                             c.max_seq,    c.eos_token, c.kv_heads};
-        for (int i = 0; i < 9; i++)
-            config[i] = int64_t(v[i]);
-        *tied = m.tied_embeddings ? 1 : 0;
-        *storage_bytes = m.storage_bytes();
         uint64_t h = 0xcbf29ce484222325ull;
         auto add = [&h](const void *p, size_t bytes) {
             const unsigned char *b = static_cast<const unsigned char *>(p);
@@ -416,6 +409,35 @@ int ref_llama2c_inspect(const char *path, int type, int64_t *config,
                 h *= 0x100000001b3ull;
             }
         };
+        auto describe = [&](const ModelConfig &c, bool is_tied, size_t bytes) {
+            const size_t v[9] = {c.layers,     c.heads,   c.dim,
+                                 c.head_dim,   c.ffn_dim, c.vocab_size,
+                                 c.max_seq,    c.eos_token, c.kv_heads};
+            for (int i = 0; i < 9; i++)
+                config[i] = int64_t(v[i]);
+            *tied = is_tied ? 1 : 0;
+            *storage_bytes = bytes;
+        };
+        if (type == 2) {
+            const ModelWeights m = load_llama2c_model(path);
+            describe(m.config, m.tied_embeddings, m.storage_bytes());
+            add(m.embeddings.data(), m.embeddings.size() * 4);
+            for (const LayerWeights &l : m.layers) {
+                for (const Matrix *q : {&l.query, &l.key, &l.value, &l.output,
+                                        &l.gate, &l.up, &l.down})
+                    add(q->data(), q->size() * 4);
+                add(l.attention_norm.data(), l.attention_norm.size() * 4);
+                add(l.ffn_norm.data(), l.ffn_norm.size() * 4);
+            }
+            add(m.final_norm.data(), m.final_norm.size() * 4);
+            if (!m.tied_embeddings)
+                add(m.lm_head.data(), m.lm_head.size() * 4);
+            *digest = h;
+            return;
+        }
+        const QuantizedModelWeights m =
+            load_llama2c_quantized_model(path, to_type(type));
+        describe(m.config, m.tied_embeddings, m.storage_bytes());
         add(m.embeddings.data(), m.embeddings.size() * 4);
         for (const QuantizedLayerWeights &l : m.layers) {
             for (const QuantizedMatrix *q : {&l.query, &l.key, &l.value,

@@ -15,10 +15,12 @@ Run here, where the reference builds (``make -C oracle ref``), to refresh
 
     python tests/golden/make_llama2c_fixture.py
 
-For each checkpoint and quantisation type it records the reference loader's
-config, tied flag, storage_bytes() and byte digest, and the ids of the
-reference's generate_tokens_cached: greedy, and top-p sampled with a fixed
-seed, both with the reference's eos stop (token 1) and context limit.
+For each checkpoint and loader type (INT8, INT4 through
+load_llama2c_quantized_model; fp32 through load_llama2c_model) it records the
+reference loader's config, tied flag, storage_bytes() and byte digest, and
+the ids of the reference's generate_tokens_cached: greedy, and top-p sampled
+with a fixed seed, both with the reference's eos stop (token 1) and context
+limit.
 """
 from __future__ import annotations
 
@@ -171,7 +173,7 @@ def main() -> None:
                 hashlib.sha256(open(path, "rb").read()).digest(), np.uint8)
             prompt = prompt_of(name)
             out[f"{name}/prompt"] = prompt
-            for qtype, qname in ((0, "int8"), (1, "int4")):
+            for qtype, qname in ((0, "int8"), (1, "int4"), (2, "fp32")):
                 cfg, tied, nbytes, digest = ref.llama2c_inspect(path, qtype)
                 key = f"{name}/{qname}"
                 out[f"{key}/config"] = np.array(cfg, np.int64)

@@ -1,7 +1,7 @@
-"""llama2.c checkpoints end to end: the host loader (load_llama2c_quantized_model,
-reference src/llama2.cpp:199-412), the generation sampler (choose_token,
-src/generate.cpp:25-73) and generate_tokens_cached (src/generate.cpp:174-216)
-through the C++ host API.
+"""llama2.c checkpoints end to end: the host loaders (load_llama2c_quantized_model
+and the fp32 load_llama2c_model, reference src/llama2.cpp:199-412), the
+generation sampler (choose_token, src/generate.cpp:25-73) and both overloads
+of generate_tokens_cached (src/generate.cpp:128-216) through the C++ host API.
 
 Checkpoints are rebuilt from seeds by tests/golden/make_llama2c_fixture.py;
 the goldens in tests/golden/llama2c_golden.npz were produced by the
@@ -20,7 +20,7 @@ from tests.conftest import golden_path
 from tests.golden import make_llama2c_fixture as fx
 
 G = np.load(golden_path("llama2c_golden.npz"))
-QTYPES = ((0, "int8"), (1, "int4"))
+QTYPES = ((0, "int8"), (1, "int4"), (2, "fp32"))
 REF_FIXTURES = os.path.join(os.environ.get("NUTLLM_REFERENCE", "/root/reference"),
                             "tests", "fixtures")
 
@@ -82,12 +82,17 @@ def test_host_loader_matches_reference_bytes(checkpoints, name, qtype, qname):
 def test_oracle_generation_matches_reference(orc, checkpoints, name, qtype, qname):
     """The oracle's generate_tokens_cached (eos stop, context limit, greedy
     and seeded top-p) gives the reference's ids on the reference's bytes."""
-    m = orc.model(_oracle_model(orc, checkpoints[name], qtype))
     c = fx.config_of(name)
     prompt = G[f"{name}/prompt"]
     key = f"{name}/{qname}"
-    assert m.generate_cached(prompt, c["max_tokens"]).tolist() == G[f"{key}/greedy"].tolist()
-    assert (m.generate_cached(prompt, c["max_tokens"], **fx.SAMPLING).tolist()
+    if qtype == nb.FP32:
+        m = orc.fp32_model(oracle.read_llama2c(checkpoints[name]))
+        gen = lambda *a, **k: m.generate_cached(*a, **k)[0]  # noqa: E731
+    else:
+        m = orc.model(_oracle_model(orc, checkpoints[name], qtype))
+        gen = m.generate_cached
+    assert gen(prompt, c["max_tokens"]).tolist() == G[f"{key}/greedy"].tolist()
+    assert (gen(prompt, c["max_tokens"], **fx.SAMPLING).tolist()
             == G[f"{key}/sampled"].tolist())
 
 
@@ -155,8 +160,8 @@ def test_loader_missing_file(tmp_path):
 def test_reference_fixtures(orc, ref, fname, qtype, qname):
     """The reference's own llama2.c fixtures: the host loader reads the same
     bytes as the reference loader, and the oracle reproduces the reference's
-    known answer (greedy ids {4, 5} after the prompt "H", both quantisations,
-    src/loader_selftest.cpp:96-116)."""
+    known answer (greedy ids {4, 5} after the prompt "H", fp32 and both
+    quantisations, src/loader_selftest.cpp:84-116)."""
     path = os.path.join(REF_FIXTURES, fname)
     assert nb.llama2c_inspect(path, qtype) == ref.llama2c_inspect(path, qtype)
     if fname == "tiny-llama2.bin":
@@ -164,8 +169,11 @@ def test_reference_fixtures(orc, ref, fname, qtype, qname):
                                     6, "H")
         want = ref.llama2c_generate(path, qtype, prompt, 32)
         assert want.tolist() == [4, 5]
-        m = orc.model(_oracle_model(orc, path, qtype))
-        assert m.generate_cached(prompt, 32).tolist() == [4, 5]
+        if qtype == nb.FP32:
+            ids = orc.fp32_model(oracle.read_llama2c(path)).generate_cached(prompt, 32)[0]
+        else:
+            ids = orc.model(_oracle_model(orc, path, qtype)).generate_cached(prompt, 32)
+        assert ids.tolist() == [4, 5]
 
 
 # ------------------------------------------------------------------ GPU
@@ -203,6 +211,62 @@ def test_llama2c_generation_errors(gpu, checkpoints):
                             top_p=0.0)
     ids, _ = nb.llama2c_generate(path, 1, np.array([2, 3], np.int32), 0)
     assert ids.size == 0
+    # the fp32 path keeps prefill_tokens' messages
+    with pytest.raises(IndexError, match="kv cache: token id out of range"):
+        nb.llama2c_generate(path, nb.FP32, np.array([2, 300], np.int32), 4)
+    with pytest.raises(ValueError, match="generation: invalid prompt length"):
+        nb.llama2c_generate(path, nb.FP32, np.zeros(0, np.int32), 4)
+
+
+def _fp32_device_model(t):
+    layers = [dict(query=t["wq"][l], key=t["wk"][l], value=t["wv"][l], output=t["wo"][l],
+                   gate=t["w1"][l], up=t["w3"][l], down=t["w2"][l],
+                   attention_norm=t["attention_norm"][l], ffn_norm=t["ffn_norm"][l])
+              for l in range(t["config"]["layers"])]
+    return nb.DeviceModel.fp32(nb.Config(**t["config"]), t["embeddings"], layers,
+                               t["final_norm"], None if t["tied"] else t["classifier"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(fx.CONFIGS))
+def test_fp32_decode_matches_oracle(gpu, orc, checkpoints, name):
+    """decode_token over fp32 weights (src/kvcache.cpp:265-284) on the
+    device: hidden rows and logits of every prompt position and greedy step
+    within 2e-3 absolute + 1e-3 relative of the oracle's restatement (fp32
+    projections summed in a different order than linear_threaded), the same
+    ids, and the cache holding the oracle's keys and values."""
+    t = oracle.read_llama2c(checkpoints[name])
+    want = orc.fp32_model(t)
+    dm = _fp32_device_model(t)
+    cache = nb.KVCache(dm)
+    c = fx.config_of(name)
+    prompt = [int(v) for v in G[f"{name}/prompt"]]
+    tok = prompt[0]
+    for step in range(len(prompt) + c["max_tokens"] // 2):
+        h = nb.decode_quantized_token(dm, tok, cache)
+        hw = want.decode(tok)
+        assert np.allclose(h, hw, atol=2e-3, rtol=1e-3), float(np.abs(h - hw).max())
+        lg, best = nb.logits(dm, cache)
+        lw = want.logits(hw)
+        assert np.allclose(lg, lw, atol=2e-3, rtol=1e-3), float(np.abs(lg - lw).max())
+        if step + 1 < len(prompt):
+            tok = prompt[step + 1]
+        else:
+            assert best == int(np.argmax(lw))
+            tok = best
+    assert cache.length() == want.length
+    kvh = t["config"]["kv_heads"]
+    for l in range(t["config"]["layers"]):
+        for hh in range(kvh):
+            for pos in (0, want.length - 1):
+                assert np.allclose(cache.key(l, hh, pos), want.keys[l, hh, pos], atol=2e-3,
+                                   rtol=1e-3)
+                assert np.allclose(cache.value(l, hh, pos), want.values[l, hh, pos],
+                                   atol=2e-3, rtol=1e-3)
+    with pytest.raises(IndexError, match="kv cache: token id out of range"):
+        nb.decode_quantized_token(dm, t["config"]["vocab_size"], cache)
+    cache.close()
+    dm.close()
 
 
 SELFTEST = os.path.join(os.path.dirname(nb.HOST_LIB), "..", "bin", "nutllm_selftest")
