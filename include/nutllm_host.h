@@ -61,6 +61,29 @@ int nut_host_tokenizer_encode(const char *path, int64_t vocab, const char *text,
 int nut_host_tokenizer_decode(const char *path, int64_t vocab, const int32_t *ids, int64_t n,
                               char *out, int64_t cap, int64_t *len_out);
 
+/* Safetensors fp32 checkpoints (reference include/loader.hpp:11-62,
+ * src/loader.cpp:286-498): load_model(path) described as
+ * nut_host_llama2c_inspect describes a llama2.c file (config, storage_bytes,
+ * FNV-1a digest of embeddings, per layer the [in][out] query, key, value,
+ * output, gate, up, down then both norms, the final norm, lm_head), and
+ * load_model + generation on the current device: cached != 0 calls
+ * generate_tokens_cached (src/generate.cpp:128-172), cached == 0
+ * generate_tokens (:101-126), each with its own checks and messages. */
+int nut_host_safetensors_inspect(const char *path, int64_t *config, uint64_t *storage_bytes,
+                                 uint64_t *digest);
+int nut_host_safetensors_generate(const char *path, const int32_t *prompt, int64_t n,
+                                  int64_t max_tokens, float temperature, float top_p,
+                                  uint32_t seed, int32_t cached, int32_t *ids, int64_t *n_out);
+
+/* Byte-level BPE Tokenizer (reference include/tokenizer.hpp:9-24):
+ * Tokenizer::load(vocab_path, merges_path).encode(text) into ids (room for
+ * `cap`; *n_out = count), or decode(ids) into out (room for `cap` bytes, not
+ * NUL-terminated; *len_out = length). */
+int nut_host_bpe_encode(const char *vocab_path, const char *merges_path, const char *text,
+                        int64_t text_len, int32_t *ids, int64_t cap, int64_t *n_out);
+int nut_host_bpe_decode(const char *vocab_path, const char *merges_path, const int32_t *ids,
+                        int64_t n, char *out, int64_t cap, int64_t *len_out);
+
 /* The generation token choice (choose_token, reference
  * src/generate.cpp:25-73) over `steps` rows of logits [steps][vocab] with
  * one std::mt19937(seed) shared by the steps, as one generation uses it. */

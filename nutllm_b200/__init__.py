@@ -234,6 +234,15 @@ def host_lib() -> C.CDLL:
                  [C.c_char_p, _I64, C.c_char_p, _I64, C.c_int32, C.c_int32, _P, _I64, _PI64])
         _declare(lib, "nut_host_tokenizer_decode",
                  [C.c_char_p, _I64, _P, _I64, C.c_char_p, _I64, _PI64])
+        _declare(lib, "nut_host_safetensors_inspect",
+                 [C.c_char_p, _PI64, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)])
+        _declare(lib, "nut_host_safetensors_generate",
+                 [C.c_char_p, _P, _I64, _I64, C.c_float, C.c_float, C.c_uint32, C.c_int32,
+                  _P, _PI64])
+        _declare(lib, "nut_host_bpe_encode",
+                 [C.c_char_p, C.c_char_p, C.c_char_p, _I64, _P, _I64, _PI64])
+        _declare(lib, "nut_host_bpe_decode",
+                 [C.c_char_p, C.c_char_p, _P, _I64, C.c_char_p, _I64, _PI64])
         _host = lib
     return _host
 
@@ -350,6 +359,55 @@ def llama2c_inspect(path: str, qtype: int) -> tuple[list, bool, int, int]:
     _check(lib.nut_host_llama2c_inspect(os.fsencode(path), qtype, cfg, C.byref(tied),
                                         C.byref(nbytes), C.byref(digest)), lib)
     return list(cfg), bool(tied.value), nbytes.value, digest.value
+
+
+def safetensors_inspect(path: str) -> tuple[list, int, int]:
+    """(config[9], storage_bytes, FNV-1a digest) of load_model(path) (the
+    fp32 safetensors loader, reference src/loader.cpp:440-498)."""
+    lib = host_lib()
+    cfg = (C.c_int64 * 9)()
+    nbytes = C.c_uint64(0)
+    digest = C.c_uint64(0)
+    _check(lib.nut_host_safetensors_inspect(os.fsencode(path), cfg, C.byref(nbytes),
+                                            C.byref(digest)), lib)
+    return list(cfg), nbytes.value, digest.value
+
+
+def safetensors_generate(path: str, prompt, max_tokens: int, temperature: float = 0.0,
+                         top_p: float = 1.0, seed: int = 1, cached: bool = True) -> np.ndarray:
+    """load_model + generate_tokens_cached (cached) or generate_tokens on the
+    current device through the C++ host API."""
+    lib = host_lib()
+    p = np.ascontiguousarray(prompt, np.int32)
+    ids = np.zeros(max(max_tokens, 1), np.int32)
+    n = C.c_int64(0)
+    _check(lib.nut_host_safetensors_generate(os.fsencode(path), _ptr(p) if p.size else None,
+                                             p.size, max_tokens, temperature, top_p, seed,
+                                             int(cached), _ptr(ids), C.byref(n)), lib)
+    return ids[:n.value]
+
+
+def bpe_encode(vocab_path: str, merges_path: str, text: bytes) -> list:
+    """Tokenizer::load(vocab_path, merges_path).encode(text) (byte-level BPE)."""
+    lib = host_lib()
+    ids = np.zeros(len(text) + 1, np.int32)
+    n = C.c_int64(0)
+    _check(lib.nut_host_bpe_encode(os.fsencode(vocab_path), os.fsencode(merges_path), text,
+                                   len(text), _ptr(ids), ids.size, C.byref(n)), lib)
+    return ids[:n.value].tolist()
+
+
+def bpe_decode(vocab_path: str, merges_path: str, ids) -> bytes:
+    """Tokenizer::load(vocab_path, merges_path).decode(ids)."""
+    lib = host_lib()
+    a = np.ascontiguousarray(ids, np.int32)
+    cap = 1 << 16
+    buf = C.create_string_buffer(cap)
+    n = C.c_int64(0)
+    _check(lib.nut_host_bpe_decode(os.fsencode(vocab_path), os.fsencode(merges_path),
+                                   _ptr(a) if a.size else None, a.size, buf, cap,
+                                   C.byref(n)), lib)
+    return buf.raw[:n.value]
 
 
 def tokenizer_encode(path: str, vocab: int, text: str, bos: bool = True,

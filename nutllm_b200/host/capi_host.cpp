@@ -11,6 +11,7 @@
 #include "llama2.hpp"
 #include "quant.hpp"
 #include "quant_model.hpp"
+#include "tokenizer.hpp"
 
 namespace {
 
@@ -73,6 +74,23 @@ struct Fnv1a {
     }
     template <typename T> void add(const std::vector<T> &v) { add(v.data(), v.size() * sizeof(T)); }
 };
+
+/* embeddings; per layer the seven [in][out] matrices then both norms; the
+ * final norm; the classifier when it is separate */
+uint64_t fp32_digest(const ModelWeights &m) {
+    Fnv1a f;
+    f.add(m.embeddings.data(), m.embeddings.size() * sizeof(float));
+    for (const LayerWeights &l : m.layers) {
+        for (const Matrix *q : {&l.query, &l.key, &l.value, &l.output, &l.gate, &l.up, &l.down})
+            f.add(q->data(), q->size() * sizeof(float));
+        f.add(l.attention_norm);
+        f.add(l.ffn_norm);
+    }
+    f.add(m.final_norm);
+    if (!m.tied_embeddings)
+        f.add(m.lm_head.data(), m.lm_head.size() * sizeof(float));
+    return f.h;
+}
 
 } // namespace
 
@@ -141,21 +159,8 @@ int nut_host_llama2c_inspect(const char *path, int32_t type, int64_t *config,
             const ModelWeights m = load_llama2c_model(path);
             describe(m.config, m.tied_embeddings, m.storage_bytes(), config, tied,
                      storage_bytes);
-            if (digest != nullptr) {
-                Fnv1a f;
-                f.add(m.embeddings.data(), m.embeddings.size() * sizeof(float));
-                for (const LayerWeights &l : m.layers) {
-                    for (const Matrix *q :
-                         {&l.query, &l.key, &l.value, &l.output, &l.gate, &l.up, &l.down})
-                        f.add(q->data(), q->size() * sizeof(float));
-                    f.add(l.attention_norm);
-                    f.add(l.ffn_norm);
-                }
-                f.add(m.final_norm);
-                if (!m.tied_embeddings)
-                    f.add(m.lm_head.data(), m.lm_head.size() * sizeof(float));
-                *digest = f.h;
-            }
+            if (digest != nullptr)
+                *digest = fp32_digest(m);
             return;
         }
         const QuantizedModelWeights m = load_llama2c_quantized_model(path, quant_type(type));
@@ -225,6 +230,69 @@ int nut_host_tokenizer_decode(const char *path, int64_t vocab, const int32_t *id
         const std::string text = t.decode(std::vector<int>(ids, ids + n));
         if (int64_t(text.size()) > cap || (cap > 0 && out == nullptr))
             throw std::length_error("llama2 tokenizer: output buffer too small");
+        std::memcpy(out, text.data(), text.size());
+        *len_out = int64_t(text.size());
+    });
+}
+
+int nut_host_safetensors_inspect(const char *path, int64_t *config, uint64_t *storage_bytes,
+                                 uint64_t *digest) {
+    return guarded([&] {
+        if (path == nullptr)
+            throw std::invalid_argument("safetensors: null path");
+        const ModelWeights m = load_model(path);
+        describe(m.config, false, m.storage_bytes(), config, nullptr, storage_bytes);
+        if (digest != nullptr)
+            *digest = fp32_digest(m);
+    });
+}
+
+int nut_host_safetensors_generate(const char *path, const int32_t *prompt, int64_t n,
+                                  int64_t max_tokens, float temperature, float top_p,
+                                  uint32_t seed, int32_t cached, int32_t *ids, int64_t *n_out) {
+    return guarded([&] {
+        if (path == nullptr || (prompt == nullptr && n > 0) || n_out == nullptr ||
+            max_tokens < 0 || (max_tokens > 0 && ids == nullptr) || n < 0)
+            throw std::invalid_argument("generation: invalid argument");
+        const ModelWeights model = load_model(path);
+        SamplingConfig sampling;
+        sampling.max_tokens = size_t(max_tokens);
+        sampling.temperature = temperature;
+        sampling.top_p = top_p;
+        sampling.seed = seed;
+        const std::vector<int> tokens(prompt, prompt + n);
+        const std::vector<int> out = cached ? generate_tokens_cached(model, tokens, sampling)
+                                            : generate_tokens(model, tokens, sampling);
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = int64_t(out.size());
+    });
+}
+
+int nut_host_bpe_encode(const char *vocab_path, const char *merges_path, const char *text,
+                        int64_t text_len, int32_t *ids, int64_t cap, int64_t *n_out) {
+    return guarded([&] {
+        if (vocab_path == nullptr || merges_path == nullptr || n_out == nullptr ||
+            (text == nullptr && text_len > 0) || text_len < 0)
+            throw std::invalid_argument("tokenizer: invalid argument");
+        const Tokenizer t = Tokenizer::load(vocab_path, merges_path);
+        const std::vector<int> out = t.encode(std::string(text, size_t(text_len)));
+        if (int64_t(out.size()) > cap || (cap > 0 && ids == nullptr))
+            throw std::length_error("tokenizer: output buffer too small");
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = int64_t(out.size());
+    });
+}
+
+int nut_host_bpe_decode(const char *vocab_path, const char *merges_path, const int32_t *ids,
+                        int64_t n, char *out, int64_t cap, int64_t *len_out) {
+    return guarded([&] {
+        if (vocab_path == nullptr || merges_path == nullptr || len_out == nullptr ||
+            (ids == nullptr && n > 0) || n < 0)
+            throw std::invalid_argument("tokenizer: invalid argument");
+        const Tokenizer t = Tokenizer::load(vocab_path, merges_path);
+        const std::string text = t.decode(std::vector<int>(ids, ids + n));
+        if (int64_t(text.size()) > cap || (cap > 0 && out == nullptr))
+            throw std::length_error("tokenizer: output buffer too small");
         std::memcpy(out, text.data(), text.size());
         *len_out = int64_t(text.size());
     });

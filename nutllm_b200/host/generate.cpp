@@ -166,3 +166,15 @@ std::vector<int> generate_tokens_cached(const ModelWeights &model,
     return generate_sampled(model.device(), model.config, prompt, sampling, cache, stats,
                             [&] { prefill_tokens(model, prompt, cache, sampling.threads); });
 }
+
+std::vector<int> generate_tokens(const ModelWeights &model, const std::vector<int> &prompt,
+                                 const SamplingConfig &sampling) {
+    model.config.validate();
+    if (prompt.empty())
+        throw std::invalid_argument("generation: prompt cannot be empty");
+    if (sampling.threads == 0)
+        throw std::invalid_argument("generation: zero threads");
+    if (prompt.size() > model.config.max_seq)
+        throw std::length_error("generation: prompt exceeds context");
+    return generate_tokens_cached(model, prompt, sampling, nullptr);
+}

@@ -43,6 +43,14 @@ std::vector<int> generate_tokens_cached(const ModelWeights &model,
                                         const SamplingConfig &sampling,
                                         GenerationStats *stats = nullptr);
 
+/* generate_tokens (src/generate.cpp:101-126): the reference recomputes the
+ * whole prefix every step; here the same loop runs through the device KV
+ * cache (the same ids up to rounding order — the reference's own selftest
+ * holds the two equal, src/kvcache_selftest.cpp:97-115).  Checks and
+ * messages are generate_tokens' own. */
+std::vector<int> generate_tokens(const ModelWeights &model, const std::vector<int> &prompt,
+                                 const SamplingConfig &sampling);
+
 /* The token choice of one step (src/generate.cpp:25-73): first-index argmax
  * for temperature <= 0; otherwise a draw from the smallest set of most
  * probable tokens whose probability reaches top_p.  Exposed for tests. */

@@ -11,7 +11,9 @@
  * (nut_model_create_f32).  thread_count must be non-zero, as in the
  * reference; the device ignores it. */
 #include <cstddef>
+#include <map>
 #include <memory>
+#include <string>
 #include <vector>
 
 #include "kvcache.hpp"
@@ -61,3 +63,57 @@ Matrix prefill_tokens(const ModelWeights &model, const std::vector<int> &tokens,
                       KVCache &cache, size_t thread_count = 1);
 std::vector<float> decode_token(const ModelWeights &model, int token, KVCache &cache,
                                 size_t thread_count = 1);
+
+/* Safetensors checkpoints (include/loader.hpp:11-45, src/loader.cpp:24-498).
+ *
+ * SafeTensorFile maps the file read-only and parses its header: a
+ * little-endian uint64 length, then that many bytes of JSON — an object
+ * whose "__metadata__" member maps names to strings and whose other
+ * members describe one F32 tensor each ({"dtype": "F32", "shape": [..],
+ * "data_offsets": [begin, end]}, byte offsets after the header).  The JSON
+ * accepted is the reference's subset: objects (duplicate keys rejected),
+ * arrays, strings with the escapes \" \\ \/ \b \f \n \r \t, and
+ * unsigned decimal integers.  Tensor views point into the mapping, which
+ * lives as long as the SafeTensorFile (or a copy of its storage).
+ *
+ * load_model reads a Llama-style fp32 checkpoint: config from the metadata
+ * strings nutllm.{layers, heads, dim, head_dim, ffn_dim, vocab_size,
+ * max_seq, eos_token} (decimal), tensors model.embed_tokens.weight,
+ * model.layers.N.self_attn.{q,k,v,o}_proj.weight,
+ * model.layers.N.mlp.{gate,up,down}_proj.weight ([out][in], transposed into
+ * the [in][out] matrices), model.layers.N.{input,post_attention}_layernorm
+ * .weight, model.norm.weight and lm_head.weight.  Errors keep the
+ * reference's classes and messages. */
+struct TensorView {
+    const float *data = nullptr;
+    std::vector<size_t> shape;
+    size_t elements = 0;
+};
+
+class SafeTensorFile {
+public:
+    static SafeTensorFile load(const std::string &path);
+
+    SafeTensorFile();
+    ~SafeTensorFile();
+    SafeTensorFile(SafeTensorFile &&) noexcept;
+    SafeTensorFile &operator=(SafeTensorFile &&) noexcept;
+    SafeTensorFile(const SafeTensorFile &) = delete;
+    SafeTensorFile &operator=(const SafeTensorFile &) = delete;
+
+    TensorView tensor(const std::string &name) const;
+    const std::string &metadata(const std::string &name) const;
+
+private:
+    struct Mapping;
+    struct Entry {
+        std::vector<size_t> shape;
+        size_t begin = 0, end = 0;
+    };
+    std::shared_ptr<Mapping> mapping_;
+    std::map<std::string, Entry> tensors_;
+    std::map<std::string, std::string> metadata_;
+    size_t payload_ = 0; /* first payload byte */
+};
+
+ModelWeights load_model(const std::string &path);

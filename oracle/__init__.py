@@ -357,6 +357,16 @@ class Fp32Model:
 # ------------------------------------------------------------- reference
 
 
+class RefError(RuntimeError):
+    """A reference call that threw: status 1 invalid_argument, 2
+    out_of_range, 3 length_error, 4 other runtime errors, 5 range_error."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"reference status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
 def reference_available() -> bool:
     return os.path.exists(REF_LIB)
 
@@ -402,12 +412,19 @@ class Reference:
                                             _P, S, C.POINTER(S)]
         lib.ref_llama2c_decode.argtypes = [C.c_char_p, S, _P, S, C.c_char_p, S,
                                            C.POINTER(S)]
+        lib.ref_safetensors_inspect.argtypes = [C.c_char_p, C.POINTER(_I64),
+                                                C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+        lib.ref_safetensors_generate.argtypes = [C.c_char_p, _P, S, S, C.c_float, C.c_float,
+                                                 C.c_uint, C.c_int, _P, C.POINTER(S)]
+        lib.ref_bpe_encode.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, S, _P, S,
+                                       C.POINTER(S)]
+        lib.ref_bpe_decode.argtypes = [C.c_char_p, C.c_char_p, _P, S, C.c_char_p, S,
+                                       C.POINTER(S)]
         self.lib = lib
 
     def _check(self, status):
         if status != 0:
-            raise RuntimeError(f"reference status {status}: "
-                               f"{self.lib.ref_last_error().decode()}")
+            raise RefError(status, self.lib.ref_last_error().decode())
 
     def quantize(self, w: np.ndarray, qtype: int):
         w = np.ascontiguousarray(w, np.float32)
@@ -534,6 +551,42 @@ class Reference:
                                                 cap, C.byref(n)))
         return buf.raw[:n.value]
 
+    def safetensors_inspect(self, path: str):
+        """(config[9], storage_bytes, fnv1a digest) of load_model(path)."""
+        cfg = (_I64 * 9)()
+        nbytes = C.c_uint64(0)
+        digest = C.c_uint64(0)
+        self._check(self.lib.ref_safetensors_inspect(path.encode(), cfg, C.byref(nbytes),
+                                                     C.byref(digest)))
+        return list(cfg), nbytes.value, digest.value
+
+    def safetensors_generate(self, path: str, prompt, max_tokens: int, temperature=0.0,
+                             top_p=1.0, seed=1, cached=True):
+        """load_model + generate_tokens_cached (or generate_tokens)."""
+        p = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(max(max_tokens, 1), np.int32)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_safetensors_generate(path.encode(), _ptr(p), p.size,
+                                                      max_tokens, temperature, top_p, seed,
+                                                      int(cached), _ptr(ids), C.byref(n)))
+        return ids[:n.value]
+
+    def bpe_encode(self, vocab_path: str, merges_path: str, text: bytes):
+        ids = np.zeros(len(text) + 1, np.int32)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_bpe_encode(vocab_path.encode(), merges_path.encode(), text,
+                                            len(text), _ptr(ids), ids.size, C.byref(n)))
+        return ids[:n.value]
+
+    def bpe_decode(self, vocab_path: str, merges_path: str, ids) -> bytes:
+        a = np.ascontiguousarray(ids, np.int32)
+        cap = 1 << 16
+        buf = C.create_string_buffer(cap)
+        n = C.c_size_t(0)
+        self._check(self.lib.ref_bpe_decode(vocab_path.encode(), merges_path.encode(),
+                                            _ptr(a), len(a), buf, cap, C.byref(n)))
+        return buf.raw[:n.value]
+
     def llama2c_encode(self, tokenizer_path: str, vocab: int, text: str, bos: bool = True):
         ids = np.zeros(4 * len(text.encode()) + 8, np.int32)
         n = C.c_size_t(0)
@@ -606,6 +659,40 @@ class RefModel:
 
 
 # ------------------------------------------------------------- llama2.c
+
+
+def read_safetensors_model(path: str) -> dict:
+    """The tensors of an fp32 safetensors checkpoint in read_llama2c's form
+    (load_model's names and metadata, src/loader.cpp:440-498): projections
+    [out][in] as stored, kv_heads 0, a separate classifier.  A checker for
+    well-formed files only (no validation beyond the shapes it reshapes)."""
+    import json
+    raw = np.fromfile(path, dtype=np.uint8)
+    n = int(raw[:8].view(np.uint64)[0])
+    header = json.loads(bytes(raw[8:8 + n]).decode())
+    md = header.pop("__metadata__")
+    base = 8 + n
+
+    def t(name):
+        e = header[name]
+        b, end = e["data_offsets"]
+        return raw[base + b:base + end].view(np.float32).reshape(e["shape"])
+
+    cfg = {k: int(md[f"nutllm.{k}"]) for k in ("layers", "heads", "dim", "head_dim",
+                                                "ffn_dim", "vocab_size", "max_seq",
+                                                "eos_token")}
+    cfg["kv_heads"] = 0
+    L = cfg["layers"]
+    stack = lambda suffix: np.stack([t(f"model.layers.{l}.{suffix}")  # noqa: E731
+                                     for l in range(L)])
+    return {"config": cfg, "tied": False, "embeddings": t("model.embed_tokens.weight"),
+            "wq": stack("self_attn.q_proj.weight"), "wk": stack("self_attn.k_proj.weight"),
+            "wv": stack("self_attn.v_proj.weight"), "wo": stack("self_attn.o_proj.weight"),
+            "w1": stack("mlp.gate_proj.weight"), "w3": stack("mlp.up_proj.weight"),
+            "w2": stack("mlp.down_proj.weight"),
+            "attention_norm": stack("input_layernorm.weight"),
+            "ffn_norm": stack("post_attention_layernorm.weight"),
+            "final_norm": t("model.norm.weight"), "classifier": t("lm_head.weight")}
 
 
 def read_llama2c(path: str) -> dict:

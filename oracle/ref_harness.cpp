@@ -44,6 +44,8 @@
 #include "generate.hpp"
 #include "kvcache.hpp"
 #include "llama2.hpp"
+#include "loader.hpp"
+#include "tokenizer.hpp"
 #include "matmul.hpp"
 #include "ops.hpp"
 #include "quant_model.hpp"
@@ -453,6 +455,86 @@ int ref_llama2c_inspect(const char *path, int type, int64_t *config,
         if (!m.tied_embeddings)
             add(m.lm_head.data(), m.lm_head.size() * 4);
         *digest = h;
+    });
+}
+
+/* load_model(path) described like ref_llama2c_inspect (type 2 digest
+ * order: embeddings, per layer the [in][out] q k v o gate up down and both
+ * norms, final norm, lm_head). */
+int ref_safetensors_inspect(const char *path, int64_t *config, uint64_t *storage_bytes,
+                            uint64_t *digest) {
+    return guarded([&] {
+        const ModelWeights m = load_model(path);
+        const ModelConfig &c = m.config;
+        const size_t v[9] = {c.layers,     c.heads,   c.dim,       c.head_dim, c.ffn_dim,
+                             c.vocab_size, c.max_seq, c.eos_token, c.kv_heads};
+        for (int i = 0; i < 9; i++)
+            config[i] = int64_t(v[i]);
+        *storage_bytes = m.storage_bytes();
+        uint64_t h = 0xcbf29ce484222325ull;
+        auto add = [&h](const void *p, size_t bytes) {
+            const unsigned char *b = static_cast<const unsigned char *>(p);
+            for (size_t i = 0; i < bytes; i++) {
+                h ^= b[i];
+                h *= 0x100000001b3ull;
+            }
+        };
+        add(m.embeddings.data(), m.embeddings.size() * 4);
+        for (const LayerWeights &l : m.layers) {
+            for (const Matrix *q : {&l.query, &l.key, &l.value, &l.output, &l.gate, &l.up,
+                                    &l.down})
+                add(q->data(), q->size() * 4);
+            add(l.attention_norm.data(), l.attention_norm.size() * 4);
+            add(l.ffn_norm.data(), l.ffn_norm.size() * 4);
+        }
+        add(m.final_norm.data(), m.final_norm.size() * 4);
+        if (!m.tied_embeddings)
+            add(m.lm_head.data(), m.lm_head.size() * 4);
+        *digest = h;
+    });
+}
+
+/* load_model + generate_tokens_cached (cached != 0) or generate_tokens. */
+int ref_safetensors_generate(const char *path, const int *prompt, size_t n,
+                             size_t max_tokens, float temperature, float top_p,
+                             unsigned seed, int cached, int *ids, size_t *n_out) {
+    return guarded([&] {
+        const ModelWeights model = load_model(path);
+        SamplingConfig sampling;
+        sampling.max_tokens = max_tokens;
+        sampling.temperature = temperature;
+        sampling.top_p = top_p;
+        sampling.seed = seed;
+        const std::vector<int> tokens(prompt, prompt + n);
+        const std::vector<int> out = cached ? generate_tokens_cached(model, tokens, sampling)
+                                            : generate_tokens(model, tokens, sampling);
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = out.size();
+    });
+}
+
+/* Tokenizer::load(vocab, merges).encode(text) / .decode(ids). */
+int ref_bpe_encode(const char *vocab_path, const char *merges_path, const char *text,
+                   size_t text_len, int *ids, size_t capacity, size_t *n_out) {
+    return guarded([&] {
+        const Tokenizer t = Tokenizer::load(vocab_path, merges_path);
+        const std::vector<int> out = t.encode(std::string(text, text_len));
+        if (out.size() > capacity)
+            throw std::length_error("harness: capacity");
+        std::copy(out.begin(), out.end(), ids);
+        *n_out = out.size();
+    });
+}
+
+int ref_bpe_decode(const char *vocab_path, const char *merges_path, const int *ids, size_t n,
+                   char *out, size_t capacity, size_t *len_out) {
+    return guarded([&] {
+        const Tokenizer t = Tokenizer::load(vocab_path, merges_path);
+        const std::string text = t.decode(std::vector<int>(ids, ids + n));
+        if (text.size() > capacity)
+            throw std::length_error("harness: capacity");
+        std::memcpy(out, text.data(), text.size());
+        *len_out = text.size();
     });
 }
 
