@@ -79,6 +79,8 @@ class Oracle:
         lib.orc_set_threads.restype = None
         lib.orc_rmsnorm.argtypes = [_P, _P, _P, _I64, C.c_float]
         lib.orc_rmsnorm.restype = None
+        lib.orc_uniform_floats.argtypes = [C.c_uint32, C.c_float, C.c_float, _I64, _P]
+        lib.orc_uniform_floats.restype = None
         lib.orc_rope.argtypes = [_P, _I64, _I64]
         lib.orc_rope.restype = None
         lib.orc_matvec_f32.argtypes = [_P, _I64, _I64, _P, _P]
@@ -163,6 +165,13 @@ class Oracle:
         out = np.zeros(lg.shape[0], np.int64)
         self._check(self.lib.orc_choose_tokens(_ptr(lg), lg.shape[0], lg.shape[1],
                                                temperature, top_p, seed, _ptr(out)))
+        return out
+
+    def uniform_floats(self, seed: int, lo: float, hi: float, shape) -> np.ndarray:
+        """std::uniform_real_distribution<float>(lo, hi) over
+        std::mt19937(seed), row-major into `shape`."""
+        out = np.empty(shape, np.float32)
+        self.lib.orc_uniform_floats(seed, lo, hi, out.size, _ptr(out))
         return out
 
     def rope(self, values: np.ndarray, position: int) -> np.ndarray:

@@ -577,6 +577,22 @@ static double uniform_double(orc_mt19937 *g, double lo, double hi) {
     return canonical * (hi - lo) + lo;
 }
 
+/* std::uniform_real_distribution<float>(lo, hi) over std::mt19937(seed) as
+ * libstdc++ computes it: generate_canonical<float, 24> takes one 32-bit
+ * draw x, u = float(x) / 2^32 (u = 1 is replaced by the float below 1),
+ * then u * (hi - lo) + lo in float.  The reference's self-tests fill their
+ * matrices this way (src/quant_selftest.cpp:16-21). */
+void orc_uniform_floats(uint32_t seed, float lo, float hi, int64_t n, float *out) {
+    orc_mt19937 g;
+    mt_seed(&g, seed);
+    for (int64_t i = 0; i < n; i++) {
+        float u = (float)mt_draw(&g) / 4294967296.0f;
+        if (u >= 1.0f)
+            u = nextafterf(1.0f, 0.0f);
+        out[i] = u * (hi - lo) + lo;
+    }
+}
+
 /* Probability order: larger weight first, lower token id on ties. */
 static const float *g_sort_weights;
 static int by_weight(const void *a, const void *b) {

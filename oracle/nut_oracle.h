@@ -91,6 +91,10 @@ int orc_generate(const orc_model *model, orc_kv *kv, const int *prompt,
  * loop (src/generate.cpp:174-216): prefill, then while fewer than
  * max_tokens ids and the cache is not full: logits, choose, stop at eos,
  * decode.  Greedy when temperature <= 0. */
+/* n values of std::uniform_real_distribution<float>(lo, hi) drawn from
+ * std::mt19937(seed) (libstdc++'s generate_canonical). */
+void orc_uniform_floats(uint32_t seed, float lo, float hi, int64_t n, float *out);
+
 int orc_choose_tokens(const float *logits, int64_t steps, int64_t vocab,
                       float temperature, float top_p, uint32_t seed,
                       int64_t *tokens);

@@ -129,3 +129,73 @@ def test_synthetic_generator_is_deterministic():
     assert np.array_equal(nb.synth_normal(99, 5, 10, 0.02), a[:10])
     t = nb.synth_tokens(3, 3, 1000, 1, 511)
     assert t.min() >= 1 and t.max() <= 511
+
+
+def _dequantize(orc, w, qtype):
+    """dequantize() and error_bound() (src/quant.cpp:199-233) of the host
+    quantiser's output for w."""
+    d, s = nb.quantize(w, qtype)
+    n = w.size
+    scale = np.array([orc.half_to_float(int(h)) for h in s], np.float32)
+    if qtype == nb.INT8:
+        q = d.view(np.int8).astype(np.float32)
+    else:
+        nib = np.stack([d & 0xF, d >> 4], axis=1).reshape(-1).astype(np.int8)
+        q = np.where(nib > 7, nib - 16, nib).astype(np.float32)[:n]
+    blk = np.arange(n) // 32
+    values = (q * scale[blk]).astype(np.float32).reshape(w.shape)
+    half_rounding = np.maximum(scale / np.float32(2047.0), np.float32(2.0 ** -25))
+    limit = np.float32(127.0 if qtype == nb.INT8 else 7.0)
+    bound = (scale * np.float32(0.5) + (limit + np.float32(0.5)) * half_rounding)[blk]
+    return values, bound.reshape(w.shape)
+
+
+def _matmul_f32(a, b):
+    """matmul_naive / matmul_quantized order: each output an in-order float
+    sum over the inner index."""
+    out = np.zeros((a.shape[0], b.shape[1]), np.float32)
+    for k in range(a.shape[1]):
+        out = (out + a[:, k:k + 1] * b[k:k + 1, :]).astype(np.float32)
+    return out
+
+
+def _perplexity(logits, targets):
+    """perplexity() (src/perplexity.cpp): max-shifted double log-sum-exp."""
+    nll = 0.0
+    for r in range(logits.shape[0]):
+        m = logits[r].max()
+        nll += np.log(np.exp((logits[r] - m).astype(np.float64)).sum()) + \
+            float(m - logits[r, targets[r]])
+    return float(np.exp(nll / logits.shape[0]))
+
+
+def test_quant_selftest_known_answers(orc):
+    """The reference's quantisation self-test on its own seeded inputs
+    (src/quant_selftest.cpp:71-184; values printed by the reference and
+    recorded in docs/08-quantisation.md:89-99): the host quantiser's
+    round-trip worst error/bound ratios 0.879 (INT8) and 0.993 (INT4), the
+    quantised-matmul ratios 0.726 and 0.756, and the synthetic perplexities
+    11.598 (fp32), 11.608 (INT8), 11.715 (INT4).  Inputs come from the
+    oracle's restatement of std::uniform_real_distribution<float> over
+    std::mt19937 (seeds 505, 606, 707)."""
+    w = orc.uniform_floats(505, -1.0, 1.0, (5, 37))
+    left = orc.uniform_floats(606, -1.0, 1.0, (3, 5))
+    acts = orc.uniform_floats(707, -1.0, 1.0, (12, 5))
+    want_rt = {nb.INT8: 0.879, nb.INT4: 0.993}
+    want_mm = {nb.INT8: 0.726, nb.INT4: 0.756}
+    ref = _matmul_f32(left, w)
+    for qtype in (nb.INT8, nb.INT4):
+        values, bound = _dequantize(orc, w, qtype)
+        err = np.abs(w - values)
+        assert np.all(err <= bound + 1e-7)
+        assert round(float((err / bound).max()), 3) == want_rt[qtype]
+        mm_bound = np.abs(left.astype(np.float64)) @ bound.astype(np.float64)
+        mm_err = np.abs(ref.astype(np.float64) - _matmul_f32(left, values))
+        assert np.all(mm_err <= mm_bound + 1e-5)
+        assert round(float((mm_err / mm_bound).max()), 3) == want_mm[qtype]
+    fp32 = _matmul_f32(acts, w)
+    targets = np.argmax(fp32, axis=1)
+    got = [_perplexity(fp32, targets)] + [
+        _perplexity(_matmul_f32(acts, _dequantize(orc, w, q)[0]), targets)
+        for q in (nb.INT8, nb.INT4)]
+    assert [round(v, 3) for v in got] == [11.598, 11.608, 11.715]
