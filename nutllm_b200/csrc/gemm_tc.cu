@@ -24,6 +24,7 @@
  */
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -155,8 +156,8 @@ struct GemmSmem {
     static constexpr size_t kBytes = size_t(STAGES) * kStage + 1024 /* align */ + 256;
 };
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreadsG, 1)
+template <int BN, int STAGES, int CTAS_PER_SM = 1>
+__global__ void __launch_bounds__(kThreadsG, CTAS_PER_SM)
 gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const GemmArgs g) {
     using S = GemmSmem<BN, STAGES>;
@@ -626,11 +627,12 @@ gemm_q4_kernel(const __grid_constant__ CUtensorMap tmA, const uint8_t *wq, const
     }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CTAS_PER_SM = 1>
 cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs &g,
                       cudaStream_t stream) {
     using S = GemmSmem<BN, STAGES>;
-    auto k = gemm_f16_kernel<BN, STAGES>;
+    static_assert(CTAS_PER_SM * (S::kBytes + 1024) <= 228 * 1024, "shared memory per SM");
+    auto k = gemm_f16_kernel<BN, STAGES, CTAS_PER_SM>;
     cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
     if (e != cudaSuccess)
@@ -654,6 +656,17 @@ cudaError_t launch_q4(const CUtensorMap &a, const uint8_t *wq, const GemmArgs &g
     k<<<grid, kThreadsG, S::kBytes, stream>>>(a, wq, g);
     count_launches(1);
     return cudaGetLastError();
+}
+
+/* CTAs per SM for the 64- and 128-column tiles: 2 (measured on B200,
+ * Llama-2-7B-shape batch-64 decode step: 58.7k -> 68.7k tok/s; 3 and 4
+ * were no better), or 1 with NUTLLM_GEMM_CTAS_PER_SM=1 (read once). */
+int ctas_per_sm() {
+    static const int n = [] {
+        const char *v = std::getenv("NUTLLM_GEMM_CTAS_PER_SM");
+        return v != nullptr && std::atoi(v) == 1 ? 1 : 2;
+    }();
+    return n;
 }
 
 } // namespace
@@ -694,16 +707,21 @@ cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_a
     int bn = 256;
     while (bn > 64 && mt * ((N + bn - 1) / bn) < sms)
         bn /= 2;
+    /* Tiles of 64 or 128 columns run several CTAs per SM with fewer stages
+     * each (about the same bytes in flight per SM): while one CTA fills its
+     * ring or drains its accumulator, the others stream. */
+    const int per_sm = bn <= 128 ? ctas_per_sm() : 1;
+    const int slots = sms * per_sm;
     /* split K (at least 4 K blocks per split) so that the CTAs fill their
-     * waves best: one CTA per SM, so a grid of t CTAs runs ceil(t / sms)
-     * waves; the fewest splits within 2 % of the best fill win (each split
-     * adds its partial product atomically) */
+     * waves best: a grid of t CTAs runs ceil(t / slots) waves; the fewest
+     * splits within 2 % of the best fill win (each split adds its partial
+     * product atomically) */
     int splits = 1;
     const int tiles = mt * ((N + bn - 1) / bn), kbs = K / kBK;
     double best = 0.0;
     for (int sp = 1; sp <= max_splits && kbs / sp >= 4; sp++) {
-        const int t = tiles * sp, waves = (t + sms - 1) / sms;
-        const double fill = double(t) / double(waves * sms);
+        const int t = tiles * sp, waves = (t + slots - 1) / slots;
+        const double fill = double(t) / double(waves * slots);
         if (fill > best + 0.02) {
             best = fill;
             splits = sp;
@@ -716,8 +734,10 @@ cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_a
     if (bn == 256)
         return launch_bn<256, 4>(ma, mb, g, stream);
     if (bn == 128)
-        return launch_bn<128, 6>(ma, mb, g, stream);
-    return launch_bn<64, 8>(ma, mb, g, stream);
+        return per_sm == 2 ? launch_bn<128, 3, 2>(ma, mb, g, stream)
+                           : launch_bn<128, 6>(ma, mb, g, stream);
+    return per_sm == 2 ? launch_bn<64, 4, 2>(ma, mb, g, stream)
+                       : launch_bn<64, 8>(ma, mb, g, stream);
 }
 
 size_t q4_packed_bytes(int N, int K) {
