@@ -440,8 +440,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
-template <int STAGES>
-__global__ void __launch_bounds__(kThreadsG, 1)
+template <int STAGES, int CTAS_PER_SM = 1>
+__global__ void __launch_bounds__(kThreadsG, CTAS_PER_SM)
 gemm_q4_kernel(const __grid_constant__ CUtensorMap tmA, const uint8_t *wq, const GemmArgs g) {
     using S = Q4Smem<STAGES>;
     constexpr int BN = kQ4N;
@@ -643,11 +643,12 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs
     return cudaGetLastError();
 }
 
-template <int STAGES>
+template <int STAGES, int CTAS_PER_SM = 1>
 cudaError_t launch_q4(const CUtensorMap &a, const uint8_t *wq, const GemmArgs &g,
                       cudaStream_t stream) {
     using S = Q4Smem<STAGES>;
-    auto k = gemm_q4_kernel<STAGES>;
+    static_assert(CTAS_PER_SM * (S::kBytes + 1024) <= 228 * 1024, "shared memory per SM");
+    auto k = gemm_q4_kernel<STAGES, CTAS_PER_SM>;
     cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
     if (e != cudaSuccess)
@@ -796,12 +797,13 @@ cudaError_t gemm_q4(const uint16_t *A, int M, const uint8_t *Wq, int N, int K, f
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int mt = (M + kBM - 1) / kBM;
+    const int per_sm = ctas_per_sm(), slots = sms * per_sm;
     int splits = 1;
     const int tiles = mt * ((N + kQ4N - 1) / kQ4N), kbs = K / kBK;
     double best = 0.0;
     for (int sp = 1; sp <= max_splits && kbs / sp >= 4; sp++) {
-        const int t = tiles * sp, waves = (t + sms - 1) / sms;
-        const double fill = double(t) / double(waves * sms);
+        const int t = tiles * sp, waves = (t + slots - 1) / slots;
+        const double fill = double(t) / double(waves * slots);
         if (fill > best + 0.02) {
             best = fill;
             splits = sp;
@@ -811,7 +813,7 @@ cudaError_t gemm_q4(const uint16_t *A, int M, const uint8_t *Wq, int N, int K, f
     if (!encode_map(&ma, A, M, K, kBM))
         return cudaErrorInvalidValue;
     const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, splits};
-    return launch_q4<8>(ma, Wq, g, stream);
+    return per_sm == 2 ? launch_q4<4, 2>(ma, Wq, g, stream) : launch_q4<8>(ma, Wq, g, stream);
 }
 
 } // namespace nut
