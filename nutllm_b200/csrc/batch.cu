@@ -234,40 +234,63 @@ __global__ void zero_cols_kernel(__half *x, int B, int from, int Kp) {
     x[b * Kp + from + (i - b * tail)] = to_half_sat(0.0f);
 }
 
+/* One CTA per (chunk of kArgChunk logits, row): the chunk's largest key
+ * goes to keys[b] with a 64-bit atomic max, so keys[b] must be zero before
+ * the launch (keys_to_ids zeroes it once read). */
+constexpr int kArgThreads = 256;
+constexpr int kArgChunk = kArgThreads * 8;
+
 __global__ void argmax_keys_kernel(const float *logits, int V, int v0, unsigned long long *keys,
                                    float *clear) {
-    __shared__ unsigned long long best[32];
-    const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ unsigned long long best[kArgThreads / 32];
+    const int b = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * kArgChunk, c1 = min(V, c0 + kArgChunk);
     const float *row = logits + size_t(b) * V;
+    float *crow = clear != nullptr ? clear + size_t(b) * V : nullptr;
     unsigned long long k = 0ull;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const unsigned long long c = argmax_key(row[i], uint32_t(v0 + i));
-        k = c > k ? c : k;
+    const bool vec = (V & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+    if (vec) {
+        for (int i = c0 + 4 * int(threadIdx.x); i < c1; i += 4 * kArgThreads) {
+            const float4 v = *reinterpret_cast<const float4 *>(row + i);
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const unsigned long long c = argmax_key(e[j], uint32_t(v0 + i + j));
+                k = c > k ? c : k;
+            }
+            if (crow != nullptr) /* consumed: the next split-K GEMM adds into it */
+                *reinterpret_cast<float4 *>(crow + i) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+    } else {
+        for (int i = c0 + int(threadIdx.x); i < c1; i += kArgThreads) {
+            const unsigned long long c = argmax_key(row[i], uint32_t(v0 + i));
+            k = c > k ? c : k;
+            if (crow != nullptr)
+                crow[i] = 0.0f;
+        }
     }
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
         k = c > k ? c : k;
     }
-    if (clear != nullptr) /* consumed: the next split-K GEMM adds into it */
-        for (int i = threadIdx.x; i < V; i += blockDim.x)
-            clear[size_t(b) * V + i] = 0.0f;
     if (lane == 0)
         best[warp] = k;
     __syncthreads();
     if (threadIdx.x == 0) {
         unsigned long long m = 0ull;
-        for (int w = 0; w < int(blockDim.x >> 5); w++)
+        for (int w = 0; w < kArgThreads / 32; w++)
             m = best[w] > m ? best[w] : m;
-        keys[b] = m;
+        atomicMax(keys + b, m);
     }
 }
 
-__global__ void keys_to_ids_kernel(const unsigned long long *keys, int B, int32_t *ids,
+__global__ void keys_to_ids_kernel(unsigned long long *keys, int B, int32_t *ids,
                                    int32_t *out, int ld, const int *step) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B)
         return;
     const int32_t t = int32_t(argmax_index(keys[b]));
+    keys[b] = 0ull; /* ready for the next atomic max */
     ids[b] = t;
     if (out != nullptr)
         out[size_t(b) * ld + *step] = t;
@@ -476,13 +499,14 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
 
 cudaError_t argmax_keys(const float *logits, int B, int V, int v0, unsigned long long *keys,
                         bool clear, cudaStream_t s) {
-    argmax_keys_kernel<<<B, 256, 0, s>>>(logits, V, v0, keys,
-                                         clear ? const_cast<float *>(logits) : nullptr);
+    const dim3 grid(unsigned((V + kArgChunk - 1) / kArgChunk), unsigned(B));
+    argmax_keys_kernel<<<grid, kArgThreads, 0, s>>>(logits, V, v0, keys,
+                                                   clear ? const_cast<float *>(logits) : nullptr);
     count_launches(1);
     return cudaGetLastError();
 }
 
-cudaError_t keys_to_ids(const unsigned long long *keys, int B, int32_t *ids, int32_t *out,
+cudaError_t keys_to_ids(unsigned long long *keys, int B, int32_t *ids, int32_t *out,
                         int ld, const int *step, cudaStream_t s) {
     keys_to_ids_kernel<<<blocks_for(B, 128), 128, 0, s>>>(keys, B, ids, out, ld, step);
     count_launches(1);

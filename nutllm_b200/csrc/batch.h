@@ -43,13 +43,14 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
 /* Per row b: the first-index argmax of logits[b][0, V) as a 64-bit key
  * (order-preserving value bits << 32 | ~(v0 + index)), so that the maximum
  * key over any split of the vocabulary is the global first-index argmax
- * (std::max_element, src/generate.cpp:28-30).  With `clear` the logits are
- * zeroed once read. */
+ * (std::max_element, src/generate.cpp:28-30).  Chunks of a row combine by
+ * atomic max into keys[b], which must be zero on entry (keys_to_ids leaves
+ * it zero).  With `clear` the logits are zeroed once read. */
 cudaError_t argmax_keys(const float *logits, int B, int V, int v0, unsigned long long *keys,
                         bool clear, cudaStream_t s);
-/* ids[b] = token of keys[b]; also appended to out[b * ld + step] when out
- * is not null. */
-cudaError_t keys_to_ids(const unsigned long long *keys, int B, int32_t *ids, int32_t *out,
+/* ids[b] = token of keys[b] (then keys[b] = 0); also appended to
+ * out[b * ld + step] when out is not null. */
+cudaError_t keys_to_ids(unsigned long long *keys, int B, int32_t *ids, int32_t *out,
                         int ld, const int *step, cudaStream_t s);
 /* ids[b] = prompts[b * n + *step] (the next prompt column). */
 cudaError_t prompt_column(const int32_t *prompts, int B, int n, const int *step, int32_t *ids,

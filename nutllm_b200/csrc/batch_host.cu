@@ -319,6 +319,7 @@ void alloc_state(nut_batch &b) {
     cuda_check(cudaMemset(b.qkv, 0, B * b.nqkv * 4), "clear rows");
     cuda_check(cudaMemset(b.gu, 0, B * 2 * b.ffn_r * 4), "clear rows");
     cuda_check(cudaMemset(b.logits, 0, B * b.vocab_r * 4), "clear rows");
+    cuda_check(cudaMemset(b.keys, 0, B * sizeof(unsigned long long)), "clear keys");
     /* RoPE table with the reference's fp32 values (frequency and angle in
      * double, rounded once; src/quant_model.cpp:26-37) */
     const size_t half = size_t(b.hd / 2), S = size_t(b.max_seq);
@@ -956,6 +957,9 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
         cuda_check(cudaMemsetAsync(b->pos, 0, sizeof(int), s), "reset position");
         cuda_check(cudaMemsetAsync(b->pstep, 0, sizeof(int), s), "reset position");
         cuda_check(cudaMemsetAsync(b->ostep, 0, sizeof(int), s), "reset position");
+        /* the argmax keys start at zero (a step cut short leaves them set) */
+        cuda_check(cudaMemsetAsync(b->keys, 0, size_t(b->B) * sizeof(unsigned long long), s),
+                   "clear keys");
         /* replayed graphs unless logits are copied out every step */
         const bool graphs = logits == nullptr && std::getenv("NUTLLM_NO_GRAPHS") == nullptr;
         if (graphs)
