@@ -47,6 +47,68 @@ __global__ void add_rmsnorm_rows_kernel(float *h, float *part, int add, const fl
         o[k] = to_half_sat(k < dim ? x[k] * scale * w[k] : 0.0f);
 }
 
+/* The same row operation with the row held in registers: 256 threads,
+ * float4 loads and stores, at most kNormVec float4 per thread (dim <=
+ * 8192, dim % 4 == 0, 16-byte aligned rows, Kp % 2 == 0).  One read of h,
+ * part and w, one write of h, part and out. */
+constexpr int kNormThreads = 256;
+constexpr int kNormVec = 8;
+
+__global__ void __launch_bounds__(kNormThreads)
+add_rmsnorm_rows_vec_kernel(float *h, float *part, int add, const float *w, int dim, int Kp,
+                            __half *out) {
+    __shared__ float red[32];
+    const int b = blockIdx.x, n4 = dim / 4;
+    float4 *x4 = reinterpret_cast<float4 *>(h + size_t(b) * dim);
+    float4 *p4 = part != nullptr ? reinterpret_cast<float4 *>(part + size_t(b) * dim) : nullptr;
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    float4 v[kNormVec], g[kNormVec];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kNormVec; j++) {
+        const int i = int(threadIdx.x) + j * kNormThreads;
+        if (i < n4) {
+            v[j] = x4[i];
+            g[j] = w4[i];
+            if (p4 != nullptr && add) {
+                const float4 q = p4[i];
+                v[j].x += q.x, v[j].y += q.y, v[j].z += q.z, v[j].w += q.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kNormVec; j++) {
+        const int i = int(threadIdx.x) + j * kNormThreads;
+        if (i < n4) {
+            if (p4 != nullptr) {
+                if (add)
+                    x4[i] = v[j];
+                p4[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f); /* the next split-K GEMM adds into it */
+            }
+            ss = fmaf(v[j].x, v[j].x, ss);
+            ss = fmaf(v[j].y, v[j].y, ss);
+            ss = fmaf(v[j].z, v[j].z, ss);
+            ss = fmaf(v[j].w, v[j].w, ss);
+        }
+    }
+    const float total = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(total / float(dim) + kEps);
+    __half2 *o2 = reinterpret_cast<__half2 *>(out + size_t(b) * Kp);
+#pragma unroll
+    for (int j = 0; j < kNormVec; j++) {
+        const int i = int(threadIdx.x) + j * kNormThreads;
+        if (i < n4) {
+            o2[2 * i] = __halves2half2(to_half_sat(v[j].x * scale * g[j].x),
+                                       to_half_sat(v[j].y * scale * g[j].y));
+            o2[2 * i + 1] = __halves2half2(to_half_sat(v[j].z * scale * g[j].z),
+                                           to_half_sat(v[j].w * scale * g[j].w));
+        }
+    }
+    const __half2 zero = __halves2half2(__float2half(0.0f), __float2half(0.0f));
+    for (int k = dim / 2 + int(threadIdx.x); k < Kp / 2; k += kNormThreads)
+        o2[k] = zero;
+}
+
 /* One thread per (sequence b, rotation pair or value element). */
 __global__ void rope_kv_batch_kernel(float *qkv, int rows, int B, int ldq, const int *pos_p,
                                      const float *rope_cos, const float *rope_sin, int heads,
@@ -410,8 +472,16 @@ cudaError_t synth_q4_packed_dev(uint64_t seed, uint64_t stream, float sigma, int
 
 cudaError_t add_rmsnorm_rows(float *h, float *part, bool add, const float *w, int B, int dim,
                              int Kp, uint16_t *out, cudaStream_t s) {
-    add_rmsnorm_rows_kernel<<<B, 1024, 0, s>>>(h, part, add ? 1 : 0, w, dim, Kp,
-                                               reinterpret_cast<__half *>(out));
+    const bool vec = dim % 4 == 0 && Kp % 2 == 0 && dim <= 4 * kNormVec * kNormThreads &&
+                     ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(part) |
+                       reinterpret_cast<uintptr_t>(w)) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+    if (vec)
+        add_rmsnorm_rows_vec_kernel<<<B, kNormThreads, 0, s>>>(
+            h, part, add ? 1 : 0, w, dim, Kp, reinterpret_cast<__half *>(out));
+    else
+        add_rmsnorm_rows_kernel<<<B, 1024, 0, s>>>(h, part, add ? 1 : 0, w, dim, Kp,
+                                                   reinterpret_cast<__half *>(out));
     count_launches(1);
     return cudaGetLastError();
 }
