@@ -41,6 +41,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SEED = 1234
+L2_BYTES = 126 << 20  # B200 L2
 
 LABELS = {
     "tinyllama-int4": "TinyLlama-1.1B INT4",
@@ -55,6 +56,19 @@ def metric_of(wl):
 
 def dtype_of(wl, nb):
     return "int4xfp32" if wl.qtype == nb.INT4 else "int8xfp32"
+
+
+
+
+def config_of(wl, world):
+    """The workload description, identical in both arms of the bench."""
+    from nutllm_b200 import synthetic as syn  # workload tables only: loads no library
+    c = wl.model_config()
+    per_token = syn.algorithmic_decode_bytes(c, wl.qtype, 0)
+    return {"workload": wl.name, "prompt": wl.prompt, "decode_steps": wl.steps,
+            "batch": wl.batch, "parallelism": f"replicas{world}",
+            "l2": ("inputs larger than L2" if per_token > L2_BYTES else "inputs fit in L2")
+                  + " (%.1f MB of weights and classifier per token)" % (per_token / 1e6)}
 
 
 def cpu_sample(wl):
@@ -215,7 +229,8 @@ def run_ours(args, rank, world, local):
 
     value = wl.steps * args.steps * world / dec_s
     prefill_tps = wl.prompt * args.steps * world / pre_s
-    e2e = wl.steps * args.steps * world / wall
+    e2e = wl.steps * args.steps * world / (wall - pre_s)
+    e2e_gen = wl.steps * args.steps * world / wall
 
     if rank != 0:
         return
@@ -255,19 +270,18 @@ def run_ours(args, rank, world, local):
         "vs_baseline": None,
         "dtype": dtype_of(wl, nb),
         "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
-        "config": {"workload": wl.name, "prompt": wl.prompt,
-                   "decode_steps": wl.steps, "batch": wl.batch,
-                   "parallelism": f"replicas{world}",
-                   "l2": "inputs larger than L2 (%.1f MB of weights and "
-                         "classifier per token)"
-                         % (syn.algorithmic_decode_bytes(c, wl.qtype, 0) / 1e6),
-                   "timing": "step: CUDA events on the library stream; "
-                             "prefill/decode split: in-kernel device timer"},
+        "config": config_of(wl, world),
+        "timing": "step: CUDA events on the library stream; prefill/decode split: "
+                  "in-kernel device timer; e2e: wall clock around nut_generate_greedy "
+                  "with host buffers, less the device prefill time",
         "prefill_tok_s": round(prefill_tps, 2),
-        "e2e": {"value": round(e2e, 2),
-                "unit": "generated tok/s via nut_generate_greedy (incl. prefill)",
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": int(prompt.nbytes),
-                "d2h_bytes_per_step": int(wl.steps * 4)},
+                "d2h_bytes_per_step": int(wl.steps * 4),
+                "what": "decode tok/s through nut_generate_greedy with host buffers: "
+                        "wall clock of the calls (prompt copy in, ids copy out, launch) "
+                        "less the in-kernel prefill time",
+                "generated_tok_s_incl_prefill": round(e2e_gen, 2)},
         "gpu_launches": int(launches),
         "roofline": roofline,
         "qmatvec": micro,
@@ -291,6 +305,15 @@ TP_WORKLOADS = {
 }
 
 
+def tp_config_of(name, spec, world):
+    """The TP workload description, identical in both arms of the bench."""
+    return {"workload": name, "layers": spec["cfg"]["layers"], "batch": spec["batch"],
+            "prompt": spec["prompt"], "decode_steps": spec["steps"],
+            "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2 (every decode step reads the weights and "
+                  "KV cache, several GB, from HBM)"}
+
+
 def tp_decode_bytes(cfg, batch, prompt, steps, world):
     """Algorithmic bytes one rank reads per decode step, averaged over the
     steps: its share of the INT4 linears (q/4 + 2 bytes per 32 weights) and
@@ -307,35 +330,31 @@ def tp_decode_bytes(cfg, batch, prompt, steps, world):
     return (lin + cls + kv) / world + norms
 
 
-def cpu_estimate_tp(spec, reps=3):
-    """The reference's CPU decode of the 7B shape at batch 1 (its own
-    kernels, all host threads), bounded: one layer's projections timed with
-    matvec_quantized_threaded (Wq, Wk, Wv, Wo, Wgate, Wup, Wdown shapes) times
-    the layer count, plus the fp32 classifier with matvec_threaded.  Attention
-    and norms (under 2 % of a token's bytes at these lengths) are not timed."""
+def cpu_reference_7b(spec, samples=1, warmup=1, n_prompt=4, n_steps=4):
+    """The reference's own quantised token loop on the full 7B shape at
+    batch 1 (it generates one sequence at a time): the unmodified reference
+    (oracle/_ref) builds and quantises the model from the seeded weights, then
+    runs prefill_quantized + greedy decode_quantized_token over all host
+    threads.  Bounded: each sample is an n_prompt-token prompt and n_steps
+    greedy steps.  Returns (decode tok/s, prefill tok/s, threads, sample)."""
     import oracle
     threads = os.cpu_count() or 1
     if not oracle.reference_available():
-        return None, threads, "oracle/_ref not built"
-    cfg = spec["cfg"]
-    d, f, L, V = cfg["dim"], cfg["ffn_dim"], cfg["layers"], cfg["vocab_size"]
-    kvd = cfg["kv_heads"] * cfg["head_dim"]
-    r = oracle.Reference()
-    rng = np.random.default_rng(SEED)
-    per_layer = 0.0
-    shapes = {(d, d): 2, (kvd, d): 2, (f, d): 2, (d, f): 1}
-    for (rows, cols), count in shapes.items():
-        w = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02)
-        data, scales = r.quantize(w, 1)
-        x = rng.standard_normal(cols, dtype=np.float32)
-        sec, _ = r.qmatvec_time(1, rows, cols, data, scales, x, threads, reps)
-        per_layer += count * sec
-    cls = rng.standard_normal((V, d), dtype=np.float32) * 0.02
-    head = r.matvec_time(cls, rng.standard_normal(d, dtype=np.float32), threads, reps)
-    token = L * per_layer + head
-    sample = (f"batch 1: one layer's quantised projections ({reps} timed calls each) "
-              f"x {L} layers + the fp32 classifier, reference kernels, {threads} threads")
-    return 1.0 / token, threads, sample
+        return None, None, threads, "oracle/_ref not built"
+    from nutllm_b200 import synthetic as syn  # workload tables only: loads no library
+    cfg = syn.Config(**spec["cfg"])
+    rm = oracle.Reference().model(cfg, 1, SEED)
+    prompt = oracle.prompt_ids(cfg, SEED, n_prompt)
+    for _ in range(warmup):
+        rm.generate(prompt, 1, threads, want_logits=False)
+    dec = pre = 0.0
+    for _ in range(samples):
+        _, _, _, ps, ds = rm.generate(prompt, n_steps, threads, want_logits=False)
+        dec += ds
+        pre += ps
+    sample = (f"batch 1, all {cfg.layers} layers: {n_prompt}-token prompt + {n_steps} greedy "
+              f"steps per sample, {samples} samples, reference kernels, {threads} threads")
+    return n_steps * samples / dec, n_prompt * samples / pre, threads, sample
 
 
 def run_batch_tp(args, rank, world, local):
@@ -388,9 +407,10 @@ def run_batch_tp(args, rank, world, local):
         return
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_estimate_tp(spec)
+        v, pv, cores, sample = cpu_reference_7b(spec)
         cpu = {"value": round(v, 3) if v else None, "unit": "decode tok/s (batch 1)",
-               "cores": cores, "kind": "reference", "sample": sample}
+               "cores": cores, "kind": "reference",
+               "prefill_tok_s": round(pv, 3) if pv else None, "sample": sample}
     value = B * steps * args.steps / dec_s
     step_s = dec_s / (args.steps * steps)
     peak, src = measured_peaks()
@@ -410,12 +430,9 @@ def run_batch_tp(args, rank, world, local):
         "dtype": "fp16xfp16 (dequantised INT4 weights)",
         "data": "synthetic (seeded random INT4 block-32 weights generated on the device, "
                 "N(0,0.02) embeddings and classifier, uniform prompt ids)",
-        "config": {"workload": args.workload, "layers": cfg.layers, "batch": B, "prompt": n,
-                   "decode_steps": steps, "parallelism": f"tp{world}",
-                   "all_reduce": allreduce if world > 1 else None,
-                   "l2": "inputs larger than L2 (every decode step reads the weights and "
-                         "KV cache, several GB, from HBM)",
-                   "timing": "CUDA events on the library stream around prefill and decode"},
+        "config": tp_config_of(args.workload, spec, world),
+        "all_reduce": allreduce if world > 1 else None,
+        "timing": "CUDA events on the library stream around prefill and decode",
         "prefill_tok_s": round(B * n * args.steps / pre_s, 2),
         "e2e": {"value": round(B * steps * args.steps / wall, 2),
                 "unit": "generated tok/s via nut_batch_generate (incl. prefill)",
@@ -646,7 +663,7 @@ def cpu_baseline(wl, c):
     n_prompt, n_steps = cpu_sample(wl)
     r = oracle.Reference()
     rm = r.model(c, wl.qtype, SEED)
-    prompt = syn.prompt_ids(c, SEED, n_prompt)
+    prompt = oracle.prompt_ids(c, SEED, n_prompt)
     _, _, _, ps, ds = rm.generate(prompt, n_steps, threads, want_logits=False)
     whole = (n_prompt, n_steps) == (wl.prompt, wl.steps)
     return {"value": round(n_steps / ds, 3), "unit": "decode tok/s",
@@ -663,8 +680,8 @@ def cpu_baseline(wl, c):
 
 def run_reference_tp(args, world):
     spec = TP_WORKLOADS[args.workload]
-    # one set of matrices, each matvec timed over `steps` calls
-    value, cores, sample = cpu_estimate_tp(spec, reps=max(args.steps, 1))
+    value, pvalue, cores, sample = cpu_reference_7b(spec, samples=max(args.steps, 1),
+                                                    warmup=min(args.warmup, 1))
     if value is None:
         print(json.dumps({"impl": "reference", "unavailable": sample}))
         return
@@ -672,10 +689,12 @@ def run_reference_tp(args, world):
         "impl": "reference",
         "metric": f"decode tok/s (Llama-2-7B INT4 shape, batch {spec['batch']}, tensor parallel)",
         "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(1e3 / value, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "int4xfp32", "data": "synthetic",
-        "config": {"workload": args.workload, "batch": 1,
-                   "note": "the reference generates one sequence at a time"},
+        "warmup": args.warmup, "ms_per_step": round(1e3 * 4 / value, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4xfp32", "data": "synthetic",
+        "config": tp_config_of(args.workload, spec, world),
+        "note": "the reference generates one sequence at a time (batch 1)",
+        "prefill_tok_s": round(pvalue, 3),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": cores,
                          "kind": "reference", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -684,13 +703,16 @@ def run_reference_tp(args, world):
 
 
 def run_reference(args, rank, world):
+    """The reference's own CPU token loop (oracle/_ref, the unmodified
+    reference compiled from its sources), fed by the oracle's restatement of
+    the seeded generator: no library of this repository is loaded."""
     if rank != 0:
         return
     if args.workload in TP_WORKLOADS:
         run_reference_tp(args, world)
         return
     import oracle
-    from nutllm_b200 import synthetic as syn
+    from nutllm_b200 import synthetic as syn  # workload tables only: loads no library
     wl = syn.WORKLOADS[args.workload]
     c = wl.model_config()
     if not oracle.reference_available():
@@ -702,7 +724,7 @@ def run_reference(args, rank, world):
     r = oracle.Reference()
     rm = r.model(c, wl.qtype, SEED)
     n_prompt, sample_steps = cpu_sample(wl)
-    prompt = syn.prompt_ids(c, SEED, n_prompt)
+    prompt = oracle.prompt_ids(c, SEED, n_prompt)
     for _ in range(min(args.warmup, 1)):
         rm.generate(prompt, 1, threads, want_logits=False)
     dec, pre = 0.0, 0.0
@@ -719,16 +741,19 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * (dec + pre) / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4xfp32" if wl.qtype == 1 else "int8xfp32", "data": "synthetic",
-        "config": {"workload": wl.name, "prompt": wl.prompt,
-                   "decode_steps": wl.steps, "batch": 1},
+        "dtype": "int4xfp32" if wl.qtype == 1 else "int8xfp32",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
+        "config": config_of(wl, world),
+        "timing": "wall clock of the reference's prefill_quantized and decode loop, "
+                  f"{threads} host threads",
         "prefill_tok_s": round(n_prompt * args.steps / pre, 3),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s",
                          "cores": threads, "kind": "reference",
                          "sample": f"{n_prompt}-token prompt + {sample_steps} "
                                    f"greedy steps of {wl.name} per step"},
         "e2e": {"value": round(value, 3), "unit": "tok/s",
-                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                "generated_tok_s_incl_prefill": round(sample_steps * args.steps / (dec + pre), 3)},
     }), flush=True)
 
 

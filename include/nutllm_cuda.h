@@ -317,12 +317,15 @@ nut_status nut_batch_generate(nut_batch *batch, const int32_t *prompts, int64_t 
  * the array's address (with that device current) and should come before
  * any stream capture.  Every call shares the array and clears the rows it
  * uses: calls whose work overlaps on the GPU race, so the caller must
- * serialise them.
+ * serialise them.  A cudaDeviceReset() after the first call on a device is
+ * not supported.
  *   hidden [batch][dim], final_norm [dim], weights [vocab][dim] (fp32),
  *   logits [batch][vocab] (may be NULL), argmax [batch] (int32);
  *   enqueued on `stream` (a cudaStream_t, NULL = legacy default stream).
- * No counterpart in the reference, whose greedy head runs on host vectors
- * (src/generate.cpp:197-201); nut_logits is the model-handle form. */
+ * Pointers need only their element's alignment (4 bytes; others fail with
+ * NUT_INVALID_ARGUMENT); 16-byte-aligned weights with dim % 4 == 0 are read
+ * as float4.  This entry point has no counterpart in the reference;
+ * nut_logits is this library's model-handle form of the same head. */
 nut_status nut_greedy_head_static(const float *hidden, const float *final_norm,
                                   const float *weights, int64_t batch, int64_t vocab,
                                   int64_t dim, float *logits, int32_t *argmax,

@@ -11,10 +11,18 @@
  *
  * The array's address is resolved once per device, on the first call made
  * on that device with the device current; that first call should therefore
- * come before any CUDA stream capture.  Every call shares the array and
- * clears the rows it uses before its own kernels run, so calls whose work
- * overlaps on the GPU (other streams, or other host threads on the same
- * device) race on it and must be serialised by the caller.
+ * come before any CUDA stream capture.  The resolved address is kept for
+ * the life of the process: a cudaDeviceReset() of a device after its first
+ * call is not supported (the next context would need the address resolved
+ * again).  Every call shares the array and clears the rows it uses before
+ * its own kernels run, so calls whose work overlaps on the GPU (other
+ * streams, or other host threads on the same device) race on it and must be
+ * serialised by the caller.
+ *
+ * Alignment: every pointer must be aligned to its element (4 bytes).  The
+ * classifier rows are read as float4 only when dim % 4 == 0 and `weights`
+ * is 16-byte aligned; any other 4-byte-aligned arena pointer takes the
+ * scalar loop, so no caller alignment beyond the element is required.
  */
 #include <algorithm>
 #include <cstdint>
@@ -70,7 +78,7 @@ __global__ void clear_keys(unsigned long long *keys, int rows) {
  * argmax folded into keys[row] with atomicMax. */
 __global__ void __launch_bounds__(256)
 head_kernel(const float *__restrict__ hidden, const float *__restrict__ norm,
-            const float *__restrict__ weights, int vocab, int dim,
+            const float *__restrict__ weights, int vocab, int dim, int vec,
             float *__restrict__ logits, unsigned long long *keys) {
     extern __shared__ float4 xs4[];
     __shared__ float red[32];
@@ -89,7 +97,6 @@ head_kernel(const float *__restrict__ hidden, const float *__restrict__ norm,
     const int warps = blockDim.x >> 5;
     float *out = logits != nullptr ? logits + size_t(blockIdx.y) * vocab : nullptr;
     unsigned long long mine = 0ull;
-    const bool vec = (dim % 4) == 0;
     for (int r = blockIdx.x * warps + warp; r < vocab; r += gridDim.x * warps) {
         const float *row = weights + size_t(r) * dim;
         float acc = 0.0f;
@@ -149,6 +156,14 @@ extern "C" nut_status nut_greedy_head_static(const float *hidden, const float *f
                         " exceeds the static scratch limit of " + std::to_string(kMaxRows));
     if (vocab > (int64_t(1) << 30) || dim > (1 << 14))
         return fail(NUT_LENGTH_ERROR, "greedy head: dimensions exceed device limits");
+    auto misaligned = [](const void *p, uintptr_t a) {
+        return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0;
+    };
+    if (misaligned(hidden, 4) || misaligned(final_norm, 4) || misaligned(weights, 4) ||
+        misaligned(logits, 4) || misaligned(argmax, 4))
+        return fail(NUT_INVALID_ARGUMENT, "greedy head: pointer not aligned to its element");
+    /* float4 rows need 16-byte row starts: dim % 4 == 0 and an aligned base */
+    const int vec = (dim % 4 == 0 && !misaligned(weights, 16)) ? 1 : 0;
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess)
@@ -171,7 +186,7 @@ extern "C" nut_status nut_greedy_head_static(const float *hidden, const float *f
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     const int per_row = int(std::min<int64_t>((vocab + 7) / 8, int64_t(4) * sms));
     head_kernel<<<dim3(per_row, rows), 256, smem, s>>>(hidden, final_norm, weights, int(vocab),
-                                                        int(dim), logits, keys);
+                                                        int(dim), vec, logits, keys);
     keys_to_index<<<(rows + 255) / 256, 256, 0, s>>>(keys, rows, argmax);
     nut::count_launches(3);
     e = cudaGetLastError();

@@ -22,12 +22,18 @@
 
 namespace {
 
-size_t checked_elements(size_t rows, size_t cols) {
-    if (rows == 0 || cols == 0 ||
-        rows > std::numeric_limits<size_t>::max() / cols)
+/* rows x cols, or invalid_argument when either is zero or the product
+ * does not fit in size_t. */
+size_t element_count(size_t rows, size_t cols) {
+    size_t n = 0;
+    const bool wraps = __builtin_mul_overflow(rows, cols, &n);
+    if (wraps || n == 0)
         throw std::invalid_argument("quantize: invalid dimensions");
-    return rows * cols;
+    return n;
 }
+
+/* Largest quantised magnitude of a type: 2^(bits-1) - 1. */
+constexpr int type_limit(QuantType type) { return type == QuantType::int8 ? 127 : 7; }
 
 uint32_t float_bits(float v) {
     uint32_t b;
@@ -100,13 +106,19 @@ float quant_half_to_float(uint16_t value) {
 QuantizedMatrix::QuantizedMatrix(size_t rows, size_t cols, size_t block_size,
                                  QuantType type)
     : rows_(rows), cols_(cols), block_size_(block_size), type_(type) {
-    const size_t elements = checked_elements(rows, cols);
+    const size_t n = element_count(rows, cols);
     if (block_size == 0)
         throw std::invalid_argument("quantize: zero block size");
-    if (elements > std::numeric_limits<size_t>::max() - (block_size - 1))
+    /* a partial last block still gets a scale: ceil(n / block_size), whose
+     * rounded-up numerator must itself fit in size_t */
+    size_t padded = 0;
+    if (__builtin_add_overflow(n, block_size - 1, &padded))
         throw std::length_error("quantize: block count overflow");
-    scales_.resize((elements + block_size - 1) / block_size);
-    data_.resize(type == QuantType::int8 ? elements : (elements + 1) / 2);
+    const size_t blocks = padded / block_size;
+    /* int8: one byte per element; int4: two elements per byte, low first */
+    const size_t bytes = type == QuantType::int8 ? n : n / 2 + (n & 1);
+    scales_.assign(blocks, 0);
+    data_.assign(bytes, 0);
 }
 
 QuantizedMatrix QuantizedMatrix::quantize(const Matrix &source, QuantType type,
@@ -121,7 +133,7 @@ QuantizedMatrix QuantizedMatrix::quantize(const float *source, size_t rows,
     if (source == nullptr)
         throw std::invalid_argument("quantize: null source");
     QuantizedMatrix out(rows, cols, block_size, type);
-    const int limit = type == QuantType::int8 ? 127 : 7;
+    const int limit = type_limit(type);
     const size_t n = out.size();
     uint8_t *data = out.data_.data();
     uint16_t *scales = out.scales_.data();
@@ -171,59 +183,80 @@ QuantizedMatrix QuantizedMatrix::from_storage(size_t rows, size_t cols,
     return out;
 }
 
-int QuantizedMatrix::quantized_value(size_t index) const {
-    if (index >= size())
+namespace {
+
+/* Flat index of (row, column) in a rows x cols matrix, or out_of_range. */
+size_t flat_index(size_t rows, size_t cols, size_t row, size_t column) {
+    if (!(row < rows && column < cols))
         throw std::out_of_range("quantized matrix: index out of range");
-    if (type_ == QuantType::int8)
-        return int(int8_t(data_[index]));
-    const unsigned nibble =
-        index % 2 == 0 ? data_[index / 2] & 0x0fu : data_[index / 2] >> 4;
-    return nibble >= 8 ? int(nibble) - 16 : int(nibble);
+    return row * cols + column;
+}
+
+/* Signed value of a two's-complement field of `bits` bits. */
+int sign_extend(unsigned field, int bits) {
+    const unsigned top = 1u << (bits - 1);
+    return int(field ^ top) - int(top);
+}
+
+} // namespace
+
+int QuantizedMatrix::quantized_value(size_t index) const {
+    if (!(index < size()))
+        throw std::out_of_range("quantized matrix: index out of range");
+    if (type_ == QuantType::int4) {
+        /* element 2i is the low nibble of byte i, element 2i+1 the high */
+        const unsigned byte = data_[index >> 1];
+        return sign_extend((byte >> (4 * (index & 1))) & 0x0fu, 4);
+    }
+    return sign_extend(data_[index], 8);
 }
 
 float QuantizedMatrix::scale(size_t block) const {
-    if (block >= scales_.size())
+    if (!(block < scales_.size()))
         throw std::out_of_range("quantized matrix: block out of range");
     return quant_half_to_float(scales_[block]);
 }
 
 float QuantizedMatrix::value(size_t row, size_t column) const {
-    if (row >= rows_ || column >= cols_)
-        throw std::out_of_range("quantized matrix: index out of range");
-    const size_t index = row * cols_ + column;
-    return float(quantized_value(index)) * scale(index / block_size_);
+    const size_t i = flat_index(rows_, cols_, row, column);
+    const float step = scale(i / block_size_);
+    return float(quantized_value(i)) * step;
 }
 
-/* Half a quantisation step plus the fp16 rounding of the scale, as the
- * reference bounds it (src/quant.cpp:224-233). */
+/* The reference's per-element bound (src/quant.cpp:224-233): half a
+ * quantisation step, plus (limit + 1/2) times the larger of the fp16
+ * scale's relative rounding (scale / 2047) and half an fp16 subnormal
+ * step (2^-25). */
 float QuantizedMatrix::error_bound(size_t row, size_t column) const {
-    if (row >= rows_ || column >= cols_)
-        throw std::out_of_range("quantized matrix: index out of range");
-    const size_t index = row * cols_ + column;
-    const float stored = scale(index / block_size_);
-    const float half_rounding = std::max(stored / 2047.0f, std::ldexp(1.0f, -25));
-    const float limit = type_ == QuantType::int8 ? 127.0f : 7.0f;
-    return stored * 0.5f + (limit + 0.5f) * half_rounding;
+    const size_t i = flat_index(rows_, cols_, row, column);
+    const float step = scale(i / block_size_);
+    const float scale_rounding = std::max(step / 2047.0f, 0x1p-25f);
+    const float reach = float(type_limit(type_)) + 0.5f;
+    return 0.5f * step + reach * scale_rounding;
 }
 
 size_t QuantizedMatrix::storage_bytes() const {
-    if (scales_.size() >
-        (std::numeric_limits<size_t>::max() - data_.size()) / sizeof(uint16_t))
+    size_t scale_bytes = 0, total = 0;
+    if (__builtin_mul_overflow(scales_.size(), sizeof(uint16_t), &scale_bytes) ||
+        __builtin_add_overflow(scale_bytes, data_.size(), &total))
         throw std::overflow_error("quantized matrix: storage size overflow");
-    return data_.size() + scales_.size() * sizeof(uint16_t);
+    return total;
 }
 
 uint8_t QuantizedMatrix::packed_byte(size_t index) const {
-    if (type_ != QuantType::int4 || index >= data_.size())
+    const bool packed = type_ == QuantType::int4;
+    if (!packed || !(index < data_.size()))
         throw std::out_of_range("quantized matrix: packed byte out of range");
     return data_[index];
 }
 
 Matrix dequantize(const QuantizedMatrix &source) {
     Matrix result(source.rows(), source.cols());
-    for (size_t r = 0; r < source.rows(); r++)
-        for (size_t c = 0; c < source.cols(); c++)
-            result.at(r, c) = source.value(r, c);
+    /* one pass over the flat row-major storage */
+    float *out = result.data();
+    const size_t cols = source.cols();
+    for (size_t i = 0, n = source.size(); i < n; i++)
+        out[i] = source.value(i / cols, i % cols);
     return result;
 }
 

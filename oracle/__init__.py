@@ -31,6 +31,21 @@ def _ptr(a):
     return None if a is None else a.ctypes.data
 
 
+def reference_dir() -> Optional[str]:
+    """Where the reference's sources lie, if anywhere: $NUTLLM_REFERENCE, else
+    the "reference_path" of the repository's BASELINE.json; None when
+    neither names an existing directory (e.g. on a GPU box)."""
+    import json
+    path = os.environ.get("NUTLLM_REFERENCE")
+    if not path:
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                path = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            path = None
+    return path if path and os.path.isdir(path) else None
+
+
 def build_oracle() -> str:
     """Builds liboracle.so with gcc if it is missing (it is plain C)."""
     if not os.path.exists(ORACLE_LIB):
@@ -99,6 +114,10 @@ class Oracle:
         lib.orc_generate_sampled.argtypes = [C.POINTER(_Model), C.POINTER(_KV), _P,
                                              _I64, _I64, C.c_float, C.c_float,
                                              C.c_uint32, _P, C.POINTER(_I64)]
+        lib.orc_synth_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_float, _P, _I64]
+        lib.orc_synth_normal.restype = None
+        lib.orc_synth_tokens.argtypes = [C.c_uint64, C.c_uint64, C.c_int, C.c_int, _P, _I64]
+        lib.orc_synth_tokens.restype = None
         self.lib = lib
 
     def _check(self, status):
@@ -180,11 +199,66 @@ class Oracle:
         self.lib.orc_rope(_ptr(values), values.size, position)
         return values
 
+    def synth_normal(self, seed: int, stream: int, n: int, sigma: float) -> np.ndarray:
+        """The benchmark's seeded N(0, sigma^2) stream (orc_synth_normal)."""
+        out = np.empty(n, np.float32)
+        self.lib.orc_synth_normal(seed, stream, sigma, _ptr(out), n)
+        return out
+
+    def synth_tokens(self, seed: int, stream: int, n: int, lo: int, hi: int) -> np.ndarray:
+        out = np.empty(n, np.int32)
+        self.lib.orc_synth_tokens(seed, stream, lo, hi, _ptr(out), n)
+        return out
+
     def model(self, weights) -> "OracleModel":
         return OracleModel(self, weights)
 
     def fp32_model(self, tensors: dict) -> "Fp32Model":
         return Fp32Model(self, tensors)
+
+
+# ------------------------------------------------- seeded workload tensors
+#
+# The benchmark's synthetic tensors drawn by the oracle's own restatement of
+# the generator, so the reference's CPU baseline loads no library of this
+# repository: embeddings stream 1, classifier stream 2, prompt ids token
+# stream 3, projection j of layer l stream 1000 + 8 l + j, N(0, 0.02).
+
+SIGMA = 0.02
+_shared_oracle = None
+
+
+def _orc() -> "Oracle":
+    global _shared_oracle
+    if _shared_oracle is None:
+        _shared_oracle = Oracle()
+    return _shared_oracle
+
+
+def projection_shapes(c):
+    kv = int(c.kv_heads or c.heads) * int(c.head_dim)
+    d, f = int(c.dim), int(c.ffn_dim)
+    return [(d, d), (kv, d), (kv, d), (d, d), (f, d), (f, d), (d, f)]
+
+
+def embeddings_fp32(c, seed: int) -> np.ndarray:
+    V, d = int(c.vocab_size), int(c.dim)
+    return _orc().synth_normal(seed, 1, V * d, SIGMA).reshape(V, d)
+
+
+def lm_head_fp32(c, seed: int) -> np.ndarray:
+    V, d = int(c.vocab_size), int(c.dim)
+    return _orc().synth_normal(seed, 2, V * d, SIGMA).reshape(V, d)
+
+
+def projection_fp32(c, seed: int, layer: int, j: int) -> np.ndarray:
+    rows, cols = projection_shapes(c)[j]
+    return _orc().synth_normal(seed, 1000 + 8 * layer + j, rows * cols,
+                               SIGMA).reshape(rows, cols)
+
+
+def prompt_ids(c, seed: int, n: int, stream: int = 3) -> np.ndarray:
+    return _orc().synth_tokens(seed, stream, n, 1, int(c.vocab_size) - 1)
 
 
 class OracleModel:
@@ -610,21 +684,20 @@ class RefModel:
 
     def __init__(self, ref: Reference, c, qtype, seed, tied, layer_fp32=None,
                  embeddings=None, lm_head=None):
-        from nutllm_b200 import synthetic as syn
         self.r = ref
         self.config = c
         cfg = (_I64 * 9)(*[int(getattr(c, n)) for n, _ in _Config._fields_])
         h = _P()
         ref._check(ref.lib.ref_model_new(cfg, qtype, int(tied), C.byref(h)))
         self.h = h
-        emb = embeddings if embeddings is not None else syn.embeddings_fp32(c, seed)
+        emb = embeddings if embeddings is not None else embeddings_fp32(c, seed)
         ref._check(ref.lib.ref_model_set_embeddings(h, _ptr(emb)))
         ones = np.ones(c.dim, np.float32)
-        lm = None if tied else (lm_head if lm_head is not None else syn.lm_head_fp32(c, seed))
+        lm = None if tied else (lm_head if lm_head is not None else lm_head_fp32(c, seed))
         ref._check(ref.lib.ref_model_set_final(h, _ptr(ones), _ptr(lm)))
         for layer in range(c.layers):
             mats = ([layer_fp32(layer, j) for j in range(7)] if layer_fp32
-                    else [syn.projection_fp32(c, seed, layer, j) for j in range(7)])
+                    else [projection_fp32(c, seed, layer, j) for j in range(7)])
             arr = (_P * 7)(*[m.ctypes.data for m in mats])
             ref._check(ref.lib.ref_model_add_layer(h, arr, _ptr(ones), _ptr(ones)))
 

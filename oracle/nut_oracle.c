@@ -694,3 +694,61 @@ int orc_generate_sampled(const orc_model *m, orc_kv *kv, const int *prompt,
     free(hidden), free(row), free(weight), free(order);
     return status;
 }
+
+/* ---- seeded synthetic inputs ------------------------------------------
+ *
+ * The benchmark's documented counter-based generator (the reference has no
+ * seeded N(0, sigma) initialiser), restated here so the reference's CPU
+ * baseline can be fed the same bytes without loading this repository's own
+ * libraries:
+ *   key     = splitmix64(seed ^ splitmix64(stream))   (Steele, Lea, Flood 2014)
+ *   u1, u2  = 53-bit uniforms in (0, 1] of splitmix64(key + 2j), (key + 2j + 1)
+ *   z0, z1  = Box-Muller in double, out[2j] = float(sigma z0), out[2j+1] =
+ *             float(sigma z1)
+ * Token ids: lo + splitmix64(splitmix64(seed ^ splitmix64(stream ^
+ * "token")) + i) mod (hi - lo + 1). */
+
+static uint64_t orc_splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+static double orc_unit53(uint64_t bits) {
+    return (double)((bits >> 11) + 1) * (1.0 / 9007199254740992.0);
+}
+
+typedef struct {
+    uint64_t key;
+    double sigma;
+    float *out;
+    int64_t n;
+} synth_ctx;
+
+static void synth_pairs(void *arg, int64_t begin, int64_t end) {
+    const synth_ctx *s = arg;
+    const double two_pi = 6.283185307179586476925286766559;
+    for (int64_t pair = begin; pair < end; pair++) {
+        const double u1 = orc_unit53(orc_splitmix64(s->key + 2 * (uint64_t)pair));
+        const double u2 = orc_unit53(orc_splitmix64(s->key + 2 * (uint64_t)pair + 1));
+        const double r = sqrt(-2.0 * log(u1));
+        const double t = two_pi * u2;
+        const int64_t i = 2 * pair;
+        s->out[i] = (float)(s->sigma * (r * cos(t)));
+        if (i + 1 < s->n)
+            s->out[i + 1] = (float)(s->sigma * (r * sin(t)));
+    }
+}
+
+void orc_synth_normal(uint64_t seed, uint64_t stream, float sigma, float *out, int64_t n) {
+    synth_ctx s = {orc_splitmix64(seed ^ orc_splitmix64(stream)), (double)sigma, out, n};
+    parallel_rows((n + 1) / 2, synth_pairs, &s);
+}
+
+void orc_synth_tokens(uint64_t seed, uint64_t stream, int lo, int hi, int *out, int64_t n) {
+    const uint64_t key = orc_splitmix64(seed ^ orc_splitmix64(stream ^ 0x746f6b656eull));
+    const uint64_t span = (uint64_t)((int64_t)hi - (int64_t)lo + 1);
+    for (int64_t i = 0; i < n; i++)
+        out[i] = (int)((int64_t)lo + (int64_t)(orc_splitmix64(key + (uint64_t)i) % span));
+}

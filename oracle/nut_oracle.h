@@ -102,6 +102,12 @@ int orc_generate_sampled(const orc_model *model, orc_kv *kv, const int *prompt,
                          int64_t n, int64_t max_tokens, float temperature,
                          float top_p, uint32_t seed, int *ids, int64_t *n_out);
 
+/* The benchmark's seeded synthetic inputs (the same documented generator
+ * as the product's host library): n N(0, sigma^2) floats of `stream`, and n
+ * token ids uniform in [lo, hi]. */
+void orc_synth_normal(uint64_t seed, uint64_t stream, float sigma, float *out, int64_t n);
+void orc_synth_tokens(uint64_t seed, uint64_t stream, int lo, int hi, int *out, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

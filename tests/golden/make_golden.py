@@ -2,7 +2,7 @@
 reference (oracle/_ref/libnutref.so, built from the reference sources by
 oracle/Makefile).  Run from the repository root:
 
-    make -C oracle ref && python tests/golden/make_golden.py
+    make -C oracle ref REF=<reference source tree> && python tests/golden/make_golden.py
 
 quant_golden.npz   seeded and edge-case fp32 matrices with the reference
                    quantiser's bytes, fp16 scales, dequantised values,

@@ -21,8 +21,7 @@ from tests.golden import make_llama2c_fixture as fx
 
 G = np.load(golden_path("llama2c_golden.npz"))
 QTYPES = ((0, "int8"), (1, "int4"), (2, "fp32"))
-REF_FIXTURES = os.path.join(os.environ.get("NUTLLM_REFERENCE", "/root/reference"),
-                            "tests", "fixtures")
+REF_FIXTURES = os.path.join(oracle.reference_dir() or os.devnull, "tests", "fixtures")
 
 
 @pytest.fixture(scope="module")

@@ -199,3 +199,22 @@ def test_quant_selftest_known_answers(orc):
         _perplexity(_matmul_f32(acts, _dequantize(orc, w, q)[0]), targets)
         for q in (nb.INT8, nb.INT4)]
     assert [round(v, 3) for v in got] == [11.598, 11.608, 11.715]
+
+
+def test_oracle_synthetic_generator_bit_identical_to_host_library(orc):
+    """The reference's CPU baseline draws its weights and prompt through the
+    oracle's own restatement of the seeded generator; it must give the host
+    library's bytes exactly (odd lengths and several streams included)."""
+    import oracle
+    for seed, stream, n, sigma in ((1234, 1, 4097, 0.02), (7, 1003, 1 << 16, 0.02),
+                                   (99, 8, 33, 1.0), (1234, 2, 1, 0.02)):
+        a = orc.synth_normal(seed, stream, n, sigma)
+        b = nb.synth_normal(seed, stream, n, sigma)
+        assert a.tobytes() == b.tobytes()
+    for seed, stream, n, lo, hi in ((1234, 3, 512, 1, 31999), (5, 9, 100, 1, 511)):
+        assert np.array_equal(orc.synth_tokens(seed, stream, n, lo, hi),
+                              nb.synth_tokens(seed, stream, n, lo, hi))
+    c = syn.WORKLOADS["tiny-int8"].model_config()
+    assert np.array_equal(oracle.projection_fp32(c, 1234, 2, 6),
+                          syn.projection_fp32(c, 1234, 2, 6))
+    assert np.array_equal(oracle.prompt_ids(c, 1234, 5), syn.prompt_ids(c, 1234, 5))

@@ -22,8 +22,7 @@ from tests.conftest import golden_path
 from tests.golden import make_safetensors_fixture as fx
 
 G = np.load(golden_path("safetensors_golden.npz"))
-REF_FIXTURES = os.path.join(os.environ.get("NUTLLM_REFERENCE", "/root/reference"),
-                            "tests", "fixtures")
+REF_FIXTURES = os.path.join(oracle.reference_dir() or os.devnull, "tests", "fixtures")
 HAVE_REF_FIXTURES = os.path.exists(os.path.join(REF_FIXTURES, "tiny.safetensors"))
 STATUS = {ValueError: 1, IndexError: 2, nb.LengthError: 3, RuntimeError: 4,
           nb.RangeError: 5}
