@@ -298,6 +298,25 @@ nut_status nut_batch_generate(nut_batch *batch, const int32_t *prompts, int64_t 
                               int64_t steps, int32_t *ids, float *logits,
                               nut_generation_stats *stats);
 
+/* One call of the peer-memory all-reduce (fp32 sum of n floats, n % 4 ==
+ * 0) that the tensor-parallel decoder can use in place of NCCL, on
+ * caller-owned buffers: recv[q] / flags[q] are rank q's receive area
+ * ([2][world][n] floats) and flag words ([world][NUT_PEER_AR_CHUNKS]), as
+ * this process addresses them (its own, or IPC mappings of the peers'),
+ * zeroed before the first call; epochs [NUT_PEER_AR_CHUNKS] and error [1]
+ * are this rank's, zeroed before the first call.  Every rank makes the same
+ * sequence of calls with the same n.  Each wait for a peer's chunk gives up
+ * after limit_ns nanoseconds: the call then returns NUT_DEVICE_TIMEOUT (the
+ * kernel has ended; the device stays usable) and clears the error word.
+ * Synchronises `stream` to read the error word.  The reference has no
+ * multi-GPU path; like its RowExecutor, which hands a worker's failure back
+ * to the caller (src/threading.cpp:58-74,91-99), a failed wait is reported
+ * to the caller instead of hanging. */
+#define NUT_PEER_AR_CHUNKS 128
+nut_status nut_peer_all_reduce(const float *x, float *out, int64_t n, float *const *recv,
+                               unsigned *const *flags, int rank, int world, unsigned *epochs,
+                               int *error, int64_t limit_ns, void *stream);
+
 /* ---- Greedy head without allocation ------------------------------------ */
 
 /* Largest batch of nut_greedy_head_static. */

@@ -200,6 +200,8 @@ def cuda_lib() -> C.CDLL:
         _declare(lib, "nut_batch_set_prefill_threshold", [_P, _I64])
         _declare(lib, "nut_batch_open_peers", [_P, _P, _I64])
         _declare(lib, "nut_batch_stream", [_P, C.POINTER(_P)])
+        _declare(lib, "nut_peer_all_reduce", [_P, _P, _I64, _P, _P, C.c_int, C.c_int, _P, _P,
+                                              _I64, _P])
         _declare(lib, "nut_batch_generate", [_P, _P, _I64, _I64, _P, _P,
                                              C.POINTER(GenerationStats)])
         _cuda = lib
@@ -606,6 +608,20 @@ def tp_shard(config: Config, rank: int, world: int) -> dict:
     _check(cuda_lib().nut_tp_shard(C.byref(config), rank, world, v))
     keys = ("head0", "heads", "kv0", "kv_heads", "ffn0", "ffn", "vocab0", "vocab_rows")
     return dict(zip(keys, [int(x) for x in v]))
+
+
+PEER_AR_CHUNKS = 128
+
+
+def peer_all_reduce(x: int, out: int, n: int, recv: Sequence[int], flags: Sequence[int],
+                    rank: int, world: int, epochs: int, error: int, limit_ns: int,
+                    stream: int = 0) -> None:
+    """nut_peer_all_reduce on device pointers (ints): raises DeviceTimeout if
+    a wait for a peer's chunk gave up after limit_ns."""
+    r = (C.c_void_p * world)(*recv)
+    f = (C.c_void_p * world)(*flags)
+    _check(cuda_lib().nut_peer_all_reduce(x, out, n, r, f, rank, world, epochs, error,
+                                          int(limit_ns), stream or None))
 
 
 def tp_unique_id() -> bytes:

@@ -1029,4 +1029,40 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
     });
 }
 
+static_assert(nut::kArChunks == NUT_PEER_AR_CHUNKS, "flag layout of the C ABI");
+
+/* One peer-memory all-reduce on caller-owned buffers (see the header). */
+nut_status nut_peer_all_reduce(const float *x, float *out, int64_t n, float *const *recv,
+                               unsigned *const *flags, int rank, int world, unsigned *epochs,
+                               int *error, int64_t limit_ns, void *stream) {
+    return guarded([&] {
+        if (x == nullptr || out == nullptr || recv == nullptr || flags == nullptr ||
+            epochs == nullptr || error == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "peer all-reduce: null pointer");
+        if (world < 1 || world > 8 || rank < 0 || rank >= world)
+            raise(NUT_INVALID_ARGUMENT, "peer all-reduce: invalid rank or world");
+        if (n <= 0 || n % 4 != 0 || n > (int64_t(1) << 28) || limit_ns <= 0)
+            raise(NUT_INVALID_ARGUMENT, "peer all-reduce: invalid size or limit");
+        auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+        if (!a16(x) || !a16(out))
+            raise(NUT_INVALID_ARGUMENT, "peer all-reduce: buffers must be 16-byte aligned");
+        for (int q = 0; q < world; q++)
+            if (recv[q] == nullptr || flags[q] == nullptr || !a16(recv[q]))
+                raise(NUT_INVALID_ARGUMENT, "peer all-reduce: invalid receive area");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cuda_check(nut::peer_all_reduce(x, out, int(n), recv, flags, rank, world, epochs, error,
+                                        uint64_t(limit_ns), s),
+                   "peer all-reduce");
+        int code = 0;
+        cuda_check(cudaMemcpyAsync(&code, error, sizeof code, cudaMemcpyDeviceToHost, s),
+                   "read error word");
+        cuda_check(cudaStreamSynchronize(s), "peer all-reduce");
+        if (code != 0) {
+            cuda_check(cudaMemsetAsync(error, 0, sizeof(int), s), "clear error word");
+            cuda_check(cudaStreamSynchronize(s), "clear error word");
+            raise(NUT_DEVICE_TIMEOUT, "peer all-reduce: a wait for a peer's chunk gave up");
+        }
+    });
+}
+
 } // extern "C"

@@ -14,6 +14,11 @@ tiny_int8_golden.npz  the reference token loop on the seeded tiny INT8 model:
                    prompt, 16 greedy ids, their logits, the prefill hidden.
 tinyllama_int4_golden.npz  the same loop at TinyLlama shape (INT4): ids and
                    the top-8 logits of every step.
+tinyllama_int8_long_golden.npz  BASELINE config 3 at its stated size:
+                   TinyLlama shape INT8, a 512-token prompt and 256 greedy
+                   steps (KV cache at 768 positions): ids, the top-16 logits
+                   of every step and the whole logit rows of five steps.
+                   Written alone by `python tests/golden/make_golden.py long`.
 """
 import os
 import sys
@@ -102,5 +107,31 @@ def main():
     print("golden vectors written to", OUT)
 
 
+LONG_FULL_STEPS = (0, 64, 128, 192, 255)
+
+
+def long_golden(ref=None):
+    """BASELINE config 3 through the reference's own loop (all host threads):
+    prefill_quantized of 512 tokens, then 256 greedy steps."""
+    ref = ref or oracle.Reference()
+    wl = syn.WORKLOADS["tinyllama-int8-long"]
+    c = wl.model_config()
+    rm = ref.model(c, wl.qtype, SEED)
+    prompt = syn.prompt_ids(c, SEED, wl.prompt)
+    ids, logits, hidden, _, _ = rm.generate(prompt, wl.steps, threads=os.cpu_count())
+    top = np.argsort(-logits, axis=1, kind="stable")[:, :16]
+    np.savez_compressed(os.path.join(OUT, "tinyllama_int8_long_golden.npz"), prompt=prompt,
+                        ids=ids, top_ids=top.astype(np.int32),
+                        top_logits=np.take_along_axis(logits, top, axis=1),
+                        full_steps=np.array(LONG_FULL_STEPS, np.int32),
+                        full_logits=logits[list(LONG_FULL_STEPS)],
+                        prefill_hidden=hidden)
+    print("long golden written to", OUT)
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "long":
+        long_golden()
+    else:
+        main()
+        long_golden()

@@ -173,6 +173,38 @@ def test_batched_step_matches_oracle(gpu, orc, name, qtype, cfg):
 
 
 @pytest.mark.gpu
+@pytest.mark.slow
+def test_batched_step_7b_shape_batch64(gpu, orc):
+    """BASELINE config 5's layer shape on one GPU: dim 4096, 32/32 heads of
+    128, FFN 11008, vocabulary 32000, two layers (to bound the oracle's
+    time), 64 sequences of 128-token prompts (the GEMM prefill in 2048-row
+    chunks) and 8 greedy steps, with the split-K and two-CTAs-per-SM GEMM
+    choices those shapes select.  Four sequences spread over the batch are
+    checked against the oracle, teacher-forced with the device's ids."""
+    cfg = _cfg(layers=2, heads=32, dim=4096, head_dim=128, ffn_dim=11008, vocab_size=32000,
+               max_seq=256, kv_heads=32)
+    w = syn.build_model(cfg, 1, 2024)
+    B, n, steps = 64, 128, 8
+    prompts = np.stack([syn.prompt_ids(cfg, 3000 + b, n) for b in range(B)])
+    tp = nb.TPBatch(B, weights=w)
+    ids, logits, st = tp.generate(prompts, steps, want_logits=True)
+    tp.close()
+    assert st.generated_tokens == B * steps and st.prefill_tokens == B * n
+    for b in range(B):  # the chosen ids are the first-index argmax of the logits
+        assert ids[b].tolist() == [int(np.argmax(logits[k, b])) for k in range(steps)]
+    dev = []
+    for b in (0, 21, 42, 63):
+        want = _forced_oracle_logits(orc, w, prompts[b], ids[b])
+        d = np.abs(logits[:, b, :] - want)
+        assert np.all(d <= ATOL + RTOL * np.abs(want)), (b, float(d.max()))
+        dev.append(d)
+    med = float(np.median(np.concatenate(dev)))
+    print(f"7B shape, batch 64: max abs {max(float(d.max()) for d in dev):.3e}, "
+          f"median {med:.3e}")
+    assert med <= MEDIAN
+
+
+@pytest.mark.gpu
 def test_batched_errors(gpu):
     cfg = _cfg()
     w = syn.build_model(cfg, 1, 3)
@@ -267,3 +299,48 @@ def test_gemm_prefill_matches_oracle(gpu, orc, qtype):
     assert float(np.median(np.concatenate(dev))) <= MEDIAN
     assert np.allclose(logits, logits_pp, rtol=1e-3, atol=1e-4)
     assert ids.tolist() == ids_pp.tolist()
+
+
+@pytest.mark.gpu
+def test_bounded_peer_wait_times_out_and_device_stays_usable(gpu):
+    """Failure detection without a GPU fault: a world-2 peer all-reduce on
+    one GPU whose 'peer' never raises its flags (both receive areas are
+    local buffers nobody else writes).  Every wait gives up after 2 ms, the
+    call returns DeviceTimeout, and the next calls on the same device work."""
+    import time
+    import torch
+    dev = torch.device("cuda", gpu)
+    torch.cuda.set_device(dev)
+    n, world = 4096, 2
+    ch = nb.PEER_AR_CHUNKS
+    x = torch.randn(n, device=dev)
+    out = torch.zeros(n, device=dev)
+    recv = [torch.zeros(2 * world * n, device=dev) for _ in range(world)]
+    flags = [torch.zeros(world * ch, dtype=torch.int32, device=dev) for _ in range(world)]
+    epochs = torch.zeros(ch, dtype=torch.int32, device=dev)
+    error = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    with pytest.raises(nb.DeviceTimeout, match="gave up"):
+        nb.peer_all_reduce(x.data_ptr(), out.data_ptr(), n, [r.data_ptr() for r in recv],
+                           [f.data_ptr() for f in flags], 0, world, epochs.data_ptr(),
+                           error.data_ptr(), 2_000_000, stream)
+    assert time.perf_counter() - t0 < 5.0
+    assert int(error.cpu()[0]) == 0  # cleared for the next call
+    # rank 0 raised its own flags on both areas before waiting
+    assert int(flags[0].cpu()[:ch].min()) == 1 and int(flags[1].cpu()[:ch].min()) == 1
+    # the device is still usable: a one-rank call sums to x, and a decode runs
+    r1 = torch.zeros(2 * n, device=dev)
+    f1 = torch.zeros(ch, dtype=torch.int32, device=dev)
+    e1 = torch.zeros(ch, dtype=torch.int32, device=dev)
+    nb.peer_all_reduce(x.data_ptr(), out.data_ptr(), n, [r1.data_ptr()], [f1.data_ptr()], 0, 1,
+                       e1.data_ptr(), error.data_ptr(), 2_000_000, stream)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(out, x)
+    wl = syn.WORKLOADS["tiny-int8"]
+    w = syn.build_model(wl.model_config(), wl.qtype, 5)
+    model = nb.DeviceModel(w, gpu)
+    kv = nb.KVCache(model)
+    ids, _, _ = nb.generate_greedy(model, kv, [1, 2, 3], 2, stop_at_eos=False)
+    assert len(ids) == 2
