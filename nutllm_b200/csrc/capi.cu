@@ -625,21 +625,24 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
     unsigned long long *trace = nullptr;
     const int stride = int(n_tokens * (3 * c.layers + 1));
     if (trace_file != nullptr) {
-        trace = dev_alloc<unsigned long long>(size_t(m->sms) * stride * 8, "alloc trace");
-        cuda_check(cudaMemsetAsync(trace, 0, size_t(m->sms) * stride * 64, s), "clear trace");
+        trace = dev_alloc<unsigned long long>(size_t(m->sms) * stride * nut::kTraceWords,
+                                              "alloc trace");
+        cuda_check(cudaMemsetAsync(trace, 0, size_t(m->sms) * stride * nut::kTraceWords * 8, s),
+                   "clear trace");
         p.trace = trace;
         p.trace_stride = stride;
     }
     cuda_check(nut::launch_decode_mk(p, m->type, m->sms, s), "persistent kernel launch");
     if (trace != nullptr) {
-        std::vector<unsigned long long> host(size_t(m->sms) * stride * 8);
+        std::vector<unsigned long long> host(size_t(m->sms) * stride * nut::kTraceWords);
         cuda_check(cudaMemcpyAsync(host.data(), trace, host.size() * 8, cudaMemcpyDeviceToHost,
                                    s),
                    "copy trace");
         cuda_check(cudaStreamSynchronize(s), "synchronize");
         dev_free(trace);
         if (FILE *f = std::fopen(trace_file, "ab")) {
-            const int32_t hdr[4] = {m->sms, stride, int32_t(n_tokens), int32_t(c.layers)};
+            const int32_t hdr[4] = {m->sms, stride, int32_t(n_tokens),
+                                    int32_t(c.layers) | (nut::kTraceWords << 16)};
             std::fwrite(hdr, sizeof hdr, 1, f);
             std::fwrite(host.data(), 8, host.size(), f);
             std::fclose(f);

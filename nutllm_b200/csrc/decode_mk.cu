@@ -137,16 +137,19 @@ struct Shared {
     float *actv;       /* [kMaxFfnBlocks * 32] SwiGLU outputs of owned blocks */
 };
 
-/* Optional phase trace (thread 0 of each CTA): one record of 8 words per
- * phase occurrence: phase id, the global timer at entry (1), and SM clock
- * stamps at entry (6), inputs staged (2), activation ready (3), digits
- * ready (4), weights consumed (5) and exit (7). */
+/* Optional phase trace (thread 0 of each CTA): one record of kTraceWords
+ * words per phase occurrence: phase id, the global timer at entry (1), and
+ * SM clock stamps at entry (6), inputs staged (2), activation ready (3),
+ * digits ready (4), weights consumed (5) and exit (7); sub-steps: the
+ * finish's red.adds issued (8) and its fence passed (9), the exported and
+ * the other gate/up tiles consumed (10, 11), the SwiGLU outputs complete
+ * (12), and the key/value fence passed (13). */
 struct Trace {
     unsigned long long *rec = nullptr;
     __device__ __forceinline__ void open(const MkParams &p, int occ, int id) {
         waited = 0;
         rec = p.trace != nullptr && occ < p.trace_stride
-                  ? p.trace + (size_t(blockIdx.x) * p.trace_stride + occ) * 8
+                  ? p.trace + (size_t(blockIdx.x) * p.trace_stride + occ) * kTraceWords
                   : nullptr;
         if (rec != nullptr && threadIdx.x == 0) {
             rec[0] = unsigned(id);
@@ -154,7 +157,7 @@ struct Trace {
             rec[6] = clock64();
         }
     }
-    /* slots 2-5 and 7: SM clock (cycles) */
+    /* slots 2-5 and 7-15: SM clock (cycles) */
     __device__ __forceinline__ void mark(int slot) const {
         if (rec != nullptr && threadIdx.x == 0)
             rec[slot] = clock64();
@@ -302,7 +305,7 @@ __device__ __forceinline__ void red_add4(float *dst, float4 v) {
  * cumulative, so one fence ahead of the counter increment publishes them
  * all to any reader that acquires the counter. */
 __device__ void finish_step(const Shared &s, const MkParams &p, int step, int row0, int nrows,
-                            int me, int count) {
+                            int me, int count, const Trace &tr) {
     cbar();
     float *dst = slot_of(p, step) + row0;
     const float4 *y4 = reinterpret_cast<const float4 *>(s.yacc);
@@ -314,8 +317,10 @@ __device__ void finish_step(const Shared &s, const MkParams &p, int step, int ro
     for (int k = z0 + int(threadIdx.x); k < z1; k += NT)
         next[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     cbar();
+    tr.mark(8);
     if (threadIdx.x == 0) {
         __threadfence();
+        tr.mark(9);
         atomicAdd(p.cnt + step % kAccSlots, 1u);
     }
 }
@@ -530,9 +535,10 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor 
     const bool ok = consume_run<TYPE, W, STAGES>(s.ring, run, cur, s.dig, s.fac, rr,
                                                  threadIdx.x >> 5, kBar, epi,
                                                  tr.wait_acc());
+    tr.mark(5);
     if (wrote_kv)
         __threadfence();
-    tr.mark(5);
+    tr.mark(13);
     tr.put_wait();
     return healthy(s) && ok;
 }
@@ -764,7 +770,7 @@ __device__ bool phase_attwo(const Shared &s, const MkParams &p, Trace &tr, Curso
         for (int r = int(threadIdx.x) + kResRegs * NT; r < nrows; r += NT)
             s.yacc[r] += __ldcg(res + r);
     }
-    finish_step(s, p, st, a * 16, nrows, c, p.count_aw);
+    finish_step(s, p, st, a * 16, nrows, c, p.count_aw, tr);
     return healthy(s) && ok;
 }
 
@@ -880,6 +886,7 @@ __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Curs
         ok = consume_run<TYPE, W, STAGES>(s.ring, ex, cur, s.dig, s.fac, rr, w, kBar, epi,
                                           tr.wait_acc());
     }
+    tr.mark(10);
     if (g.ex_lo > g.gu_lo) {
         t_first = g.gu_lo;
         const TileRun rest{L.gu + size_t(g.gu_lo) * p.nb_dim * TB,
@@ -889,7 +896,9 @@ __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Curs
                                           tr.wait_acc()) &&
              ok;
     }
+    tr.mark(11);
     cbar(); /* every SwiGLU output written; the gate/up digits are free */
+    tr.mark(12);
     if (w < g.nd) {
         /* digits of Wdown block db_lo + w; tiles before gu_lo come from
          * earlier CTAs through the tagged vector */
@@ -920,7 +929,7 @@ __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Curs
     }
     tr.mark(5);
     tr.put_wait();
-    finish_step(s, p, st, 0, p.dim, c, p.count_gd);
+    finish_step(s, p, st, 0, p.dim, c, p.count_gd, tr);
     return healthy(s) && ok;
 }
 

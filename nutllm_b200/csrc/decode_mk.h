@@ -42,6 +42,9 @@ struct MkLayerPtrs {
  * read as one 64-bit access. */
 using Tagged = uint2;
 
+/* Words per phase record of the optional trace. */
+constexpr int kTraceWords = 16;
+
 struct MkParams {
     int layers, dim, kvd, heads, kv_heads, hd, ffn, vocab, max_seq;
     int nb_dim, nb_ffn;                 /* padded blocks of K = dim / ffn */
@@ -73,7 +76,7 @@ struct MkParams {
     float *logits;                      /* [to - from + 1][vocab] or null */
     int *error;
     unsigned long long *stamps;         /* [3] start, prefill done, end (ns) */
-    unsigned long long *trace;          /* optional [ctas][trace_stride][8] */
+    unsigned long long *trace;          /* optional [ctas][trace_stride][kTraceWords] */
     int trace_stride;
     uint64_t limit_ns;
     int att_chunk;                      /* positions per attention chunk */
