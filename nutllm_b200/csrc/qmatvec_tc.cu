@@ -199,8 +199,16 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_ring_kernel(QTParams p) {
     constexpr int TB = G::kTileBytes;
     const TileRun run{p.tiles + size_t(rt0) * p.nb * TB,
                       p.scales + size_t(rt0) * p.nb * 16, (rt1 - rt0) * p.nb, p.nb};
+    /* launched with programmatic stream serialisation, the next kernel of
+     * the stream may start as soon as this one's CTAs leave their SMs;
+     * everything it reads before its own griddepcontrol.wait is constant */
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == kWarps) {
         if (lane == 0) {
+            /* x may be the previous kernel's output: wait for that grid
+             * (a no-op without a programmatic dependency) before reading
+             * it; the weights need no wait */
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             /* x first: its few bytes must not queue behind the weights */
             if (p.stage_x) {
                 mbar_expect_tx(s.xbar, uint32_t(p.K) * 4u);
@@ -221,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_ring_kernel(QTParams p) {
         }
         return;
     }
+    /* the previous grid (x's producer, y's last reader) has completed */
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (p.stage_x) {
         if (!mbar_wait(s.xbar, 0, p.limit_ns)) {
             report(p.error, kErrTimeoutInput);
@@ -246,6 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_ring_kernel(QTParams p) {
     named_barrier(1, kWarps * 32);
     /* floor(tile / nb) by a multiply-high: exact for tile * nb < 2^32 */
     const uint32_t inv_nb = uint32_t((0xffffffffull + uint64_t(p.nb)) / uint64_t(p.nb));
+    /* row tiles are whole stages: no stage straddles two row tiles */
+    const bool whole_stages = p.nb % G::kChunkTiles == 0;
     float *part_w = s.part + size_t(warp) * p.rows_cta;
     const int group = warp / kGroupWarps, gw = warp % kGroupWarps;
     int cur_rt = -1;
@@ -269,9 +281,20 @@ __global__ void __launch_bounds__(kThreads, 1) qmatvec_ring_kernel(QTParams p) {
             const uint16_t *ss = ring.scales + size_t(cur.stage) * (kStageScaleBytes / 2);
             float y[PP], y8[PP];
             int rt[PP];
-            if (n == G::kChunkTiles) {
-                /* a whole stage: no guards, so the pairs' loads and
-                 * products interleave */
+            if (n == G::kChunkTiles && whole_stages) {
+                /* a whole stage inside one row tile: its row tile and first
+                 * block are stage constants, so every load below is a base
+                 * plus an immediate, and without guards the pairs' loads
+                 * and products interleave */
+                const int r = int(__umulhi(uint32_t(t0), inv_nb));
+                const int kb = t0 - r * p.nb;
+#pragma unroll
+                for (int u = 0; u < PP; u++) {
+                    const int tl = 2 * (gw + u * kGroupWarps); /* tile within the stage */
+                    rt[u] = r;
+                    pair_sum<TYPE>(sd, ss, tl, kb + tl, s.dl, s.fl, y[u], y8[u]);
+                }
+            } else if (n == G::kChunkTiles) {
 #pragma unroll
                 for (int u = 0; u < PP; u++) {
                     const int tl = 2 * (gw + u * kGroupWarps); /* tile within the stage */
@@ -344,7 +367,17 @@ template <int TYPE, int ST>
 void go(const QTParams &p, int grid, size_t smem, cudaStream_t stream) {
     auto kernel = qmatvec_ring_kernel<TYPE, ST>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    kernel<<<grid, kThreads, smem, stream>>>(p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, p);
     nut::count_launches(1);
 }
 
