@@ -130,6 +130,7 @@ struct Shared {
     float *fac;
     float *uni;        /* ... or attention scratch */
     float *red;        /* [2][kRowBatch][W][16] */
+    float *part;       /* [2][W][kParkTiles][16] row-tile parks of the grouped path */
     float *wsum;       /* [W] */
     unsigned long long *bestk; /* [W] */
     int *flag;         /* [0] fatal, [1] token */
@@ -194,6 +195,8 @@ __device__ Shared carve(uint8_t *base, const MkParams &p) {
     auto align16 = [](size_t o) { return (o + 15) & ~size_t(15); };
     s.red = reinterpret_cast<float *>(base + off);
     off = align16(off + 2 * kRowBatch * W * 16 * 4);
+    s.part = reinterpret_cast<float *>(base + off);
+    off = align16(off + size_t(2) * W * kParkTiles * 16 * 4);
     s.wsum = reinterpret_cast<float *>(base + off);
     off = align16(off + W * 4);
     s.bestk = reinterpret_cast<unsigned long long *>(base + off);
@@ -492,11 +495,15 @@ __device__ bool phase_qkv(const Shared &s, const MkParams &p, Trace &tr, Cursor 
         rope_cs[threadIdx.x] = rc;
         rope_sn[threadIdx.x] = rsn;
     }
-    tr.mark(2);
     constexpr int TB = TileGeom<TYPE>::kTileBytes;
     const MkLayerPtrs &L = p.layer[l];
     const TileRun run{L.qkv + size_t(a) * p.nb_dim * TB, L.qkv_s + size_t(a) * p.nb_dim * 16,
                       (b - a) * p.nb_dim, p.nb_dim};
+    /* the grouped consume path gives warp w the pairs of warps w and w ^ 4
+     * (W / 2 = 4): each digitised half of them */
+    if (grouped_run<TYPE>(run))
+        named_barrier(2 + ((threadIdx.x >> 5) & 3), 64);
+    tr.mark(2);
     const uint32_t tag = qkv_tag(p, i, l);
     const int lane = threadIdx.x & 31;
     const float *cs = rope_cs, *sn = rope_sn;
@@ -1133,7 +1140,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_mk_kernel(const MkParams p)
     }
     if (blockIdx.x == 0 && threadIdx.x == 0)
         p.stamps[0] = global_ns();
-    RowReduce rr{s.red, 0};
+    RowReduce rr{s.red, 0, s.part, 0};
     Cursor cur;
     int occ = 0;
     bool alive = true;
@@ -1196,6 +1203,7 @@ size_t fixed_smem(int stages, int dim, int ffn) {
 size_t tail_smem(int stages, int dim) {
     auto align16 = [](size_t o) { return (o + 15) & ~size_t(15); };
     size_t off = align16(2 * kRowBatch * W * 16 * 4);
+    off = align16(off + size_t(2) * W * kParkTiles * 16 * 4);
     off = align16(off + W * 4);
     off = align16(off + W * 8);
     off = align16(off + 16);

@@ -56,6 +56,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
                  : "memory");
 }
 
+/* Arrival that counts `count` times (one warp standing in for several). */
+__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(count)
+                 : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -331,11 +338,24 @@ __device__ __forceinline__ void pair_mma(const uint8_t *stage_data,
  * tile. */
 constexpr int kRowBatch = 4;
 
-/* Per-CTA reduction buffer for row-tile results. */
+/* Row tiles parked per chunk by the grouped consume path. */
+constexpr int kParkTiles = 16;
+
+/* Per-CTA reduction buffers for row-tile results. */
 struct RowReduce {
-    float *red; /* [2][kRowBatch][warps][16] */
+    float *red;  /* [2][kRowBatch][warps][16] (general path) */
     int buf;
+    float *part; /* [2][warps][kParkTiles][16] (grouped path), or null */
+    int pbuf;    /* half of `part` the next grouped run uses */
 };
+
+/* Runs that consume_run hands to the grouped path (when it has a park
+ * buffer): row tiles of whole stages. */
+template <int TYPE>
+__device__ __forceinline__ bool grouped_run(const TileRun &run) {
+    constexpr int CT = TileGeom<TYPE>::kChunkTiles;
+    return run.nb % CT == 0 && run.tiles % run.nb == 0;
+}
 
 /* Stage cursor: the CTA-wide count of consumed stages, kept as (index,
  * parity) so no division is needed. */
@@ -394,6 +414,147 @@ __device__ __forceinline__ void flush_rows(float (&sg)[kRowBatch], float (&sg8)[
     rr.buf ^= 1;
 }
 
+/* Products of one pair of tiles (tiles `tile`, `tile` + 1 of the stage,
+ * blocks b0, b0 + 1) as pair_mma computes them, with the two mma's chained
+ * into one accumulator: the first product's B carries block b0's digits
+ * only in columns 0-3 and the second's block b0 + 1's only in columns 4-7,
+ * so D = A1 B1 + (A0 B0 + seed) holds exactly pair_mma's column sums and
+ * every lane reads its two digit sums from one result.  Writes (does not
+ * add) the lane's partial sums for rows g and g + 8. */
+template <int TYPE>
+__device__ __forceinline__ void pair_chain(const uint8_t *stage_data,
+                                           const uint16_t *stage_scales, int tile,
+                                           int b0, const int8_t *dig,
+                                           const float *fac, float &yg, float &yg8) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    uint32_t a0[4], a1[4];
+    load_a<TYPE>(stage_data, tile, a0);
+    load_a<TYPE>(stage_data, tile + 1, a1);
+    const int slot = g >> 2, half = c >> 1;
+    const int8_t *src = dig + (b0 + slot) * 128 + (g & 3) * 32 + 4 * c;
+    const uint32_t bx0 = *reinterpret_cast<const uint32_t *>(src);
+    const uint32_t bx1 = *reinterpret_cast<const uint32_t *>(src + 16);
+    const uint32_t m = slot == 0 ? 0xffffffffu : 0u;
+    int d[4];
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0[0]), "r"(a0[1]), "r"(a0[2]), "r"(a0[3]), "r"(bx0 & m), "r"(bx1 & m),
+          "r"(kMagic));
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a1[0]), "r"(a1[1]), "r"(a1[2]), "r"(a1[3]), "r"(bx0 & ~m), "r"(bx1 & ~m));
+    const float f0 = __int_as_float(d[0]) - kMagicF, f1 = __int_as_float(d[1]) - kMagicF;
+    const float f2 = __int_as_float(d[2]) - kMagicF, f3 = __int_as_float(d[3]) - kMagicF;
+    const float tg = fmaf(f0, 128.0f, f1), tg8 = fmaf(f2, 128.0f, f3);
+    const float F = fac[2 * (b0 + half) + (c & 1)];
+    const uint16_t *sc = stage_scales + (tile + half) * 16;
+    yg = tg * (half_bits_to_float(sc[g]) * F);
+    yg8 = tg8 * (half_bits_to_float(sc[g + 8]) * F);
+}
+
+/* consume_run for runs whose row tiles are whole stages (nb a multiple of
+ * a stage's tiles), when rr.part is given.  The WARPS consumer warps form
+ * two groups of WARPS / 2: group q takes the run's stages q, q + 2, ..., so
+ * one group's per-stage tail overlaps the other's products, and warp gw of
+ * a group multiplies the stage's pairs gw, gw + WARPS / 2, ... (block pairs
+ * congruent to gw modulo WARPS / 2: a warp needs the digits of its own
+ * pairs and of warp gw + WARPS / 2's, which callers make visible) into
+ * independent accumulators.  Each warp parks its sum of every row tile in
+ * its own slots of rr.part (shuffles over the four lanes of a row group,
+ * then one add per row), in stage order; after every kParkTiles row tiles
+ * (and at the end) one barrier, then warp k finishes row tiles k, k +
+ * WARPS, ... of the chunk: y = the warps' parks added in warp order (a fixed
+ * order), epi(rt, y) with y on lanes 0..15, as in flush_rows. */
+template <int TYPE, int WARPS, int STAGES, typename Epi>
+__device__ bool consume_rows_grouped(const Ring &ring, const TileRun &run, Cursor &cur,
+                                     const int8_t *dig, const float *fac, float *part, int w,
+                                     int barrier_id, Epi &epi, long long *wait_cycles) {
+    using G = TileGeom<TYPE>;
+    constexpr int GW = WARPS / 2;               /* warps per group */
+    static_assert(WARPS == 2 * GW, "two groups of equal size");
+    constexpr int PP = G::kChunkTiles / 2 / GW; /* pairs per warp per stage */
+    static_assert(PP * 2 * GW == G::kChunkTiles, "stage split");
+    const int group = w / GW, gw = w % GW;
+    const int lane = threadIdx.x & 31;
+    const int spr = run.nb / G::kChunkTiles; /* stages per row tile */
+    const int nrt = run.tiles / run.nb;
+    float *mine = part + size_t(w) * kParkTiles * 16;
+    bool poisoned = false;
+    for (int c0 = 0; c0 < nrt; c0 += kParkTiles) {
+        const int c1 = min(nrt, c0 + kParkTiles);
+        if (lane < 16)
+            for (int r = 0; r < c1 - c0; r++)
+                mine[r * 16 + lane] = 0.0f;
+        __syncwarp();
+        for (int j = c0 * spr + group; j < c1 * spr; j += 2) {
+            const int idx = cur.stage + j;
+            const int stage = idx % STAGES;
+            const uint32_t parity = cur.parity ^ (uint32_t(idx / STAGES) & 1u);
+            if (!poisoned)
+                poisoned = *reinterpret_cast<volatile int *>(ring.fatal) != 0;
+            const long long w0 = wait_cycles != nullptr ? clock64() : 0;
+            if (!poisoned && !mbar_wait(&ring.full[stage], parity, ring.limit_ns)) {
+                report(ring.error, kErrTimeoutFull);
+                *reinterpret_cast<volatile int *>(ring.fatal) = 1;
+                poisoned = true;
+            }
+            if (wait_cycles != nullptr)
+                *wait_cycles += clock64() - w0;
+            if (!poisoned) {
+                const uint8_t *sd = ring.data + size_t(stage) * kStageBytes;
+                const uint16_t *ss = ring.scales + size_t(stage) * (kStageScaleBytes / 2);
+                const int kb = (j % spr) * G::kChunkTiles; /* first block of the stage */
+                float y[PP], y8[PP];
+#pragma unroll
+                for (int u = 0; u < PP; u++) {
+                    const int tl = 2 * (gw + u * GW);
+                    pair_chain<TYPE>(sd, ss, tl, kb + tl, dig, fac, y[u], y8[u]);
+                }
+                float t = y[0], t8 = y8[0];
+#pragma unroll
+                for (int u = 1; u < PP; u++) {
+                    t += y[u];
+                    t8 += y8[u];
+                }
+                t += __shfl_xor_sync(0xffffffffu, t, 1);
+                t8 += __shfl_xor_sync(0xffffffffu, t8, 1);
+                t += __shfl_xor_sync(0xffffffffu, t, 2);
+                t8 += __shfl_xor_sync(0xffffffffu, t8, 2);
+                if ((lane & 3) == 0) {
+                    const int r = j / spr - c0, g = lane >> 2;
+                    mine[r * 16 + g] += t;
+                    mine[r * 16 + g + 8] += t8;
+                }
+            }
+            __syncwarp();
+            /* the ring's stages expect WARPS arrivals: each of the group's
+             * WARPS / 2 warps counts twice */
+            if (lane == 0 && !poisoned)
+                mbar_arrive_n(&ring.empty[stage], 2);
+        }
+        named_barrier(barrier_id, WARPS * 32); /* every park of the chunk written */
+        for (int r = w; r < c1 - c0; r += WARPS) {
+            float v = 0.0f;
+            if (lane < 16) {
+#pragma unroll
+                for (int q = 0; q < WARPS; q++)
+                    v += part[(size_t(q) * kParkTiles + r) * 16 + lane];
+            }
+            epi(c0 + r, v);
+        }
+        if (c1 < nrt)
+            named_barrier(barrier_id, WARPS * 32); /* parks free for the next chunk */
+    }
+    /* every consumer passes the run's stages */
+    const int nst = nrt * spr;
+    const int idx = cur.stage + nst;
+    cur.parity ^= uint32_t(idx / STAGES) & 1u;
+    cur.stage = idx % STAGES;
+    return !poisoned;
+}
+
 /* Consumes one run of row tiles with WARPS consumer warps (w = this warp).
  * Every finished row tile `rt` (index within the run) reaches epi(rt, y)
  * on one warp, lanes 0..15 holding y for rows 16 rt + lane (other lanes
@@ -405,6 +566,17 @@ __device__ bool consume_run(const Ring &ring, const TileRun &run, Cursor &cur,
                             int w, int barrier_id, Epi &&epi,
                             long long *wait_cycles = nullptr) {
     using G = TileGeom<TYPE>;
+    if constexpr (WARPS % 2 == 0 && (G::kChunkTiles / 2) % (WARPS / 2) == 0) {
+        if (rr.part != nullptr && grouped_run<TYPE>(run)) {
+            /* consecutive runs alternate halves: a warp may zero its slots
+             * for run n + 1 while a slower warp still reads run n's (it
+             * cannot reach run n + 2 before run n + 1's barrier) */
+            float *half = rr.part + size_t(rr.pbuf) * WARPS * kParkTiles * 16;
+            rr.pbuf ^= 1;
+            return consume_rows_grouped<TYPE, WARPS, STAGES>(ring, run, cur, dig, fac, half, w,
+                                                             barrier_id, epi, wait_cycles);
+        }
+    }
     const int lane = threadIdx.x & 31;
     float ya = 0.0f, ya8 = 0.0f, yb = 0.0f, yb8 = 0.0f;
     float sg[kRowBatch], sg8[kRowBatch];
