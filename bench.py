@@ -10,8 +10,9 @@ whole loop on the device.
             HBM (each generation timed with CUDA events on the library's
             stream; the prefill/decode split inside the one launch from the
             kernel's device-timer stamps)
-  e2e       generated tok/s through the C ABI call a user makes
-            (nut_generate_greedy: prompt from host memory in, ids out)
+  e2e       decode tok/s through the C ABI call a user makes
+            (nut_generate_greedy: prompt from host memory in, ids out; wall
+            clock less the in-kernel prefill time)
   roofline  the dominant kernel (the persistent token loop, one launch per
             generation) against the measured HBM copy bandwidth
   qmatvec   microbenchmark (a): the quantised matvec at the BASELINE shapes
@@ -20,9 +21,14 @@ whole loop on the device.
   cpu_baseline  the reference's own CPU token loop (oracle/_ref) on this
             host, all threads, on the whole workload once
 
+  tp        BASELINE config 5 beside it: the Llama-2-7B shape, 64 sequences,
+            tensor-parallel over the run's N ranks (NCCL all-reduce after
+            Wo and Wdown), a few generations (--no-tp skips it)
+
 `--impl reference` times the reference CPU implementation instead.
 Multi-GPU: batch-1 decode of a model that fits one GPU does not shard;
-`--gpus N` runs N independent replicas (weak scaling, no collective).
+`--gpus N` runs N independent replicas (weak scaling, no collective) as
+`value`, and the tensor-parallel 7B path over the same N ranks as `tp`.
 """
 from __future__ import annotations
 
@@ -93,6 +99,8 @@ def parse():
                    help="run only the kernel microbenchmarks (one JSON line)")
     p.add_argument("--micro-shape", default=None,
                    help="restrict the microbenchmarks to one ROWSxCOLS weight shape")
+    p.add_argument("--no-tp", action="store_true",
+                   help="skip the tensor-parallel 7B side measurement of the default line")
     return p.parse_args()
 
 
@@ -229,6 +237,7 @@ def run_ours(args, rank, world, local):
 
     value = wl.steps * args.steps * world / dec_s
     prefill_tps = wl.prompt * args.steps * world / pre_s
+    tp = None if args.no_tp else tp_side(rank, world, local)
     e2e = wl.steps * args.steps * world / (wall - pre_s)
     e2e_gen = wl.steps * args.steps * world / wall
 
@@ -289,6 +298,7 @@ def run_ours(args, rank, world, local):
         "fp32": fp32,
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
+        "tp": tp,
     }
     print(json.dumps(line), flush=True)
 
@@ -355,6 +365,58 @@ def cpu_reference_7b(spec, samples=1, warmup=1, n_prompt=4, n_steps=4):
     sample = (f"batch 1, all {cfg.layers} layers: {n_prompt}-token prompt + {n_steps} greedy "
               f"steps per sample, {samples} samples, reference kernels, {threads} threads")
     return n_steps * samples / dec, n_prompt * samples / pre, threads, sample
+
+
+def tp_side(rank, world, local, steps=3, warmup=3, workload="llama7b-int4-b64"):
+    """BASELINE config 5 (Llama-2-7B shape, INT4, 64 sequences, 128-token
+    prompts, 128 greedy steps) tensor-parallel over this run's `world` ranks
+    (one per GPU, NCCL all-reduce after Wo and after Wdown), measured beside
+    the default line so that every bench line, the driver's scaling run
+    included, records the tensor-parallel path at its N.  Every rank takes
+    part; returns rank 0's summary (None elsewhere)."""
+    import torch
+    import nutllm_b200 as nb
+    spec = TP_WORKLOADS[workload]
+    cfg = nb.Config(**spec["cfg"])
+    B, n, nsteps = spec["batch"], spec["prompt"], spec["steps"]
+    torch.cuda.set_device(local)
+    nccl_id = None
+    if world > 1:
+        box = [nb.tp_unique_id() if rank == 0 else None]
+        _pg.broadcast_object_list(box, src=0)
+        nccl_id = box[0]
+    tp = nb.TPBatch(B, rank=rank, world=world, nccl_id=nccl_id, config=cfg, seed=SEED,
+                    device=local)
+    rng = np.random.default_rng(SEED)
+    prompts = rng.integers(1, cfg.vocab_size, size=(B, n)).astype(np.int32)
+    for _ in range(warmup):
+        tp.generate(prompts, nsteps)
+    barrier = _barrier(world)
+    barrier()
+    torch.cuda.synchronize(local)
+    dec_s = pre_s = 0.0
+    for _ in range(steps):
+        _, _, st = tp.generate(prompts, nsteps)
+        dec_s += st.decode_seconds
+        pre_s += st.prefill_seconds
+    barrier()
+    tp.close()
+    dec_s = _max_over_ranks(dec_s, world)
+    pre_s = _max_over_ranks(pre_s, world)
+    if rank != 0:
+        return None
+    per_rank = tp_decode_bytes(spec["cfg"], B, n, nsteps, world)
+    step_s = dec_s / (steps * nsteps)
+    peak, _ = measured_peaks()
+    return {"metric": f"decode tok/s (Llama-2-7B INT4 shape, batch {B}, tensor parallel)",
+            "value": round(B * nsteps * steps / dec_s, 2), "unit": "tok/s",
+            "config": tp_config_of(workload, spec, world), "all_reduce": "nccl",
+            "steps": steps, "warmup": warmup,
+            "ms_per_decode_step": round(step_s * 1e3, 4),
+            "prefill_tok_s": round(B * n * steps / pre_s, 2),
+            "roofline_frac_per_rank": round(per_rank / step_s / 1e9 / peak, 4),
+            "timing": "CUDA events on the library stream around prefill and decode, "
+                      "max over ranks"}
 
 
 def run_batch_tp(args, rank, world, local):
