@@ -166,6 +166,22 @@ nut_status nut_matvec_f32(const float *matrix, const float *vector, float *outpu
 nut_status nut_model_create_f32(const nut_model_f32_view *view, int device, nut_model **out);
 nut_status nut_model_create(const nut_model_view *view, int device,
                             nut_model **out);
+/* The same model built in steps, so a loader can overlap reading and
+ * quantising layer l + 1 on the host with the upload of layer l:
+ * nut_model_begin takes a view whose `layers` may be NULL (the fp32
+ * tensors and the configuration are uploaded and checked), then
+ * nut_model_add_layer appends layers 0, 1, ... in order (each packed into
+ * tiles and copied to the device before it returns; the host buffers may be
+ * reused afterwards), and nut_model_finish completes the model once
+ * config.layers layers were added.  A model cannot back a KV cache before
+ * it is finished; nut_model_destroy releases it at any step.  nut_model_add_layer
+ * may be called from another host thread than nut_model_begin, one call at
+ * a time.  Same checks, classes and messages as nut_model_create
+ * (reference QuantizedModelWeights construction, include/quant_model.hpp:
+ * 31-53, with src/quant_model.cpp:158-172's layer-count check). */
+nut_status nut_model_begin(const nut_model_view *view, int device, nut_model **out);
+nut_status nut_model_add_layer(nut_model *model, const nut_layer_view *layer);
+nut_status nut_model_finish(nut_model *model);
 nut_status nut_model_destroy(nut_model *model);
 /* QuantizedModelWeights::storage_bytes (src/quant_model.cpp:140-156). */
 nut_status nut_model_storage_bytes(const nut_model *model, uint64_t *bytes);

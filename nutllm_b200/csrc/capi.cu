@@ -337,6 +337,11 @@ struct nut_model {
     };
     std::vector<F16Layer> f16w;
     int *gemm_error = nullptr;
+    /* creation in steps (nut_model_begin / add_layer / finish) */
+    bool building = false;
+    int64_t added = 0;
+    std::vector<nut::MkLayerPtrs> build_ptrs;
+    std::vector<float> build_an, build_fn;
     ~nut_model() {
         if (stream) {
             cudaStreamSynchronize(stream);
@@ -970,134 +975,188 @@ nut_status nut_qmatvec(nut_qmatrix *matrix, const float *x, float *y) {
     });
 }
 
+/* Model creation in three steps (nut_model_create runs all three): the
+ * fp32 tensors and the shape checks, then one layer at a time (its
+ * projections packed into tiles and uploaded), then the tables of the
+ * persistent kernel and the RoPE rows.  A loader can quantise layer l + 1
+ * on the host while layer l is added. */
+void model_begin(nut_model &mm, const nut_model_view *view, int device) {
+    if (view == nullptr)
+        raise(NUT_INVALID_ARGUMENT, "model: null argument");
+    const nut_config &c = view->config;
+    validate_config(c);
+    if (view->quant_type != NUT_QUANT_INT8 && view->quant_type != NUT_QUANT_INT4)
+        raise(NUT_INVALID_ARGUMENT, "model: unknown quant type");
+    if (view->embeddings == nullptr || view->final_norm == nullptr ||
+        (!view->tied_embeddings && view->lm_head == nullptr))
+        raise(NUT_INVALID_ARGUMENT, "model: null fp32 tensor");
+    nut_model *m = &mm;
+    m->device = device;
+    m->cfg = c;
+    m->kv_heads = c.kv_heads == 0 ? c.heads : c.kv_heads;
+    m->type = view->quant_type;
+    m->tied = view->tied_embeddings != 0;
+    cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "create stream");
+    const size_t dim = size_t(c.dim), V = size_t(c.vocab_size);
+    const int64_t kvd = m->kv_heads * c.head_dim;
+    m->storage_bytes = (V * dim + dim + (m->tied ? 0 : V * dim)) * 4;
+    m->embeddings = dev_alloc<float>(V * dim, "alloc embeddings");
+    cuda_check(cudaMemcpy(m->embeddings, view->embeddings, V * dim * 4, cudaMemcpyHostToDevice),
+               "copy embeddings");
+    m->final_norm = dev_alloc<float>(dim, "alloc final norm");
+    cuda_check(cudaMemcpy(m->final_norm, view->final_norm, dim * 4, cudaMemcpyHostToDevice),
+               "copy final norm");
+    if (!m->tied) {
+        m->lm_head = dev_alloc<float>(V * dim, "alloc lm_head");
+        cuda_check(cudaMemcpy(m->lm_head, view->lm_head, V * dim * 4, cudaMemcpyHostToDevice),
+                   "copy lm_head");
+    }
+    int max_smem = 0;
+    cuda_check(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device),
+               "device attribute");
+    cuda_check(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device),
+               "device attribute");
+    int coop = 0;
+    cuda_check(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device),
+               "device attribute");
+    m->mk = coop != 0 && nut::mk_supported(int(c.dim), int(c.ffn_dim), int(kvd),
+                                           int(c.head_dim), int(c.heads), view->quant_type,
+                                           max_smem, m->sms);
+    m->building = true;
+    m->added = 0;
+    m->build_ptrs.clear();
+    m->build_an.clear();
+    m->build_fn.clear();
+}
+
+void model_add_layer(nut_model &mm, const nut_layer_view &lv) {
+    nut_model *m = &mm;
+    const nut_config &c = m->cfg;
+    if (!m->building || m->added >= c.layers)
+        raise(NUT_INVALID_ARGUMENT, "quantized decode: layer count mismatch");
+    if (lv.attention_norm == nullptr || lv.ffn_norm == nullptr)
+        raise(NUT_INVALID_ARGUMENT, "model: null norm weights");
+    const size_t dim = size_t(c.dim);
+    const int64_t kvd = m->kv_heads * c.head_dim;
+    const int t = m->type;
+    if (m->mk) {
+        check_view(lv.query, c.dim, c.dim, t, "query");
+        check_view(lv.key, kvd, c.dim, t, "key");
+        check_view(lv.value, kvd, c.dim, t, "value");
+        check_view(lv.output, c.dim, c.dim, t, "output");
+        check_view(lv.gate, c.ffn_dim, c.dim, t, "gate");
+        check_view(lv.up, c.ffn_dim, c.dim, t, "up");
+        check_view(lv.down, c.dim, c.ffn_dim, t, "down");
+        m->mk_layers.emplace_back();
+        nut::MkLayer &d = m->mk_layers.back();
+        d.qkv = upload_stacked({&lv.query, &lv.key, &lv.value});
+        d.wo = upload_tiles(lv.output, nut::kPairColumn);
+        d.gu = upload_gate_up(lv.gate, lv.up);
+        d.down = upload_tiles(lv.down, nut::kBlockColumn);
+        m->build_ptrs.push_back({d.qkv.data, d.wo.data, d.gu.data, d.down.data, d.qkv.scales,
+                                 d.wo.scales, d.gu.scales, d.down.scales});
+        for (const nut_qmatrix_view *q : {&lv.query, &lv.key, &lv.value, &lv.output, &lv.gate,
+                                          &lv.up, &lv.down}) {
+            const size_t n = size_t(q->rows * q->cols);
+            m->storage_bytes += (t == NUT_QUANT_INT8 ? n : (n + 1) / 2) + (n + 31) / 32 * 2;
+        }
+        m->build_an.insert(m->build_an.end(), lv.attention_norm, lv.attention_norm + dim);
+        m->build_fn.insert(m->build_fn.end(), lv.ffn_norm, lv.ffn_norm + dim);
+    } else {
+        m->layers.emplace_back();
+        DevLayer &d = m->layers.back();
+        d.q = upload(lv.query, c.dim, c.dim, t, "query");
+        d.k = upload(lv.key, kvd, c.dim, t, "key");
+        d.v = upload(lv.value, kvd, c.dim, t, "value");
+        d.o = upload(lv.output, c.dim, c.dim, t, "output");
+        d.gate = upload(lv.gate, c.ffn_dim, c.dim, t, "gate");
+        d.up = upload(lv.up, c.ffn_dim, c.dim, t, "up");
+        d.down = upload(lv.down, c.dim, c.ffn_dim, t, "down");
+        for (const nut::DevQMatrix *q : {&d.q, &d.k, &d.v, &d.o, &d.gate, &d.up, &d.down})
+            m->storage_bytes += q->data_bytes() + q->scale_count() * 2;
+        d.attention_norm = dev_alloc<float>(dim, "alloc norm");
+        d.ffn_norm = dev_alloc<float>(dim, "alloc norm");
+        cuda_check(cudaMemcpy(d.attention_norm, lv.attention_norm, dim * 4,
+                              cudaMemcpyHostToDevice),
+                   "copy norm");
+        cuda_check(cudaMemcpy(d.ffn_norm, lv.ffn_norm, dim * 4, cudaMemcpyHostToDevice),
+                   "copy norm");
+    }
+    m->storage_bytes += 2 * dim * 4;
+    m->added++;
+}
+
+void model_finish(nut_model &mm) {
+    nut_model *m = &mm;
+    if (!m->building || m->added != m->cfg.layers)
+        raise(NUT_INVALID_ARGUMENT, "quantized decode: layer count mismatch");
+    if (m->mk) {
+        const auto &ptrs = m->build_ptrs;
+        m->mk_ptrs = dev_alloc<nut::MkLayerPtrs>(ptrs.size(), "alloc layer table");
+        cuda_check(cudaMemcpy(m->mk_ptrs, ptrs.data(), ptrs.size() * sizeof(ptrs[0]),
+                              cudaMemcpyHostToDevice),
+                   "copy layer table");
+        m->attn_norms = dev_alloc<float>(m->build_an.size(), "alloc norms");
+        m->ffn_norms = dev_alloc<float>(m->build_fn.size(), "alloc norms");
+        cuda_check(cudaMemcpy(m->attn_norms, m->build_an.data(), m->build_an.size() * 4,
+                              cudaMemcpyHostToDevice),
+                   "copy norms");
+        cuda_check(cudaMemcpy(m->ffn_norms, m->build_fn.data(), m->build_fn.size() * 4,
+                              cudaMemcpyHostToDevice),
+                   "copy norms");
+    }
+    m->build_ptrs = {};
+    m->build_an = {};
+    m->build_fn = {};
+    upload_rope(m);
+    settle_uploads();
+    m->building = false;
+}
+
 nut_status nut_model_create(const nut_model_view *view, int device,
                             nut_model **out) {
     return guarded([&] {
         if (view == nullptr || out == nullptr)
             raise(NUT_INVALID_ARGUMENT, "model: null argument");
-        const nut_config &c = view->config;
-        validate_config(c);
-        if (view->quant_type != NUT_QUANT_INT8 && view->quant_type != NUT_QUANT_INT4)
-            raise(NUT_INVALID_ARGUMENT, "model: unknown quant type");
-        if (view->n_layers != c.layers || view->layers == nullptr)
+        validate_config(view->config);
+        if (view->n_layers != view->config.layers || view->layers == nullptr)
             raise(NUT_INVALID_ARGUMENT, "quantized decode: layer count mismatch");
-        if (view->embeddings == nullptr || view->final_norm == nullptr ||
-            (!view->tied_embeddings && view->lm_head == nullptr))
-            raise(NUT_INVALID_ARGUMENT, "model: null fp32 tensor");
         DeviceScope scope(device);
         auto m = std::make_unique<nut_model>();
-        m->device = device;
-        m->cfg = c;
-        m->kv_heads = c.kv_heads == 0 ? c.heads : c.kv_heads;
-        m->type = view->quant_type;
-        m->tied = view->tied_embeddings != 0;
-        cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking),
-                   "create stream");
-        const size_t dim = size_t(c.dim), V = size_t(c.vocab_size);
-        const int64_t kvd = m->kv_heads * c.head_dim;
-        uint64_t bytes = (V * dim + dim + (m->tied ? 0 : V * dim)) * 4;
-        m->embeddings = dev_alloc<float>(V * dim, "alloc embeddings");
-        cuda_check(cudaMemcpy(m->embeddings, view->embeddings, V * dim * 4,
-                              cudaMemcpyHostToDevice),
-                   "copy embeddings");
-        m->final_norm = dev_alloc<float>(dim, "alloc final norm");
-        cuda_check(cudaMemcpy(m->final_norm, view->final_norm, dim * 4,
-                              cudaMemcpyHostToDevice),
-                   "copy final norm");
-        if (!m->tied) {
-            m->lm_head = dev_alloc<float>(V * dim, "alloc lm_head");
-            cuda_check(cudaMemcpy(m->lm_head, view->lm_head, V * dim * 4,
-                                  cudaMemcpyHostToDevice),
-                       "copy lm_head");
-        }
-        int max_smem = 0;
-        cuda_check(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device),
-                   "device attribute");
-        cuda_check(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin,
-                                          device),
-                   "device attribute");
-        int coop = 0;
-        cuda_check(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device),
-                   "device attribute");
-        m->mk = coop != 0 &&
-                nut::mk_supported(int(c.dim), int(c.ffn_dim), int(kvd), int(c.head_dim),
-                                  int(c.heads), view->quant_type, max_smem, m->sms);
-        if (m->mk) {
-            std::vector<nut::MkLayerPtrs> ptrs;
-            std::vector<float> an(size_t(c.layers) * dim), fn(size_t(c.layers) * dim);
-            for (int64_t l = 0; l < c.layers; l++) {
-                const nut_layer_view &lv = view->layers[l];
-                if (lv.attention_norm == nullptr || lv.ffn_norm == nullptr)
-                    raise(NUT_INVALID_ARGUMENT, "model: null norm weights");
-                const int t = view->quant_type;
-                check_view(lv.query, c.dim, c.dim, t, "query");
-                check_view(lv.key, kvd, c.dim, t, "key");
-                check_view(lv.value, kvd, c.dim, t, "value");
-                check_view(lv.output, c.dim, c.dim, t, "output");
-                check_view(lv.gate, c.ffn_dim, c.dim, t, "gate");
-                check_view(lv.up, c.ffn_dim, c.dim, t, "up");
-                check_view(lv.down, c.dim, c.ffn_dim, t, "down");
-                m->mk_layers.emplace_back();
-                nut::MkLayer &d = m->mk_layers.back();
-                d.qkv = upload_stacked({&lv.query, &lv.key, &lv.value});
-                d.wo = upload_tiles(lv.output, nut::kPairColumn);
-                d.gu = upload_gate_up(lv.gate, lv.up);
-                d.down = upload_tiles(lv.down, nut::kBlockColumn);
-                ptrs.push_back({d.qkv.data, d.wo.data, d.gu.data, d.down.data,
-                                d.qkv.scales, d.wo.scales, d.gu.scales, d.down.scales});
-                for (const nut_qmatrix_view *q : {&lv.query, &lv.key, &lv.value, &lv.output,
-                                                  &lv.gate, &lv.up, &lv.down}) {
-                    const size_t n = size_t(q->rows * q->cols);
-                    bytes += (t == NUT_QUANT_INT8 ? n : (n + 1) / 2) + (n + 31) / 32 * 2;
-                }
-                std::copy(lv.attention_norm, lv.attention_norm + dim, an.begin() + l * dim);
-                std::copy(lv.ffn_norm, lv.ffn_norm + dim, fn.begin() + l * dim);
-                bytes += 2 * dim * 4;
-            }
-            m->mk_ptrs = dev_alloc<nut::MkLayerPtrs>(ptrs.size(), "alloc layer table");
-            cuda_check(cudaMemcpy(m->mk_ptrs, ptrs.data(), ptrs.size() * sizeof(ptrs[0]),
-                                  cudaMemcpyHostToDevice),
-                       "copy layer table");
-            m->attn_norms = dev_alloc<float>(an.size(), "alloc norms");
-            m->ffn_norms = dev_alloc<float>(fn.size(), "alloc norms");
-            cuda_check(cudaMemcpy(m->attn_norms, an.data(), an.size() * 4,
-                                  cudaMemcpyHostToDevice),
-                       "copy norms");
-            cuda_check(cudaMemcpy(m->ffn_norms, fn.data(), fn.size() * 4,
-                                  cudaMemcpyHostToDevice),
-                       "copy norms");
-        }
-        for (int64_t l = 0; !m->mk && l < c.layers; l++) {
-            const nut_layer_view &lv = view->layers[l];
-            if (lv.attention_norm == nullptr || lv.ffn_norm == nullptr)
-                raise(NUT_INVALID_ARGUMENT, "model: null norm weights");
-            m->layers.emplace_back();
-            DevLayer &d = m->layers.back();
-            const int t = view->quant_type;
-            d.q = upload(lv.query, c.dim, c.dim, t, "query");
-            d.k = upload(lv.key, kvd, c.dim, t, "key");
-            d.v = upload(lv.value, kvd, c.dim, t, "value");
-            d.o = upload(lv.output, c.dim, c.dim, t, "output");
-            d.gate = upload(lv.gate, c.ffn_dim, c.dim, t, "gate");
-            d.up = upload(lv.up, c.ffn_dim, c.dim, t, "up");
-            d.down = upload(lv.down, c.dim, c.ffn_dim, t, "down");
-            for (const nut::DevQMatrix *q : {&d.q, &d.k, &d.v, &d.o, &d.gate,
-                                             &d.up, &d.down})
-                bytes += q->data_bytes() + q->scale_count() * 2;
-            d.attention_norm = dev_alloc<float>(dim, "alloc norm");
-            d.ffn_norm = dev_alloc<float>(dim, "alloc norm");
-            cuda_check(cudaMemcpy(d.attention_norm, lv.attention_norm, dim * 4,
-                                  cudaMemcpyHostToDevice),
-                       "copy norm");
-            cuda_check(cudaMemcpy(d.ffn_norm, lv.ffn_norm, dim * 4,
-                                  cudaMemcpyHostToDevice),
-                       "copy norm");
-            bytes += 2 * dim * 4;
-        }
-        m->storage_bytes = bytes;
-        upload_rope(m.get());
-        settle_uploads();
+        model_begin(*m, view, device);
+        for (int64_t l = 0; l < view->n_layers; l++)
+            model_add_layer(*m, view->layers[l]);
+        model_finish(*m);
         *out = m.release();
+    });
+}
+
+nut_status nut_model_begin(const nut_model_view *view, int device, nut_model **out) {
+    return guarded([&] {
+        if (out == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "model: null argument");
+        DeviceScope scope(device);
+        auto m = std::make_unique<nut_model>();
+        model_begin(*m, view, device);
+        *out = m.release();
+    });
+}
+
+nut_status nut_model_add_layer(nut_model *model, const nut_layer_view *layer) {
+    return guarded([&] {
+        if (model == nullptr || layer == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "model: null argument");
+        DeviceScope scope(model->device);
+        model_add_layer(*model, *layer);
+    });
+}
+
+nut_status nut_model_finish(nut_model *model) {
+    return guarded([&] {
+        if (model == nullptr)
+            raise(NUT_INVALID_ARGUMENT, "model: null argument");
+        DeviceScope scope(model->device);
+        model_finish(*model);
     });
 }
 
@@ -1204,6 +1263,8 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
     return guarded([&] {
         if (model == nullptr || out == nullptr)
             raise(NUT_INVALID_ARGUMENT, "kv cache: null argument");
+        if (model->building)
+            raise(NUT_INVALID_ARGUMENT, "kv cache: model creation not finished");
         DeviceScope scope(model->device);
         auto kv = std::make_unique<nut_kv>();
         kv->model = model;

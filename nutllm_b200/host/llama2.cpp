@@ -1,9 +1,10 @@
 /* llama2.c loader.  The checks and their exception classes and messages
  * follow the reference (src/llama2.cpp:133-150,199-298) so callers see the
  * same errors; reading is positioned std::ifstream reads of one tensor at a
- * time, and the layers' projections are quantised by a few host threads
- * (each matrix is quantised independently, so the bytes do not depend on
- * the split). */
+ * time.  The quantised loader goes layer by layer: a layer's seven
+ * projections are quantised by seven host threads (each matrix on its own,
+ * so the bytes do not depend on the split) while the previous layer is
+ * packed and uploaded to the device in the background. */
 #include "llama2.hpp"
 
 #include <algorithm>
@@ -156,48 +157,52 @@ Sections parse(Checkpoint &file) {
     return s;
 }
 
-/* One projection of every layer: rows x cols per layer at `first`. */
-std::vector<QuantizedMatrix> quantize_layers(Checkpoint &file, size_t first, size_t rows,
-                                             size_t cols, size_t layers, QuantType type) {
-    const size_t n = mul_checked(rows, cols, "quantized projection");
-    const size_t workers =
-        std::max<size_t>(1, std::min<size_t>(layers, std::thread::hardware_concurrency()));
-    std::vector<std::vector<float>> raw(workers, std::vector<float>(n));
-    std::vector<QuantizedMatrix> out;
-    out.reserve(layers);
-    for (size_t base = 0; base < layers; base += workers) {
-        const size_t count = std::min(workers, layers - base);
-        for (size_t w = 0; w < count; w++)
-            file.read(raw[w].data(), first + (base + w) * n, n);
-        std::vector<std::unique_ptr<QuantizedMatrix>> done(count);
-        std::vector<std::exception_ptr> errors(count);
-        std::vector<std::thread> pool;
-        for (size_t w = 0; w < count; w++)
-            pool.emplace_back([&, w] {
-                try {
-                    done[w].reset(new QuantizedMatrix(
-                        QuantizedMatrix::quantize(raw[w].data(), rows, cols, type)));
-                } catch (...) {
-                    errors[w] = std::current_exception();
-                }
-            });
-        for (std::thread &t : pool)
-            t.join();
-        for (size_t w = 0; w < count; w++) {
-            if (errors[w])
-                std::rethrow_exception(errors[w]);
-            out.push_back(std::move(*done[w]));
-        }
+/* The seven projections of layer l, read from their sections and
+ * quantised by one host thread each (each matrix is quantised on its own,
+ * so the bytes do not depend on the split).  `raw` keeps seven fp32
+ * buffers across layers. */
+QuantizedLayerWeights quantize_layer(Checkpoint &file, const Sections &s, size_t l,
+                                     QuantType type, std::vector<std::vector<float>> &raw) {
+    const ModelConfig &c = s.config;
+    struct Proj {
+        size_t first, rows, cols;
+    };
+    const size_t att = mul_checked(c.dim, c.dim, "quantized projection");
+    const size_t kv = mul_checked(c.kv_dim(), c.dim, "quantized projection");
+    const size_t ff = mul_checked(c.ffn_dim, c.dim, "quantized projection");
+    /* query key value output gate up down, [out][in] as stored */
+    const Proj p[7] = {{s.wq + l * att, c.dim, c.dim},     {s.wk + l * kv, c.kv_dim(), c.dim},
+                       {s.wv + l * kv, c.kv_dim(), c.dim}, {s.wo + l * att, c.dim, c.dim},
+                       {s.w1 + l * ff, c.ffn_dim, c.dim},  {s.w3 + l * ff, c.ffn_dim, c.dim},
+                       {s.w2 + l * ff, c.dim, c.ffn_dim}};
+    raw.resize(7);
+    for (int j = 0; j < 7; j++) {
+        raw[j].resize(p[j].rows * p[j].cols);
+        file.read(raw[j].data(), p[j].first, raw[j].size());
     }
-    return out;
-}
-
-std::vector<std::vector<float>> read_norms(Checkpoint &file, size_t first, size_t layers,
-                                           size_t dim) {
-    std::vector<std::vector<float>> norms(layers, std::vector<float>(dim));
-    for (size_t l = 0; l < layers; l++)
-        file.read(norms[l].data(), first + l * dim, dim);
-    return norms;
+    std::vector<std::unique_ptr<QuantizedMatrix>> done(7);
+    std::vector<std::exception_ptr> errors(7);
+    std::vector<std::thread> pool;
+    for (int j = 0; j < 7; j++)
+        pool.emplace_back([&, j] {
+            try {
+                done[j].reset(new QuantizedMatrix(
+                    QuantizedMatrix::quantize(raw[j].data(), p[j].rows, p[j].cols, type)));
+            } catch (...) {
+                errors[j] = std::current_exception();
+            }
+        });
+    for (std::thread &t : pool)
+        t.join();
+    for (int j = 0; j < 7; j++)
+        if (errors[j])
+            std::rethrow_exception(errors[j]);
+    std::vector<float> an(c.dim), fn(c.dim);
+    file.read(an.data(), s.attention_norms + l * c.dim, c.dim);
+    file.read(fn.data(), s.ffn_norms + l * c.dim, c.dim);
+    return QuantizedLayerWeights(std::move(*done[0]), std::move(*done[1]), std::move(*done[2]),
+                                 std::move(*done[3]), std::move(*done[4]), std::move(*done[5]),
+                                 std::move(*done[6]), std::move(an), std::move(fn));
 }
 
 /* One stored [out][in] projection of a layer into the reference's
@@ -240,6 +245,12 @@ ModelWeights load_llama2c_model(const std::string &path) {
     return model;
 }
 
+/* Streams to the device while it loads: the fp32 tensors first (their
+ * device copy starts at once), then layer by layer, each quantised on the
+ * host while a background thread packs and uploads the previous one
+ * (StreamingUpload), so on a GPU host the returned weights already carry
+ * their device image.  The host storage and the checks are those of the
+ * reference loader (src/llama2.cpp:339-412). */
 QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, QuantType type) {
     Checkpoint file(path);
     const Sections s = parse(file);
@@ -247,26 +258,17 @@ QuantizedModelWeights load_llama2c_quantized_model(const std::string &path, Quan
     QuantizedModelWeights model(c, type, !s.shared_classifier);
     model.tied_embeddings = s.shared_classifier;
     file.read(model.embeddings.data(), s.embeddings, c.vocab_size * c.dim);
-
-    auto att_norms = read_norms(file, s.attention_norms, c.layers, c.dim);
-    auto wq = quantize_layers(file, s.wq, c.dim, c.dim, c.layers, type);
-    auto wk = quantize_layers(file, s.wk, c.kv_dim(), c.dim, c.layers, type);
-    auto wv = quantize_layers(file, s.wv, c.kv_dim(), c.dim, c.layers, type);
-    auto wo = quantize_layers(file, s.wo, c.dim, c.dim, c.layers, type);
-    auto ffn_norms = read_norms(file, s.ffn_norms, c.layers, c.dim);
-    auto gate = quantize_layers(file, s.w1, c.ffn_dim, c.dim, c.layers, type);
-    auto down = quantize_layers(file, s.w2, c.dim, c.ffn_dim, c.layers, type);
-    auto up = quantize_layers(file, s.w3, c.ffn_dim, c.dim, c.layers, type);
     file.read(model.final_norm.data(), s.final_norm, c.dim);
     if (!s.shared_classifier)
         file.read(model.lm_head.data(), s.classifier, c.vocab_size * c.dim);
-
-    model.layers.reserve(c.layers);
-    for (size_t l = 0; l < c.layers; l++)
-        model.layers.emplace_back(std::move(wq[l]), std::move(wk[l]), std::move(wv[l]),
-                                  std::move(wo[l]), std::move(gate[l]), std::move(up[l]),
-                                  std::move(down[l]), std::move(att_norms[l]),
-                                  std::move(ffn_norms[l]));
+    model.layers.reserve(c.layers); /* the uploader reads earlier layers in place */
+    StreamingUpload upload(model);
+    std::vector<std::vector<float>> raw;
+    for (size_t l = 0; l < c.layers; l++) {
+        model.layers.push_back(quantize_layer(file, s, l, type, raw));
+        upload.add(l);
+    }
+    upload.finish(model);
     return model;
 }
 

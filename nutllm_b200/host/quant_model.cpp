@@ -4,7 +4,11 @@
  * (src/quant_model.cpp:140-220). */
 #include "quant_model.hpp"
 
+#include <condition_variable>
+#include <deque>
+#include <mutex>
 #include <stdexcept>
+#include <thread>
 #include <utility>
 
 #include "device.hpp"
@@ -72,6 +76,38 @@ void check_decode(const QuantizedModelWeights &model, const KVCache &cache,
         throw std::invalid_argument("quantized decode: zero threads");
 }
 
+nut_layer_view layer_view(const QuantizedLayerWeights &l) {
+    nut_layer_view v{};
+    v.query = view_of(l.query);
+    v.key = view_of(l.key);
+    v.value = view_of(l.value);
+    v.output = view_of(l.output);
+    v.gate = view_of(l.gate);
+    v.up = view_of(l.up);
+    v.down = view_of(l.down);
+    v.attention_norm = l.attention_norm.data();
+    v.ffn_norm = l.ffn_norm.data();
+    return v;
+}
+
+/* The fp32 tensors and configuration; `layers` is left to the caller. */
+nut_model_view model_view(const QuantizedModelWeights &w) {
+    const ModelConfig &config = w.config;
+    nut_model_view v{};
+    v.config = nut_config{int64_t(config.layers),    int64_t(config.heads),
+                          int64_t(config.dim),       int64_t(config.head_dim),
+                          int64_t(config.ffn_dim),   int64_t(config.vocab_size),
+                          int64_t(config.max_seq),   int64_t(config.eos_token),
+                          int64_t(config.kv_heads)};
+    v.quant_type = w.quant_type == QuantType::int8 ? NUT_QUANT_INT8 : NUT_QUANT_INT4;
+    v.tied_embeddings = w.tied_embeddings ? 1 : 0;
+    v.embeddings = w.embeddings.data();
+    v.final_norm = w.final_norm.data();
+    v.lm_head = w.tied_embeddings ? nullptr : w.lm_head.data();
+    v.n_layers = int64_t(config.layers);
+    return v;
+}
+
 } // namespace
 
 nut_model *QuantizedModelWeights::device() const {
@@ -80,35 +116,108 @@ nut_model *QuantizedModelWeights::device() const {
     if (layers.size() != config.layers)
         throw std::invalid_argument("quantized decode: layer count mismatch");
     std::vector<nut_layer_view> lv(layers.size());
-    for (size_t i = 0; i < layers.size(); i++) {
-        const QuantizedLayerWeights &l = layers[i];
-        lv[i].query = view_of(l.query);
-        lv[i].key = view_of(l.key);
-        lv[i].value = view_of(l.value);
-        lv[i].output = view_of(l.output);
-        lv[i].gate = view_of(l.gate);
-        lv[i].up = view_of(l.up);
-        lv[i].down = view_of(l.down);
-        lv[i].attention_norm = l.attention_norm.data();
-        lv[i].ffn_norm = l.ffn_norm.data();
-    }
-    nut_model_view v{};
-    v.config = nut_config{int64_t(config.layers),    int64_t(config.heads),
-                          int64_t(config.dim),       int64_t(config.head_dim),
-                          int64_t(config.ffn_dim),   int64_t(config.vocab_size),
-                          int64_t(config.max_seq),   int64_t(config.eos_token),
-                          int64_t(config.kv_heads)};
-    v.quant_type = quant_type == QuantType::int8 ? NUT_QUANT_INT8 : NUT_QUANT_INT4;
-    v.tied_embeddings = tied_embeddings ? 1 : 0;
-    v.embeddings = embeddings.data();
-    v.final_norm = final_norm.data();
-    v.lm_head = tied_embeddings ? nullptr : lm_head.data();
+    for (size_t i = 0; i < layers.size(); i++)
+        lv[i] = layer_view(layers[i]);
+    nut_model_view v = model_view(*this);
     v.layers = lv.data();
     v.n_layers = int64_t(lv.size());
     nut_model *m = nullptr;
     nutdev::check(nut_model_create(&v, nutdev::current_device(), &m));
     device_.reset(m, [](nut_model *p) { nut_model_destroy(p); });
     return m;
+}
+
+void QuantizedModelWeights::adopt_device(nut_model *m) {
+    device_.reset(m, [](nut_model *p) { nut_model_destroy(p); });
+}
+
+/* ---- streaming upload ---------------------------------------------------- */
+
+struct StreamingUpload::State {
+    const QuantizedModelWeights *weights = nullptr;
+    nut_model *model = nullptr;
+    std::mutex lock;
+    std::condition_variable wake;
+    std::deque<size_t> queue;
+    bool closing = false;
+    bool failed = false;
+    std::thread worker;
+
+    void run() {
+        for (;;) {
+            size_t l = 0;
+            {
+                std::unique_lock<std::mutex> g(lock);
+                wake.wait(g, [&] { return closing || !queue.empty(); });
+                if (queue.empty())
+                    return;
+                l = queue.front();
+                queue.pop_front();
+            }
+            if (failed)
+                continue;
+            const nut_layer_view v = layer_view(weights->layers[l]);
+            if (nut_model_add_layer(model, &v) != NUT_OK) {
+                std::lock_guard<std::mutex> g(lock);
+                failed = true;
+            }
+        }
+    }
+    void stop() {
+        {
+            std::lock_guard<std::mutex> g(lock);
+            closing = true;
+        }
+        wake.notify_all();
+        if (worker.joinable())
+            worker.join();
+    }
+};
+
+StreamingUpload::StreamingUpload(const QuantizedModelWeights &weights)
+    : state_(new State) {
+    int count = 0;
+    if (nut_device_count(&count) != NUT_OK || count <= 0)
+        return;
+    const nut_model_view v = model_view(weights);
+    nut_model *m = nullptr;
+    if (nut_model_begin(&v, nutdev::current_device(), &m) != NUT_OK)
+        return;
+    state_->weights = &weights;
+    state_->model = m;
+    state_->worker = std::thread([s = state_.get()] { s->run(); });
+}
+
+StreamingUpload::~StreamingUpload() {
+    state_->stop();
+    if (state_->model != nullptr)
+        nut_model_destroy(state_->model);
+}
+
+bool StreamingUpload::active() const { return state_->model != nullptr; }
+
+void StreamingUpload::add(size_t layer) {
+    if (state_->model == nullptr)
+        return;
+    {
+        std::lock_guard<std::mutex> g(state_->lock);
+        state_->queue.push_back(layer);
+    }
+    state_->wake.notify_one();
+}
+
+void StreamingUpload::finish(QuantizedModelWeights &weights) {
+    state_->stop();
+    nut_model *m = state_->model;
+    if (m == nullptr)
+        return;
+    state_->model = nullptr;
+    if (state_->failed || weights.layers.size() != weights.config.layers ||
+        nut_model_finish(m) != NUT_OK) {
+        nut_model_destroy(m); /* first use uploads again and reports the error */
+        return;
+    }
+    weights.adopt_device(m);
 }
 
 std::vector<float> prefill_quantized(const QuantizedModelWeights &model,

@@ -53,9 +53,35 @@ struct QuantizedModelWeights {
     /* The device image (uploaded on first use; later changes to the host
      * weights are not seen by it). */
     nut_model *device() const;
+    /* Takes ownership of a finished device image of these weights (built
+     * by a streaming loader), so first use does not upload them again. */
+    void adopt_device(nut_model *model);
 
 private:
     mutable std::shared_ptr<nut_model> device_;
+};
+
+/* Builds the device image of a model while a loader is still producing its
+ * layers: the constructor uploads the fp32 tensors (nut_model_begin) when a
+ * device is present, add(l) queues layer l for a background thread that
+ * packs and uploads it (nut_model_add_layer) while the loader reads and
+ * quantises the next one, and finish() waits for the thread, completes the
+ * image (nut_model_finish) and gives it to the weights.  Without a device,
+ * or if any device step fails, it stands aside and the weights keep the
+ * upload-on-first-use path (which then reports the failure). */
+class StreamingUpload {
+public:
+    explicit StreamingUpload(const QuantizedModelWeights &model);
+    ~StreamingUpload();
+    StreamingUpload(const StreamingUpload &) = delete;
+    StreamingUpload &operator=(const StreamingUpload &) = delete;
+    void add(size_t layer);
+    void finish(QuantizedModelWeights &model);
+    bool active() const;
+
+private:
+    struct State;
+    std::unique_ptr<State> state_;
 };
 
 std::vector<float> prefill_quantized(const QuantizedModelWeights &model,

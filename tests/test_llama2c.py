@@ -344,3 +344,63 @@ def test_tokenizer_reference_fixture():
     if oracle.reference_available():
         assert ids == oracle.Reference().llama2c_encode(tok, 6, "H").tolist()
     assert nb.tokenizer_decode(tok, 6, ids + [4, 5]) == b"Hi!"
+
+
+def _write_tinyllama_shape(path, layers=2, seed=77):
+    """A seeded llama2.c checkpoint of TinyLlama's layer shape (dim 2048,
+    FFN 5632, 32 heads over 4 kv heads, vocabulary 32000, tied classifier)
+    with `layers` layers, written tensor by tensor."""
+    dim, ffn, heads, kv, vocab, max_seq = 2048, 5632, 32, 4, 32000, 256
+    hd = dim // heads
+    kvd = kv * hd
+    stream = [1000]
+
+    def normal(n, sigma=0.02):
+        stream[0] += 1
+        return nb.synth_normal(seed, stream[0], n, sigma)
+
+    with open(path, "wb") as f:
+        f.write(np.array([dim, ffn, layers, heads, kv, vocab, max_seq], np.int32).tobytes())
+        f.write(normal(vocab * dim).tobytes())                         # embeddings
+        f.write(np.ones(layers * dim, np.float32).tobytes())           # attention norms
+        for rows, cols in ((dim, dim), (kvd, dim), (kvd, dim), (dim, dim)):
+            f.write(normal(layers * rows * cols).tobytes())            # wq wk wv wo
+        f.write(np.ones(layers * dim, np.float32).tobytes())           # ffn norms
+        for rows, cols in ((ffn, dim), (dim, ffn), (ffn, dim)):
+            f.write(normal(layers * rows * cols).tobytes())            # w1 w2 w3
+        f.write(np.ones(dim, np.float32).tobytes())                    # final norm
+        f.write(np.zeros(max_seq * hd, np.float32).tobytes())          # RoPE (unused)
+    return path
+
+
+@pytest.mark.gpu
+@pytest.mark.slow
+def test_streaming_loader_tinyllama_shape(gpu, orc, tmp_path):
+    """load_llama2c_quantized_model streams to the device: layer l + 1 is
+    read and quantised on the host while layer l is packed and uploaded,
+    and the returned weights carry that device image.  On a two-layer
+    TinyLlama-shape INT4 checkpoint, the host bytes equal the oracle
+    quantiser's (storage size), the generated ids equal the oracle's greedy
+    ids at every step whose top-2 gap is clear, and the load is timed."""
+    import time
+    path = _write_tinyllama_shape(str(tmp_path / "tl2.bin"))
+    prompt = np.array([1, 3407, 20, 9011, 17], np.int32)
+    steps = 6
+    t0 = time.perf_counter()
+    ids, st = nb.llama2c_generate(path, nb.INT4, prompt, steps)
+    total = time.perf_counter() - t0
+    work = st.prefill_seconds + st.decode_seconds
+    m = _oracle_model(orc, path, nb.INT4)
+    cfg, tied, nbytes, _ = nb.llama2c_inspect(path, nb.INT4)
+    assert tied and nbytes == m.storage_bytes()
+    om = orc.model(m)
+    ids_o, lg_o, _ = om.generate(prompt, steps)
+    assert len(ids) == steps
+    s = np.sort(lg_o, axis=1)
+    clear = (s[:, -1] - s[:, -2]) > 4e-3
+    print(f"streaming load + generate of a 2-layer TinyLlama-shape INT4 checkpoint "
+          f"({os.path.getsize(path) / 1e6:.0f} MB): {total:.2f} s, of which "
+          f"{work * 1e3:.1f} ms on the device; ids compared at {int(clear.sum())} of {steps}")
+    first = next((i for i, c in enumerate(clear) if not c), steps)
+    assert first > 0
+    assert ids[:first].tolist() == ids_o[:first].tolist()
