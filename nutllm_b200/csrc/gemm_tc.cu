@@ -300,6 +300,214 @@ gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     }
 }
 
+/* ---- persistent form ----------------------------------------------------
+
+   For products of several waves of tiles: one CTA per SM walks the work
+   units u = blockIdx.x, blockIdx.x + gridDim.x, ... (unit = output tile x
+   K split; M tiles fastest, so the CTAs of one moment share a weight tile
+   in L2).  The accumulator is double-buffered in tensor memory (2 x BN
+   columns): while warps 0-3 drain unit i's accumulator to Y, warp 5 already
+   multiplies unit i + 1 into the other half, and warp 4 keeps streaming
+   stages across unit boundaries.  Barriers: full / empty per stage (as in
+   gemm_f16_kernel), acc_full[2] (the MMA warp's commit: an accumulator
+   is complete) and acc_empty[2] (the 128 epilogue threads: an accumulator
+   has been read).  Every wait is bounded; on a timeout a role records the
+   error, raises the CTA's abort flag and stops, the producer still waits
+   (bounded) for the copies it issued, and the CTA frees its tensor memory. */
+
+struct PersistArgs {
+    int tiles_m, tiles_n, splits, units;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreadsG, 1)
+gemm_f16_persist(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const GemmArgs g, const PersistArgs pa) {
+    using S = GemmSmem<BN, STAGES>;
+    static_assert(2 * BN <= 512, "two accumulators in tensor memory");
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *tiles = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStage);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;  /* [2] */
+    uint64_t *acc_empty = acc_full + 2;   /* [2] */
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kb_total = g.K / kBK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], kEpiWarps * 32);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kEpiWarps + 1)
+        tmem_alloc(tmem_slot, 2 * BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto unit_of = [&](int u, int &m0, int &n0, int &kb0, int &kbn) {
+        const int per = pa.tiles_m * pa.tiles_n;
+        const int sp = u / per, t = u - sp * per;
+        const int tn = t / pa.tiles_m, tm = t - tn * pa.tiles_m;
+        m0 = tm * kBM;
+        n0 = tn * BN;
+        kb0 = sp * kb_total / pa.splits;
+        kbn = (sp + 1) * kb_total / pa.splits - kb0;
+    };
+
+    if (warp == kEpiWarps) {
+        /* TMA producer: one stage sequence across all of this CTA's units */
+        if (lane == 0) {
+            int issued = 0;
+            bool stop = false;
+            for (int u = blockIdx.x; u < pa.units && !stop; u += gridDim.x) {
+                int m0, n0, kb0, kbn;
+                unit_of(u, m0, n0, kb0, kbn);
+                for (int kb = 0; kb < kbn; kb++) {
+                    const int s = issued % STAGES;
+                    const uint32_t par = uint32_t((issued / STAGES) & 1);
+                    if (issued >= STAGES &&
+                        (*abort_flag || !mbar_wait(&empty[s], par ^ 1u, g.limit_ns))) {
+                        atomicCAS(g.error, 0, kGemmErrEmpty);
+                        *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    uint8_t *a = tiles + s * S::kStage;
+                    mbar_expect_tx(&full[s], uint32_t(S::kStage));
+                    tma_load_2d(a, &tmA, (kb0 + kb) * kBK, m0, &full[s]);
+                    tma_load_2d(a + S::kA, &tmB, (kb0 + kb) * kBK, n0, &full[s]);
+                    issued++;
+                }
+            }
+            /* every issued copy has landed before the CTA can exit */
+            for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; i++)
+                mbar_wait(&full[i % STAGES], uint32_t((i / STAGES) & 1), g.limit_ns);
+        }
+    } else if (warp == kEpiWarps + 1) {
+        /* MMA issuer */
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(kBM, BN);
+            int consumed = 0, local = 0;
+            bool stop = false;
+            for (int u = blockIdx.x; u < pa.units && !stop; u += gridDim.x, local++) {
+                int m0, n0, kb0, kbn;
+                unit_of(u, m0, n0, kb0, kbn);
+                const int acc = local & 1;
+                /* the epilogue has read this accumulator's previous unit */
+                if (local >= 2 && (*abort_flag ||
+                                   !mbar_wait(&acc_empty[acc], uint32_t(((local >> 1) - 1) & 1),
+                                              g.limit_ns))) {
+                    atomicCAS(g.error, 0, kGemmErrAccum);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * BN);
+                for (int kb = 0; kb < kbn; kb++) {
+                    const int s = consumed % STAGES;
+                    const uint32_t par = uint32_t((consumed / STAGES) & 1);
+                    if (*abort_flag || !mbar_wait(&full[s], par, g.limit_ns)) {
+                        atomicCAS(g.error, 0, kGemmErrFull);
+                        *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(tiles + s * S::kStage), b = a + S::kA;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        umma_f16(d, smem_desc_sw128(a + k * 32), smem_desc_sw128(b + k * 32),
+                                  idesc, (kb | k) != 0);
+                    umma_commit(&empty[s]);
+                    consumed++;
+                }
+                if (!stop)
+                    umma_commit(&acc_full[acc]);
+            }
+        }
+        __syncwarp();
+    } else {
+        /* epilogue: warp w owns TMEM lanes (rows) 32 w .. 32 w + 31 */
+        int local = 0;
+        for (int u = blockIdx.x; u < pa.units; u += gridDim.x, local++) {
+            int m0, n0, kb0, kbn;
+            unit_of(u, m0, n0, kb0, kbn);
+            const int acc = local & 1;
+            bool ok = !*abort_flag &&
+                      mbar_wait(&acc_full[acc], uint32_t((local >> 1) & 1), g.limit_ns);
+            if (!ok)
+                atomicCAS(g.error, 0, kGemmErrAccum);
+            ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+            if (!ok) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const int row = m0 + warp * 32 + lane;
+            const uint32_t base = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float v[16];
+                tmem_ld16(base + uint32_t(c), v);
+                if (row >= g.M)
+                    continue;
+                float *y = g.Y + size_t(row) * g.ldy + n0 + c;
+                const bool vec = n0 + c + 16 <= g.N && (g.ldy % 4) == 0;
+                if (pa.splits > 1) {
+                    if (vec) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            asm volatile(
+                                "red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n"
+                                ::"l"(y + j), "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]),
+                                "f"(v[j + 3])
+                                : "memory");
+                    } else {
+                        for (int j = 0; j < 16; j++)
+                            if (n0 + c + j < g.N)
+                                atomicAdd(y + j, v[j]);
+                    }
+                } else if (vec) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        if (g.accumulate) {
+                            const float4 r = *reinterpret_cast<const float4 *>(y + j);
+                            o.x += r.x, o.y += r.y, o.z += r.z, o.w += r.w;
+                        }
+                        *reinterpret_cast<float4 *>(y + j) = o;
+                    }
+                } else {
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c + j < g.N)
+                            y[j] = g.accumulate ? y[j] + v[j] : v[j];
+                }
+            }
+            /* this accumulator may be overwritten by the unit after next */
+            tc_fence_before();
+            mbar_arrive(&acc_empty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
 /* ---- dequantisation and activation rounding ---- */
 
 /* Fragment tiles (any tile order) -> fp16 [row_tiles * 16][blocks * 32]
@@ -643,6 +851,21 @@ cudaError_t launch_bn(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs
     return cudaGetLastError();
 }
 
+template <int BN, int STAGES>
+cudaError_t launch_persist(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs &g,
+                           const PersistArgs &pa, int grid, cudaStream_t stream) {
+    using S = GemmSmem<BN, STAGES>;
+    static_assert(S::kBytes + 64 <= 227 * 1024, "shared memory per CTA");
+    auto k = gemm_f16_persist<BN, STAGES>;
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
+    if (e != cudaSuccess)
+        return e;
+    k<<<grid, kThreadsG, S::kBytes, stream>>>(a, b, g, pa);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
 template <int STAGES, int CTAS_PER_SM = 1>
 cudaError_t launch_q4(const CUtensorMap &a, const uint8_t *wq, const GemmArgs &g,
                       cudaStream_t stream) {
@@ -731,6 +954,19 @@ cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_a
     CUtensorMap ma, mb;
     if (!encode_map(&ma, A, M, K, kBM) || !encode_map(&mb, B, N_alloc, K, bn))
         return cudaErrorInvalidValue;
+    /* several waves of 256-column tiles: one persistent CTA per SM, the
+     * accumulator double-buffered in tensor memory so each unit's epilogue
+     * overlaps the next unit's products (NUTLLM_GEMM_PERSIST=0: one CTA per
+     * unit, as below) */
+    static const bool persist_on = [] {
+        const char *e = std::getenv("NUTLLM_GEMM_PERSIST");
+        return e == nullptr || std::atoi(e) != 0;
+    }();
+    if (persist_on && bn == 256 && tiles * splits > slots) {
+        const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, splits};
+        const PersistArgs pa{mt, (N + bn - 1) / bn, splits, tiles * splits};
+        return launch_persist<256, 4>(ma, mb, g, pa, std::min(sms, pa.units), stream);
+    }
     const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, splits};
     if (bn == 256)
         return launch_bn<256, 4>(ma, mb, g, stream);
