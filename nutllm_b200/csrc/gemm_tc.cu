@@ -508,6 +508,312 @@ gemm_f16_persist(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
 }
 
+/* ---- SM-pair persistent form (tcgen05 cta_group::2) -----------------------
+
+   For the same products as gemm_f16_persist when M covers 256-row tiles:
+   the two CTAs of a cluster (an SM pair) compute one 256 x 256 output tile
+   per work unit with one 2-SM product.  CTA r of the pair stages rows
+   m0 + 128 r .. of A and rows n0 + 128 r .. of B (16 KB each per 64-wide K
+   block), so each SM streams half of B: 32 KB of operands per stage for
+   128 x 256 x 64 products instead of 48 KB in the one-SM form, a third less
+   L2-to-SM traffic per flop.  The leader (rank 0) issues
+   tcgen05.mma.cta_group::2 (M = 256, N = 256), which multiplies A halves
+   and B halves across the pair and leaves rows m0 + 128 r .. of the tile
+   in CTA r's tensor memory (256 fp32 columns, double-buffered: 512).
+   Barriers: both CTAs' TMA loads complete on the leader's full[s] (it
+   expects both CTAs' bytes); the leader's commit arrives on empty[s] and
+   on acc_full[a] of both CTAs (multicast arrive of tcgen05.commit); the
+   epilogue threads of both CTAs arrive on the leader's acc_empty[a].
+   Only loads of this GPU's own memory, none multicast.  Every wait is
+   bounded, and both CTAs meet at one cluster barrier before freeing their
+   tensor memory. */
+
+constexpr int kPairBN = 256;                 /* tile columns (B rows) per pair */
+constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  /* clears the peer bit: rank 0's copy */
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t ncluster_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+/* Shared::cluster address of the same variable in CTA `rank` of the cluster. */
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(
+                     cluster_addr)
+                 : "memory");
+}
+/* 2-SM TMA load into this CTA's shared memory, completing on the barrier
+ * at cluster address `bar` (the leader's). */
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y,
+                                                 uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     smem_u32(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t addr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(addr), "r"(cols)
+                 : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+/* Arrives on the barrier at this offset in both CTAs of the pair once every
+ * 2-SM product issued so far by this thread has completed. */
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+    const uint16_t both = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;\n" ::"r"(smem_u32(bar)),
+        "h"(both)
+        : "memory");
+}
+
+template <int STAGES>
+struct PairSmem {
+    static constexpr int kA = kBM * kBK * 2;      /* 16 KB: this CTA's 128 rows of A */
+    static constexpr int kB = 128 * kBK * 2;      /* 16 KB: this CTA's 128 rows of B */
+    static constexpr int kStage = kA + kB;
+    static constexpr size_t kBytes = size_t(STAGES) * kStage + 1024 /* align */ + 256;
+};
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreadsG, 1)
+gemm_f16_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const GemmArgs g, const PersistArgs pa) {
+    using S = PairSmem<STAGES>;
+    constexpr int BN = kPairBN;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *tiles = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * S::kStage);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;  /* [2] */
+    uint64_t *acc_empty = acc_full + 2;   /* [2] (the leader's counts both CTAs) */
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int pair = int(cluster_id_x()), pairs = int(ncluster_x());
+    const int kb_total = g.K / kBK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 2 * kEpiWarps * 32);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kEpiWarps + 1)
+        tmem_alloc_pair(tmem_slot, 2 * BN);
+    tc_fence_before();
+    /* both CTAs' barriers are initialised before either signals the other */
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto unit_of = [&](int u, int &m0, int &n0, int &kb0, int &kbn) {
+        const int per = pa.tiles_m * pa.tiles_n;
+        const int sp = u / per, t = u - sp * per;
+        const int tn = t / pa.tiles_m, tm = t - tn * pa.tiles_m;
+        m0 = tm * 2 * kBM;
+        n0 = tn * BN;
+        kb0 = sp * kb_total / pa.splits;
+        kbn = (sp + 1) * kb_total / pa.splits - kb0;
+    };
+
+    if (warp == kEpiWarps) {
+        /* TMA producer of this CTA's halves (both CTAs) */
+        if (lane == 0) {
+            int issued = 0;
+            bool stop = false;
+            for (int u = pair; u < pa.units && !stop; u += pairs) {
+                int m0, n0, kb0, kbn;
+                unit_of(u, m0, n0, kb0, kbn);
+                for (int kb = 0; kb < kbn; kb++) {
+                    const int s = issued % STAGES;
+                    const uint32_t par = uint32_t((issued / STAGES) & 1);
+                    if (issued >= STAGES &&
+                        (*abort_flag || !mbar_wait(&empty[s], par ^ 1u, g.limit_ns))) {
+                        atomicCAS(g.error, 0, kGemmErrEmpty);
+                        *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    uint8_t *a = tiles + s * S::kStage;
+                    if (rank == 0)
+                        mbar_expect_tx(&full[s], uint32_t(2 * S::kStage));
+                    const uint32_t bar = smem_u32(&full[s]) & kPeerMask;
+                    tma_load_2d_pair(a, &tmA, (kb0 + kb) * kBK, m0 + int(rank) * kBM, bar);
+                    tma_load_2d_pair(a + S::kA, &tmB, (kb0 + kb) * kBK, n0 + int(rank) * 128,
+                                     bar);
+                    issued++;
+                }
+            }
+            /* the leader's full barriers count both CTAs' copies: every
+             * issued copy has landed before the leader exits */
+            if (rank == 0)
+                for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; i++)
+                    mbar_wait(&full[i % STAGES], uint32_t((i / STAGES) & 1), g.limit_ns);
+        }
+    } else if (warp == kEpiWarps + 1) {
+        /* MMA issuer: the leader only */
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_f16(2 * kBM, BN);
+            int consumed = 0, local = 0;
+            bool stop = false;
+            for (int u = pair; u < pa.units && !stop; u += pairs, local++) {
+                int m0, n0, kb0, kbn;
+                unit_of(u, m0, n0, kb0, kbn);
+                const int acc = local & 1;
+                /* both CTAs' epilogues have read this accumulator's
+                 * previous unit */
+                if (local >= 2 && (*abort_flag ||
+                                   !mbar_wait(&acc_empty[acc], uint32_t(((local >> 1) - 1) & 1),
+                                              g.limit_ns))) {
+                    atomicCAS(g.error, 0, kGemmErrAccum);
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * BN);
+                for (int kb = 0; kb < kbn; kb++) {
+                    const int s = consumed % STAGES;
+                    const uint32_t par = uint32_t((consumed / STAGES) & 1);
+                    if (*abort_flag || !mbar_wait(&full[s], par, g.limit_ns)) {
+                        atomicCAS(g.error, 0, kGemmErrFull);
+                        *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(tiles + s * S::kStage), b = a + S::kA;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        umma_f16_pair(d, smem_desc_sw128(a + k * 32),
+                                      smem_desc_sw128(b + k * 32), idesc, (kb | k) != 0);
+                    umma_commit_pair(&empty[s]);
+                    consumed++;
+                }
+                if (!stop)
+                    umma_commit_pair(&acc_full[acc]);
+            }
+        }
+        __syncwarp();
+    } else {
+        /* epilogue (both CTAs): warp w owns TMEM lanes 32 w .. 32 w + 31,
+         * i.e. rows m0 + 128 rank + 32 w + lane of the unit's tile */
+        const uint32_t leader_empty0 = map_rank(smem_u32(&acc_empty[0]), 0);
+        const uint32_t leader_empty1 = map_rank(smem_u32(&acc_empty[1]), 0);
+        int local = 0;
+        for (int u = pair; u < pa.units; u += pairs, local++) {
+            int m0, n0, kb0, kbn;
+            unit_of(u, m0, n0, kb0, kbn);
+            const int acc = local & 1;
+            bool ok = !*abort_flag &&
+                      mbar_wait(&acc_full[acc], uint32_t((local >> 1) & 1), g.limit_ns);
+            if (!ok)
+                atomicCAS(g.error, 0, kGemmErrAccum);
+            ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
+            if (!ok) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const int row = m0 + int(rank) * kBM + warp * 32 + lane;
+            const uint32_t base = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                float v[16];
+                tmem_ld16(base + uint32_t(c), v);
+                if (row >= g.M)
+                    continue;
+                float *y = g.Y + size_t(row) * g.ldy + n0 + c;
+                const bool vec = n0 + c + 16 <= g.N && (g.ldy % 4) == 0;
+                if (pa.splits > 1) {
+                    if (vec) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            asm volatile(
+                                "red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n"
+                                ::"l"(y + j), "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]),
+                                "f"(v[j + 3])
+                                : "memory");
+                    } else {
+                        for (int j = 0; j < 16; j++)
+                            if (n0 + c + j < g.N)
+                                atomicAdd(y + j, v[j]);
+                    }
+                } else if (vec) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        if (g.accumulate) {
+                            const float4 r = *reinterpret_cast<const float4 *>(y + j);
+                            o.x += r.x, o.y += r.y, o.z += r.z, o.w += r.w;
+                        }
+                        *reinterpret_cast<float4 *>(y + j) = o;
+                    }
+                } else {
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c + j < g.N)
+                            y[j] = g.accumulate ? y[j] + v[j] : v[j];
+                }
+            }
+            /* this accumulator may be overwritten by the unit after next */
+            tc_fence_before();
+            mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    /* the peer's tensor memory is written by the leader's products and read
+     * by the peer's epilogue: free it only when both CTAs are done */
+    cluster_sync();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 2 * BN);
+    }
+}
+
 /* ---- dequantisation and activation rounding ---- */
 
 /* Fragment tiles (any tile order) -> fp16 [row_tiles * 16][blocks * 32]
@@ -866,6 +1172,45 @@ cudaError_t launch_persist(const CUtensorMap &a, const CUtensorMap &b, const Gem
     return cudaGetLastError();
 }
 
+/* Launches the SM-pair kernel with as many pairs as fit at once (at most
+ * one per work unit).  cudaErrorNotSupported when no pair fits. */
+template <int STAGES>
+cudaError_t launch_pair(const CUtensorMap &a, const CUtensorMap &b, const GemmArgs &g,
+                        const PersistArgs &pa, cudaStream_t stream) {
+    using S = PairSmem<STAGES>;
+    static_assert(S::kBytes + 64 <= 227 * 1024, "shared memory per CTA");
+    auto k = gemm_f16_pair<STAGES>;
+    cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::kBytes));
+    if (e != cudaSuccess)
+        return e;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreadsG);
+    cfg.dynamicSmemBytes = S::kBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int fits = -1; /* pairs resident at once (same for every call) */
+    if (fits < 0) {
+        cfg.gridDim = dim3(2 * 74);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess)
+            n = 0;
+        fits = n;
+    }
+    if (fits <= 0)
+        return cudaErrorNotSupported;
+    cfg.gridDim = dim3(2 * std::min(fits, pa.units));
+    e = cudaLaunchKernelEx(&cfg, k, a, b, g, pa);
+    count_launches(1);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 template <int STAGES, int CTAS_PER_SM = 1>
 cudaError_t launch_q4(const CUtensorMap &a, const uint8_t *wq, const GemmArgs &g,
                       cudaStream_t stream) {
@@ -962,6 +1307,26 @@ cudaError_t gemm_f16(const uint16_t *A, int M, const uint16_t *B, int N, int N_a
         const char *e = std::getenv("NUTLLM_GEMM_PERSIST");
         return e == nullptr || std::atoi(e) != 0;
     }();
+    /* SM pairs (two 128-row halves of a 256 x 256 tile per cluster) when M
+     * spans more than one 128-row tile (NUTLLM_GEMM_PAIR=0: one SM per tile) */
+    static const bool pair_on = [] {
+        const char *e = std::getenv("NUTLLM_GEMM_PAIR");
+        return e == nullptr || std::atoi(e) != 0;
+    }();
+    if (persist_on && pair_on && bn == 256 && tiles * splits > slots && M > kBM) {
+        /* no split K: these products already span several waves of pairs,
+         * and a split's atomic epilogue costs more than the wave it fills
+         * (32000 x 2048 x 512: 76 us unsplit, 113 us in two splits) */
+        const int mt2 = (M + 2 * kBM - 1) / (2 * kBM), nt2 = (N + 255) / 256;
+        CUtensorMap mb2;
+        if (!encode_map(&mb2, B, N_alloc, K, 128))
+            return cudaErrorInvalidValue;
+        const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, 1};
+        const PersistArgs pa{mt2, nt2, 1, mt2 * nt2};
+        const cudaError_t e = launch_pair<6>(ma, mb2, g, pa, stream);
+        if (e != cudaErrorNotSupported)
+            return e;
+    }
     if (persist_on && bn == 256 && tiles * splits > slots) {
         const GemmArgs g{M, N, K, Y, ldy, accumulate ? 1 : 0, error, limit_ns, splits};
         const PersistArgs pa{mt, (N + bn - 1) / bn, splits, tiles * splits};

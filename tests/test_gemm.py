@@ -72,3 +72,16 @@ def test_gemm_edge_shapes(gpu, shape):
     """Partial output tiles in both dimensions, a single token, K = 64."""
     y, exact, bound = run_gemm(gpu, *shape, nb.INT4)
     assert np.all(np.abs(y - exact) <= bound)
+
+
+@pytest.mark.parametrize("shape", [(32000, 2048, 512), (20000, 2048, 300)],
+                         ids=lambda s: f"{s[0]}x{s[1]}xM{s[2]}")
+def test_gemm_sm_pairs(gpu, shape):
+    """Several waves of 256-column tiles with more than 128 tokens: the
+    SM-pair form (256 x 256 tiles over two CTAs).  The second shape has a
+    partial 256-row tile (rows 256..299 of 512) and a partial last column
+    tile (20000 = 78 x 256 + 32)."""
+    y, exact, bound = run_gemm(gpu, *shape, nb.INT4)
+    assert np.all(np.isfinite(y))
+    err = np.abs(y - exact)
+    assert np.all(err <= bound), f"max excess {float((err - bound).max()):.3e}"
