@@ -142,8 +142,8 @@ struct Shared {
  * words per phase occurrence: phase id, the global timer at entry (1), and
  * SM clock stamps at entry (6), inputs staged (2), activation ready (3),
  * digits ready (4), weights consumed (5) and exit (7); sub-steps: the
- * finish's red.adds issued (8) and its fence passed (9), the exported and
- * the other gate/up tiles consumed (10, 11), the SwiGLU outputs complete
+ * finish's red.adds issued (8) and its fence passed (9), the gate/up tiles
+ * consumed (11), the SwiGLU outputs complete
  * (12), and the key/value fence passed (13). */
 struct Trace {
     unsigned long long *rec = nullptr;
@@ -788,12 +788,15 @@ __device__ bool phase_attwo(const Shared &s, const MkParams &p, Trace &tr, Curso
  * block in units of kDownUnitPairs row-tile pairs.  CTA c takes the
  * contiguous unit range [u0, u1) of the nbf U units.  A block's Wdown
  * units need all 32 SwiGLU outputs of the block, so gate/up tiles whose
- * block's Wdown is (partly) owned by a later CTA are "exported": computed
- * first and published as tagged values; only the first Wdown block of a
- * range can "import" tiles computed by earlier CTAs. */
+ * block's Wdown is (partly) owned by a later CTA are "exported": published
+ * as tagged values; only the first Wdown block of a range can "import"
+ * tiles computed by earlier CTAs.  The gate/up tiles are consumed as one
+ * run in tile order (measured: one run with its exported tiles last beats
+ * an exported-first run followed by the rest, 1,945 against 1,938 decode
+ * tok/s, since each run pays its own start-up, barrier and epilogue). */
 struct GdPlan {
     int gu_lo, gu_hi; /* gate/up row tiles [gu_lo, gu_hi) */
-    int ex_lo;        /* exported tiles [ex_lo, gu_hi) (run first) */
+    int ex_lo;        /* exported tiles [ex_lo, gu_hi) */
     int d_lo, d_hi;   /* Wdown units [d_lo, d_hi) (block d / du, part d % du) */
     int du;           /* Wdown units per block */
     int db_lo, nd;    /* Wdown blocks db_lo .. db_lo + nd - 1 (digit slots) */
@@ -823,11 +826,11 @@ __device__ __forceinline__ GdPlan gd_plan(const MkParams &p, int c) {
     return g;
 }
 
-/* GUDOWN (hB = hA + Wdown silu(gate) * up) over this CTA's work units: the
- * exported gate/up tiles, the other gate/up tiles, SwiGLU
- * (src/quant_model.cpp:197-198) into shared memory (and, for exported
- * tiles, into the tagged act vector), then its Wdown units, plus its share
- * of the residual rows, added into step 2 (i L + l) + 1. */
+/* GUDOWN (hB = hA + Wdown silu(gate) * up) over this CTA's work units: its
+ * gate/up tiles, SwiGLU (src/quant_model.cpp:197-198) into shared memory
+ * (and, for exported tiles, into the tagged act vector), then its Wdown
+ * units, plus its share of the residual rows, added into step 2 (i L + l)
+ * + 1. */
 template <int TYPE, int STAGES>
 __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                              RowReduce &rr, int i, int l) {
@@ -886,23 +889,13 @@ __device__ bool phase_gudown(const Shared &s, const MkParams &p, Trace &tr, Curs
         }
     };
     bool ok = true;
-    if (g.gu_hi > g.ex_lo) {
-        t_first = g.ex_lo;
-        const TileRun ex{L.gu + size_t(g.ex_lo) * p.nb_dim * TB,
-                         L.gu_s + size_t(g.ex_lo) * p.nb_dim * 16,
-                         (g.gu_hi - g.ex_lo) * p.nb_dim, p.nb_dim};
-        ok = consume_run<TYPE, W, STAGES>(s.ring, ex, cur, s.dig, s.fac, rr, w, kBar, epi,
-                                          tr.wait_acc());
-    }
-    tr.mark(10);
-    if (g.ex_lo > g.gu_lo) {
+    if (g.gu_hi > g.gu_lo) {
         t_first = g.gu_lo;
-        const TileRun rest{L.gu + size_t(g.gu_lo) * p.nb_dim * TB,
-                           L.gu_s + size_t(g.gu_lo) * p.nb_dim * 16,
-                           (g.ex_lo - g.gu_lo) * p.nb_dim, p.nb_dim};
-        ok = consume_run<TYPE, W, STAGES>(s.ring, rest, cur, s.dig, s.fac, rr, w, kBar, epi,
-                                          tr.wait_acc()) &&
-             ok;
+        const TileRun gu{L.gu + size_t(g.gu_lo) * p.nb_dim * TB,
+                         L.gu_s + size_t(g.gu_lo) * p.nb_dim * 16,
+                         (g.gu_hi - g.gu_lo) * p.nb_dim, p.nb_dim};
+        ok = consume_run<TYPE, W, STAGES>(s.ring, gu, cur, s.dig, s.fac, rr, w, kBar, epi,
+                                          tr.wait_acc());
     }
     tr.mark(11);
     cbar(); /* every SwiGLU output written; the gate/up digits are free */
@@ -1074,20 +1067,14 @@ __device__ void producer(const Shared &s, const MkParams &p) {
                     return;
             }
             if (c < p.count_gd) {
-                /* the consumer's order: exported gate/up tiles, the other
-                 * gate/up tiles, then the Wdown units */
+                /* the consumer's order: the gate/up tiles, then the Wdown
+                 * units */
                 const GdPlan g = gd_plan(p, c);
-                if (g.gu_hi > g.ex_lo &&
-                    !produce_run_c<TYPE, STAGES>(s.ring,
-                        TileRun{L.gu + size_t(g.ex_lo) * p.nb_dim * TB,
-                                L.gu_s + size_t(g.ex_lo) * p.nb_dim * 16,
-                                (g.gu_hi - g.ex_lo) * p.nb_dim, p.nb_dim}, cur))
-                    return;
-                if (g.ex_lo > g.gu_lo &&
+                if (g.gu_hi > g.gu_lo &&
                     !produce_run_c<TYPE, STAGES>(s.ring,
                         TileRun{L.gu + size_t(g.gu_lo) * p.nb_dim * TB,
                                 L.gu_s + size_t(g.gu_lo) * p.nb_dim * 16,
-                                (g.ex_lo - g.gu_lo) * p.nb_dim, p.nb_dim}, cur))
+                                (g.gu_hi - g.gu_lo) * p.nb_dim, p.nb_dim}, cur))
                     return;
                 for (int d = g.d_lo; d < g.d_hi; d++) {
                     const int b = d / g.du, q0 = (d - b * g.du) * kDownUnitPairs;
