@@ -529,7 +529,7 @@ def run_batch_tp(args, rank, world, local):
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
 # capture summarised in profiles/decode_mk_tinyllama_int4.md
-NCU_TRAFFIC: dict = {"tinyllama-int4": 15_659_737_000 + 12_164_096}
+NCU_TRAFFIC: dict = {"tinyllama-int4": 15_657_720_320 + 11_981_568}
 
 QMATVEC_SHAPES = [(2048, 2048), (5632, 2048), (2048, 5632), (32000, 2048)]
 
