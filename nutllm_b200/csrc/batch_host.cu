@@ -663,9 +663,9 @@ void prefill(nut_batch &b, int n) {
                                           b.heads_r, b.kvh_r, b.hd, b.kcache, b.vcache, l,
                                           b.max_seq, s, M, n, s0),
                        "rope");
-            cuda_check(nut::attention_batch(b.pf_qkv, b.B, b.nqkv, b.pos, b.kcache, b.vcache, l,
-                                            b.heads_r, b.kvh_r, b.hd, b.max_seq, b.kp_ctx,
-                                            b.pf_ctx16, s, M, n, s0),
+            cuda_check(nut::attention_prefill(b.pf_qkv, n, cs, b.nqkv, s0, b.B, 0, b.kcache,
+                                              b.vcache, l, b.heads_r, b.kvh_r, b.hd, b.max_seq,
+                                              b.kp_ctx, b.pf_ctx16, true, s),
                        "attention");
             proj(b, b.pf_ctx16, L.wo, L.wo4, dim, b.kp_ctx, b.pf_part, M);
             if (b.world > 1)

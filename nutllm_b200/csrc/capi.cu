@@ -746,10 +746,12 @@ void prefill_batched(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n)
                                      int(c.heads), int(m->kv_heads), int(c.head_dim), dim, kvd,
                                      kv->keys, kv->values, int(l), int(c.max_seq), s),
                    "rope");
-        cuda_check(nut::attention_rows(kv->pf_qkv, M, nqkv, 0, kv->keys, kv->values, int(l),
-                                       int(c.heads), int(m->kv_heads), int(c.head_dim), dim,
-                                       int(c.max_seq), kp_dim, kv->pf_ctx, s),
+        cuda_check(nut::attention_prefill(kv->pf_qkv, M, 1, nqkv, 0, 1, 0, kv->keys, kv->values,
+                                          int(l), int(c.heads), int(m->kv_heads),
+                                          int(c.head_dim), int(c.max_seq), kp_dim, kv->pf_ctx,
+                                          false, s),
                    "attention");
+        cuda_check(nut::zero_tail(kv->pf_ctx, M, dim, kp_dim, s), "attention");
         gemm(kv->pf_ctx, L.wo, B.wo, dim, kp_dim, kv->pf_h, true);
         cuda_check(nut::rmsnorm_rows(kv->pf_h, m->ffn_norms + l * dim, M, dim, kp_dim, kv->pf_x, s),
                    "rmsnorm");
@@ -787,7 +789,11 @@ void upload_rope(nut_model *m) {
 }
 
 bool use_batched_prefill(const nut_model *m, int64_t n) {
-    return m->mk && m->prefill_min > 0 && n >= m->prefill_min;
+    const nut_config &c = m->cfg;
+    const int kvd = int(m->kv_heads * c.head_dim), nqkv = int(c.dim) + 2 * kvd;
+    return m->mk && m->prefill_min > 0 && n >= m->prefill_min &&
+           nut::attention_prefill_supported(int(c.heads), int(m->kv_heads), int(c.head_dim),
+                                            nqkv);
 }
 
 } // namespace

@@ -11,9 +11,10 @@
  *   rope_kv_rows      RoPE on the q and k rows in place (the reference's
  *                     unfused products, src/quant_model.cpp:26-37) and the
  *                     k, v rows appended to the KV cache
- *   attention_rows    causal GQA attention of every (token, head)
- *                     (attention_step, src/quant_model.cpp:68-105), context
- *                     rounded to fp16 for the output projection
+ *   attention_prefill causal GQA attention of every (token, head)
+ *                     (attention_step, src/quant_model.cpp:68-105) in tiles
+ *                     that share their keys and values, context rounded to
+ *                     fp16 for the output projection
  *   swiglu_rows       a = fp16(silu(gate) * up) (src/ops.cpp:136-138) from the
  *                     gate/up GEMM's rows interleaved in groups of 8
  * fp16 conversions round to nearest and saturate at +-65504.
@@ -100,67 +101,204 @@ __global__ void rope_kv_rows_kernel(float *qkv, int M, int ldq, int start, const
     vcache[((size_t(layer) * kv_heads + h) * max_seq + pos) * hd + d] = row[dim + kvd + e];
 }
 
-/* One warp per (token m, head h); 4 warps per CTA.  Positions 0 .. start+m:
- * scores (a lane per position) into the warp's shared buffer, max and
- * exp-sum by shuffles, then the context with each lane owning dims lane,
- * lane + 32, ... */
-constexpr int kAttWarps = 4;
+/* Causal attention of the prompt rows, tiled (attention_step,
+ * src/quant_model.cpp:68-105, for every prompt token and head at once).
+ *
+ * CTA (tile, kv head g, sequence) owns kTileRows (token, head) rows: the
+ * G = heads / kv_heads query heads of group g for QT = kTileRows / G
+ * consecutive tokens, i.e. every row of the tile reads the same keys and
+ * values.  Those are staged once per CTA, kChunk positions at a time, in a
+ * double-buffered shared-memory ring (cp.async), and used by all 64 rows;
+ * the previous kernel (one warp per row) read each key and value row from
+ * L2 once per (token, head).  Warp w takes rows 8 w .. 8 w + 7:
+ *   scores  lane j holds position c0 + j of the chunk for the warp's 8
+ *           rows (key rows padded to hd + 1 floats: conflict-free; query
+ *           rows broadcast as float4);
+ *   softmax online per row: chunk maximum by shuffles, the running
+ *           maximum, exp weights (0 past the row's own position), the
+ *           lane's share of the exp sum, the context rescaled;
+ *   context lane owns dims lane, lane + 32, ... (DPL of them), weights
+ *           broadcast from the warp's slice of shared memory.
+ * After the last chunk the exp sums are reduced across lanes and the
+ * context row is divided by it and rounded to fp16.  fp32 throughout; the
+ * summation order differs from the reference's double sums only by
+ * rounding.  Tiles with the longest histories are scheduled first. */
+constexpr int kTileRows = 64;
+constexpr int kTileWarps = 8;
+constexpr int kWarpRows = kTileRows / kTileWarps; /* 8 */
+constexpr int kChunk = 32;
 
-__global__ void __launch_bounds__(kAttWarps * 32)
-attention_rows_kernel(const float *qkv, int M, int ldq, int start, const float *kcache,
-                      const float *vcache, int layer, int heads, int kv_heads, int hd, int dim,
-                      int max_seq, int Kp, __half *ctx) {
-    extern __shared__ float att_smem[];
+__device__ __forceinline__ void cp_async4(float *dst, const float *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async16(float *dst, const float *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <int DPL>
+__global__ void __launch_bounds__(kTileWarps * 32)
+attention_tiles_kernel(float *qkv, int ldq, int n, int seq0, int cache_seqs, int start,
+                       const float *kcache, const float *vcache, int layer, int heads,
+                       int kv_heads, int hd, int max_seq, int Kp, __half *ctx, int zero_q) {
+    extern __shared__ __align__(16) float att_smem[];
+    const int G = heads / kv_heads, QT = kTileRows / G;
+    const int ntiles = (n + QT - 1) / QT;
+    const int tile = ntiles - 1 - int(blockIdx.x); /* longest histories first */
+    const int g = int(blockIdx.y), sq = int(blockIdx.z);
+    const int t0 = tile * QT, nt = min(QT, n - t0), R = nt * G;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t item = int64_t(blockIdx.x) * kAttWarps + warp;
-    if (item >= int64_t(M) * heads)
-        return;
-    const int m = int(item / heads), h = int(item - int64_t(m) * heads);
-    const int npos = start + m + 1;
-    float *q = att_smem + size_t(warp) * (hd + max_seq);
-    float *w = q + hd;
-    const float *qsrc = qkv + size_t(m) * ldq + h * hd;
-    for (int d = lane; d < hd; d += 32)
-        q[d] = qsrc[d];
-    __syncwarp();
-    const int g = h / (heads / kv_heads);
-    const size_t base = (size_t(layer) * kv_heads + g) * size_t(max_seq) * hd;
-    const float scale = 1.0f / sqrtf(float(hd));
-    float mx = -INFINITY;
-    for (int j = lane; j < npos; j += 32) {
-        const float *kj = kcache + base + size_t(j) * hd;
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-        int d = 0;
-        for (; d + 4 <= hd; d += 4) {
-            const float4 k4 = *reinterpret_cast<const float4 *>(kj + d);
-            a0 = fmaf(q[d], k4.x, a0);
-            a1 = fmaf(q[d + 1], k4.y, a1);
-            a2 = fmaf(q[d + 2], k4.z, a2);
-            a3 = fmaf(q[d + 3], k4.w, a3);
+    const int ldk = hd + 1;
+    float *Qs = att_smem;                       /* [kTileRows][hd] */
+    float *Ks = Qs + kTileRows * hd;            /* [2][kChunk][hd + 1] */
+    float *Vs = Ks + 2 * kChunk * ldk;          /* [2][kChunk][hd] */
+    float *Ps = Vs + 2 * kChunk * hd;           /* [kTileWarps][kWarpRows][kChunk] */
+    const size_t base =
+        ((size_t(layer) * cache_seqs + size_t(seq0 + sq)) * kv_heads + g) * size_t(max_seq) * hd;
+    /* positions 0 .. P - 1 cover every row of the tile */
+    const int P = start + t0 + nt, nch = (P + kChunk - 1) / kChunk;
+    auto stage = [&](int c) {
+        const int buf = c & 1, j0 = c * kChunk;
+        float *kd = Ks + buf * kChunk * ldk, *vd = Vs + buf * kChunk * hd;
+        /* rows past P repeat row P - 1 (finite values; their weights are 0) */
+        for (int i = threadIdx.x; i < kChunk * hd; i += kTileWarps * 32) {
+            const int jj = i / hd, d = i - jj * hd;
+            const int j = min(j0 + jj, P - 1);
+            cp_async4(kd + jj * ldk + d, kcache + base + size_t(j) * hd + d);
         }
-        for (; d < hd; d++)
-            a0 = fmaf(q[d], kj[d], a0);
-        const float sc = ((a0 + a1) + (a2 + a3)) * scale;
-        w[j] = sc;
-        mx = fmaxf(mx, sc);
+        for (int i = threadIdx.x; i < kChunk * hd / 4; i += kTileWarps * 32) {
+            const int jj = i / (hd / 4), d = (i - jj * (hd / 4)) * 4;
+            const int j = min(j0 + jj, P - 1);
+            cp_async16(vd + jj * hd + d, vcache + base + size_t(j) * hd + d);
+        }
+        cp_async_commit();
+    };
+    stage(0);
+    /* the tile's query rows (row i: token t0 + i / G, head g G + i % G) */
+    for (int i = threadIdx.x; i < kTileRows * hd / 4; i += kTileWarps * 32) {
+        const int r = i / (hd / 4), d = (i - r * (hd / 4)) * 4;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r < R) {
+            const int t = t0 + r / G, h = g * G + r % G;
+            float *src = qkv + (size_t(sq) * n + t) * ldq + h * hd + d;
+            v = *reinterpret_cast<const float4 *>(src);
+            if (zero_q) /* consumed: the next split-K GEMM adds into it */
+                *reinterpret_cast<float4 *>(src) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        *reinterpret_cast<float4 *>(Qs + r * hd + d) = v;
     }
-    mx = warp_max(mx);
-    float sum = 0.0f;
-    for (int j = lane; j < npos; j += 32) {
-        const float e = expf(w[j] - mx);
-        w[j] = e;
-        sum += e;
+    const float scale = 1.0f / sqrtf(float(hd));
+    const int r0 = warp * kWarpRows;
+    /* the last position any row of this warp attends to (-1: no live row) */
+    const int wmax = r0 < R ? start + t0 + min(R - 1, r0 + kWarpRows - 1) / G : -1;
+    float m[kWarpRows], l[kWarpRows], acc[kWarpRows][DPL];
+#pragma unroll
+    for (int r = 0; r < kWarpRows; r++) {
+        m[r] = -INFINITY;
+        l[r] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DPL; k++)
+            acc[r][k] = 0.0f;
     }
-    sum = warp_sum(sum);
-    __syncwarp();
-    const float inv = 1.0f / sum;
-    __half *out = ctx + size_t(m) * Kp + h * hd;
-    for (int d = lane; d < hd; d += 32) {
-        const float *vd = vcache + base + d;
-        float c = 0.0f;
-        for (int j = 0; j < npos; j++)
-            c = fmaf(w[j], vd[size_t(j) * hd], c);
-        out[d] = to_half_sat(c * inv);
+    float *pw = Ps + warp * kWarpRows * kChunk;
+    for (int c = 0; c < nch; c++) {
+        if (c + 1 < nch) {
+            stage(c + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int buf = c & 1, j = c * kChunk + lane;
+        if (c * kChunk <= wmax) {
+            const float *kr = Ks + buf * kChunk * ldk + lane * ldk;
+            float s[kWarpRows];
+#pragma unroll
+            for (int r = 0; r < kWarpRows; r++)
+                s[r] = 0.0f;
+            for (int d = 0; d < hd; d += 4) {
+                const float k0 = kr[d], k1 = kr[d + 1], k2 = kr[d + 2], k3 = kr[d + 3];
+#pragma unroll
+                for (int r = 0; r < kWarpRows; r++) {
+                    const float4 q = *reinterpret_cast<const float4 *>(Qs + (r0 + r) * hd + d);
+                    s[r] = fmaf(q.x, k0, s[r]);
+                    s[r] = fmaf(q.y, k1, s[r]);
+                    s[r] = fmaf(q.z, k2, s[r]);
+                    s[r] = fmaf(q.w, k3, s[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kWarpRows; r++) {
+                const int row = r0 + r;
+                const bool live = row < R && j <= start + t0 + row / G;
+                const float sc = live ? s[r] * scale : -INFINITY;
+                const float mn = fmaxf(m[r], warp_max(sc));
+                float p = 0.0f, corr = 1.0f;
+                if (mn != -INFINITY) {
+                    corr = expf(m[r] - mn); /* 0 while m is still -inf */
+                    p = expf(sc - mn);      /* 0 past the row's position */
+                }
+                l[r] = fmaf(l[r], corr, p);
+#pragma unroll
+                for (int k = 0; k < DPL; k++)
+                    acc[r][k] *= corr;
+                m[r] = mn;
+                pw[r * kChunk + lane] = p;
+            }
+            __syncwarp();
+            const float *vb = Vs + buf * kChunk * hd;
+            for (int jj = 0; jj < kChunk; jj += 4) {
+                float v[4][DPL];
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+#pragma unroll
+                    for (int k = 0; k < DPL; k++) {
+                        const int d = lane + 32 * k;
+                        v[u][k] = d < hd ? vb[(jj + u) * hd + d] : 0.0f;
+                    }
+#pragma unroll
+                for (int r = 0; r < kWarpRows; r++) {
+                    const float4 p4 = *reinterpret_cast<const float4 *>(pw + r * kChunk + jj);
+#pragma unroll
+                    for (int k = 0; k < DPL; k++) {
+                        acc[r][k] = fmaf(p4.x, v[0][k], acc[r][k]);
+                        acc[r][k] = fmaf(p4.y, v[1][k], acc[r][k]);
+                        acc[r][k] = fmaf(p4.z, v[2][k], acc[r][k]);
+                        acc[r][k] = fmaf(p4.w, v[3][k], acc[r][k]);
+                    }
+                }
+            }
+            __syncwarp(); /* the weights are rewritten by the next chunk */
+        }
+        __syncthreads(); /* buffer c & 1 is restaged by chunk c + 2 */
+    }
+#pragma unroll
+    for (int r = 0; r < kWarpRows; r++) {
+        const int row = r0 + r;
+        const float total = warp_sum(l[r]);
+        if (row >= R)
+            continue;
+        const int t = t0 + row / G, h = g * G + row % G;
+        __half *out = ctx + (size_t(sq) * n + t) * Kp + h * hd;
+        const float inv = 1.0f / total;
+#pragma unroll
+        for (int k = 0; k < DPL; k++) {
+            const int d = lane + 32 * k;
+            if (d < hd)
+                out[d] = to_half_sat(acc[r][k] * inv);
+        }
     }
 }
 
@@ -225,25 +363,73 @@ cudaError_t rope_kv_rows(float *qkv, int M, int ldq, int start, const float *rop
     return cudaGetLastError();
 }
 
-size_t attention_rows_smem(int hd, int max_seq) {
-    return size_t(kAttWarps) * size_t(hd + max_seq) * sizeof(float);
+bool attention_prefill_supported(int heads, int kv_heads, int hd, int ldq) {
+    if (kv_heads <= 0 || heads % kv_heads != 0)
+        return false;
+    const int G = heads / kv_heads;
+    return G <= kTileRows && kTileRows % G == 0 && hd > 0 && hd % 4 == 0 && hd <= 256 &&
+           ldq % 4 == 0;
 }
 
-cudaError_t attention_rows(const float *qkv, int M, int ldq, int start, const float *kcache,
-                           const float *vcache, int layer, int heads, int kv_heads, int hd,
-                           int dim, int max_seq, int Kp, uint16_t *ctx, cudaStream_t s) {
-    const size_t smem = attention_rows_smem(hd, max_seq);
-    cudaError_t e = cudaFuncSetAttribute(attention_rows_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+template <int DPL>
+cudaError_t launch_tiles(float *qkv, int n, int nseq, int ldq, int seq0, int cache_seqs,
+                         int start, const float *kcache, const float *vcache, int layer,
+                         int heads, int kv_heads, int hd, int max_seq, int Kp, __half *ctx,
+                         int zero_q, cudaStream_t s) {
+    const size_t smem = (size_t(kTileRows) * hd + size_t(2 * kChunk) * (hd + 1) +
+                         size_t(2 * kChunk) * hd + size_t(kTileRows) * kChunk) *
+                        sizeof(float);
+    auto k = attention_tiles_kernel<DPL>;
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess)
         return e;
+    const int QT = kTileRows / (heads / kv_heads);
+    const dim3 grid((n + QT - 1) / QT, kv_heads, nseq);
+    k<<<grid, kTileWarps * 32, smem, s>>>(qkv, ldq, n, seq0, cache_seqs, start, kcache, vcache,
+                                          layer, heads, kv_heads, hd, max_seq, Kp, ctx, zero_q);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t attention_prefill(float *qkv, int n, int nseq, int ldq, int seq0, int cache_seqs,
+                              int start, const float *kcache, const float *vcache, int layer,
+                              int heads, int kv_heads, int hd, int max_seq, int Kp,
+                              uint16_t *ctx, bool zero_q, cudaStream_t s) {
+    if (!attention_prefill_supported(heads, kv_heads, hd, ldq) || n <= 0 || nseq <= 0 ||
+        nseq > 65535 || start < 0 || start + n > max_seq)
+        return cudaErrorInvalidValue;
     auto *c = reinterpret_cast<__half *>(ctx);
-    const int64_t items = int64_t(M) * heads;
-    attention_rows_kernel<<<blocks_for(items, kAttWarps), kAttWarps * 32, smem, s>>>(
-        qkv, M, ldq, start, kcache, vcache, layer, heads, kv_heads, hd, dim, max_seq, Kp, c);
-    zero_tail_kernel<<<blocks_for(int64_t(M) * (Kp > dim ? Kp - dim : 1), 256), 256, 0, s>>>(
-        c, M, dim, Kp);
-    count_launches(2);
+    const int zq = zero_q ? 1 : 0;
+    switch ((hd + 31) / 32) {
+    case 1:
+        return launch_tiles<1>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
+                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 2:
+        return launch_tiles<2>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
+                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 3:
+        return launch_tiles<3>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
+                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 4:
+        return launch_tiles<4>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
+                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 5:
+    case 6:
+        return launch_tiles<6>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
+                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    default:
+        return launch_tiles<8>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
+                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    }
+}
+
+cudaError_t zero_tail(uint16_t *x, int M, int dim, int Kp, cudaStream_t s) {
+    if (Kp <= dim)
+        return cudaSuccess;
+    zero_tail_kernel<<<blocks_for(int64_t(M) * (Kp - dim), 256), 256, 0, s>>>(
+        reinterpret_cast<__half *>(x), M, dim, Kp);
+    count_launches(1);
     return cudaGetLastError();
 }
 

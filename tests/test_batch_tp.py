@@ -297,7 +297,13 @@ def test_gemm_prefill_matches_oracle(gpu, orc, qtype):
         assert np.all(d <= ATOL + RTOL * np.abs(want)), (b, float(d.max()))
         dev.append(d)
     assert float(np.median(np.concatenate(dev))) <= MEDIAN
-    assert np.allclose(logits, logits_pp, rtol=1e-3, atol=1e-4)
+    # The two prompt paths run different attention kernels (tiled prefill
+    # vs one row per pass), so their fp32 contexts differ by rounding; the
+    # fp16 rounding of the contexts and activations carries that into the
+    # logits at ~5e-4 (measured 2.4e-4 .. 4.7e-4 on a B200, with each path
+    # ~8e-4 from the oracle).  The agreement bound is that noise level, 30x
+    # inside the oracle bound, and the ids must be identical.
+    assert np.allclose(logits, logits_pp, rtol=1e-3, atol=1e-3)
     assert ids.tolist() == ids_pp.tolist()
 
 
