@@ -170,16 +170,14 @@ template <int CPL>
 __global__ void __launch_bounds__(kAttWarps * 32)
 attention_batch_kernel(const float *qkv, int B, int ldq, const int *pos_p, const float *kcache,
                        const float *vcache, int layer, int heads, int kv_heads, int hd,
-                       int max_seq, int Kp, __half *ctx, int pf_n, int seq0) {
+                       int max_seq, int Kp, __half *ctx) {
     extern __shared__ float sm[];
-    /* decode: row b is sequence b at *pos; prefill: row b is position
-     * b % pf_n of sequence seq0 + b / pf_n (causal: positions 0..that) */
+    /* row b is sequence b at *pos */
     const int b = blockIdx.x / heads, h = blockIdx.x - b * heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int npos = (pf_n > 0 ? b % pf_n : *pos_p) + 1;
-    const int sq = pf_n > 0 ? seq0 + b / pf_n : b;
+    const int npos = *pos_p + 1;
     const int g = h / (heads / kv_heads);
-    const size_t base = ((size_t(layer) * B + sq) * kv_heads + g) * size_t(max_seq) * hd;
+    const size_t base = ((size_t(layer) * B + b) * kv_heads + g) * size_t(max_seq) * hd;
     const int lpr = hd / 4 / CPL;                    /* lanes per row (a power of two) */
     const int rpi = 32 / lpr;                        /* rows per warp step */
     const int sub = lane / lpr, li = lane - sub * lpr;
@@ -505,7 +503,7 @@ template <int CPL>
 cudaError_t launch_attention(const float *qkv, int rows, int B, int ldq, const int *pos,
                              const float *kcache, const float *vcache, int layer, int heads,
                              int kv_heads, int hd, int max_seq, int Kp, __half *ctx, int lpr,
-                             int pf_n, int seq0, cudaStream_t s) {
+                             cudaStream_t s) {
     const size_t nst = size_t(kAttWarps) * size_t(32 / lpr);
     const size_t smem = (size_t(hd) * (1 + nst) + 2 * nst) * sizeof(float);
     auto k = attention_batch_kernel<CPL>;
@@ -516,16 +514,15 @@ cudaError_t launch_attention(const float *qkv, int rows, int B, int ldq, const i
             return e;
     }
     k<<<rows * heads, kAttWarps * 32, smem, s>>>(qkv, B, ldq, pos, kcache, vcache, layer, heads,
-                                                 kv_heads, hd, max_seq, Kp, ctx, pf_n, seq0);
+                                                 kv_heads, hd, max_seq, Kp, ctx);
     return cudaGetLastError();
 }
 
 cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
                             const float *kcache, const float *vcache, int layer, int heads,
                             int kv_heads, int hd, int max_seq, int Kp, uint16_t *ctx,
-                            cudaStream_t s, int rows, int pf_n, int seq0) {
-    if (rows <= 0)
-        rows = B;
+                            cudaStream_t s) {
+    const int rows = B;
     /* float4 rows over lpr lanes (the largest power of two dividing
      * hd / 4, at most 32), CPL float4 per lane */
     if (hd % 4 != 0 || hd <= 0)
@@ -539,19 +536,19 @@ cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
     switch (cpl) {
     case 1:
         e = launch_attention<1>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
-                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
+                                kv_heads, hd, max_seq, Kp, c16, lpr, s);
         break;
     case 2:
         e = launch_attention<2>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
-                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
+                                kv_heads, hd, max_seq, Kp, c16, lpr, s);
         break;
     case 3:
         e = launch_attention<3>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
-                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
+                                kv_heads, hd, max_seq, Kp, c16, lpr, s);
         break;
     case 4:
         e = launch_attention<4>(qkv, rows, B, ldq, pos, kcache, vcache, layer, heads,
-                                kv_heads, hd, max_seq, Kp, c16, lpr, pf_n, seq0, s);
+                                kv_heads, hd, max_seq, Kp, c16, lpr, s);
         break;
     default:
         return cudaErrorInvalidValue;

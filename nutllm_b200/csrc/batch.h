@@ -26,6 +26,9 @@ cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const floa
                           const float *rope_sin, int heads, int kv_heads, int hd,
                           float *kcache, float *vcache, int layer, int max_seq,
                           cudaStream_t s, int rows = 0, int pf_n = 0, int seq0 = 0);
+/* Prefill form (rows > 0, pf_n > 0): qkv row m is position
+ * m % pf_n of sequence seq0 + m / pf_n (B is still the batch the cache
+ * holds).  The prefill's causal attention is attention_prefill (prefill.h). */
 
 /* Attention of every (sequence, head) at position *pos over cached
  * positions 0 .. *pos (attention_step, src/quant_model.cpp:68-105: scores
@@ -35,10 +38,7 @@ cudaError_t rope_kv_batch(float *qkv, int B, int ldq, const int *pos, const floa
 cudaError_t attention_batch(const float *qkv, int B, int ldq, const int *pos,
                             const float *kcache, const float *vcache, int layer, int heads,
                             int kv_heads, int hd, int max_seq, int Kp, uint16_t *ctx,
-                            cudaStream_t s, int rows = 0, int pf_n = 0, int seq0 = 0);
-/* Prefill form of both (rows > 0, pf_n > 0): qkv row m is position m % pf_n
- * of sequence seq0 + m / pf_n (B is still the batch the cache holds); the
- * attention is causal over that sequence's positions 0 .. m % pf_n. */
+                            cudaStream_t s);
 
 /* Per row b: the first-index argmax of logits[b][0, V) as a 64-bit key
  * (order-preserving value bits << 32 | ~(v0 + index)), so that the maximum
