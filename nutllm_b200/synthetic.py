@@ -124,3 +124,26 @@ def algorithmic_generation_bytes(c: Config, qtype: int, n_prompt: int,
         total += algorithmic_decode_bytes(
             c, qtype, pos, n_prompt - 1 <= pos <= n_prompt + steps - 2)
     return total
+
+
+# Prompts of at least this many tokens are prefilled as GEMMs by default
+# (the library's nut_model_set_prefill_threshold default).
+GEMM_PREFILL_MIN = 64
+
+
+def algorithmic_decode_launch_bytes(c: Config, qtype: int, n_prompt: int,
+                                    steps: int) -> int:
+    """Bytes of the persistent decode launch of one greedy generation.  With
+    a prompt of GEMM_PREFILL_MIN tokens or more the prompt goes through the
+    GEMM prefill first, and the launch reads the classifier for the prompt's
+    last hidden state and then runs the passes at positions n_prompt ..
+    n_prompt+steps-1 (logits after all but the last); shorter prompts run
+    every pass in the launch (algorithmic_generation_bytes)."""
+    if n_prompt < GEMM_PREFILL_MIN:
+        return algorithmic_generation_bytes(c, qtype, n_prompt, steps)
+    last = n_prompt - 1
+    total = (algorithmic_decode_bytes(c, qtype, last, True)
+             - algorithmic_decode_bytes(c, qtype, last, False))
+    for pos in range(n_prompt, n_prompt + steps):
+        total += algorithmic_decode_bytes(c, qtype, pos, pos <= n_prompt + steps - 2)
+    return total
