@@ -612,6 +612,7 @@ void run_mk(nut_model *m, nut_kv *kv, const int32_t *tokens, int64_t n_prompt,
     p.gd_unit = nut::ffn_units_per_block(p.rt_down_pairs);
     p.gd_total = p.nbf * p.gd_unit;
     p.act = kv->tagged + dim + 2 * kvd;
+    p.xchg = p.act + ffn;
     p.prompt = kv->mk_prompt;
     p.n_prompt = int(n_prompt);
     p.n_tokens = int(n_tokens);
@@ -1296,7 +1297,10 @@ nut_status nut_kv_create(nut_model *model, nut_kv **out) {
         for (auto &e : kv->ev)
             cuda_check(cudaEventCreate(&e), "create event");
         if (model->mk) {
-            kv->tagged_count = size_t(c.dim) + 2 * kvd + size_t(c.ffn_dim);
+            /* q | k | v, the SwiGLU outputs, and one partial attention
+             * state (hd + 2 elements) per CTA */
+            kv->tagged_count = size_t(c.dim) + 2 * kvd + size_t(c.ffn_dim) +
+                               size_t(model->sms) * size_t(c.head_dim + 2);
             kv->mk_acc = dev_alloc<float>(size_t(nut::kAccSlots) * c.dim, "alloc accumulators");
             kv->mk_cnt = dev_alloc<unsigned int>(nut::kAccSlots, "alloc step counters");
             kv->tagged = dev_alloc<nut::Tagged>(kv->tagged_count, "alloc tagged");

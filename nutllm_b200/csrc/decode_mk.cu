@@ -46,6 +46,7 @@
  * atomicMax key per token plus a count of CTAs that finished the
  * classifier.  Every wait is bounded by limit_ns and reports into *error.
  */
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 
@@ -89,6 +90,7 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
                  "l"(src)
                  : "memory");
 }
+
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
@@ -705,12 +707,251 @@ __device__ bool head_context(const Shared &s, const MkParams &p, int l, int h, i
     return true;
 }
 
+/* ---- attention of long histories (the LONG kernel) ---------------------
+
+   Generations whose positions exceed one attention chunk run a second
+   instantiation of the kernel with the functions below; the others keep
+   the single-chunk code above unchanged (the persistent kernel's speed
+   depends on its register allocation and code layout, measured: folding
+   both into one instantiation cost 2-12 % at short contexts). */
+
+/* Per-head attention scratch of the LONG kernel.  Key and value rows
+ * are padded to hd + 4 floats: 16-byte rows for the bulk of the copies,
+ * and a float4 read by the 8 lanes of a quarter-warp (8 consecutive
+ * positions) touches 8 distinct 16-byte bank groups. */
+struct LongScratch {
+    float *q;        /* [hd] */
+    float *wm, *wl;  /* [W] per-warp maximum and exp sum of a chunk */
+    float *part;     /* [W][hd] per-warp partial contexts of a chunk */
+    float *cur;      /* [2 hd] current k and v while pos is past the chunk */
+    float *w;        /* [CH] exp weights */
+    float *Kt, *Vt;  /* [CH][hd + 4] */
+    int CH, ld;
+    __device__ LongScratch(const Shared &s, const MkParams &p) {
+        const int hd = p.hd;
+        ld = hd + 4;
+        q = s.uni;
+        wm = q + hd;
+        wl = wm + W;
+        part = wl + W;
+        cur = part + W * hd;
+        w = cur + 2 * hd;
+        const int used = hd + 2 * W + W * hd + 2 * hd + 3; /* + padding of w */
+        CH = (p.union_floats - used) / (2 * ld + 1);
+        if (CH > NT)
+            CH = NT;
+        Kt = w + ((CH + 3) & ~3);
+        Vt = Kt + CH * ld;
+    }
+};
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+
+/* Asynchronous copies of cached keys and values of kv head g, positions
+ * [p0, p0 + n) other than `pos`, into the tiles (16 bytes per copy; hd is a
+ * multiple of 4). */
+__device__ __forceinline__ void long_fetch(const LongScratch &t, const MkParams &p, int l,
+                                           int g, int p0, int n, int pos) {
+    const int hd = p.hd, q4 = hd / 4;
+    const size_t base = (size_t(l) * p.kv_heads + g) * size_t(p.max_seq) * hd;
+    for (int idx = threadIdx.x; idx < n * q4; idx += NT) {
+        const int j = idx / q4, d = (idx - j * q4) * 4, q = p0 + j;
+        if (q == pos)
+            continue;
+        const size_t off = base + size_t(q) * hd + d;
+        cp_async16(t.Kt + j * t.ld + d, p.kcache + off);
+        cp_async16(t.Vt + j * t.ld + d, p.vcache + off);
+    }
+}
+
+/* Partial attention of query head h at position pos (attention_step,
+ * src/quant_model.cpp:68-105: scores q.k / sqrt(hd), exp(score - max),
+ * weights / total, context) over positions lo .. hi of the history (hi <=
+ * pos), in chunks of CH, with q, and the current k and v when hi == pos,
+ * taken from the tagged q|k|v vector (tag tag_in).  Threads d < hd return
+ * the running maximum m, the exp sum `total` and the unnormalised context
+ * `acc` of dim d (context = acc / total).  Within a chunk warp w takes
+ * positions 32 w .. 32 w + 31 (one per lane): scores, the warp's maximum
+ * and exp sum by shuffles, and its partial context (each lane owning dims
+ * lane, lane + 32, ...); threads d < hd then merge the warps' partials into
+ * the running state carried across chunks.  Collective. */
+__device__ bool head_partial(const Shared &s, const MkParams &p, int l, int h, int pos,
+                             uint32_t tag_in, int lo, int hi, float &m, float &total,
+                             float &acc) {
+    const int hd = p.hd, G = p.heads / p.kv_heads;
+    const float scale = 1.0f / sqrtf(float(hd));
+    const LongScratch t(s, p);
+    const int ld = t.ld;
+    const int g = h / G, lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+    /* history does not depend on this token: fetch it first */
+    long_fetch(t, p, l, g, lo, min(t.CH, hi + 1 - lo), pos);
+    /* q of head h and, when this range ends at pos, the current k, v of kv
+     * head g */
+    const bool has_cur = hi == pos;
+    if (threadIdx.x < 3 * hd) {
+        const int part = threadIdx.x / hd, d = threadIdx.x - part * hd;
+        if (part == 0 || has_cur) {
+            const int row = part == 0 ? h * hd + d : p.dim + (part - 1) * p.kvd + g * hd + d;
+            float v;
+            if (wait_tag<false>(p.qkv + row, tag_in, p.limit_ns, v)) {
+                if (part == 0)
+                    t.q[d] = v;
+                else if (pos - lo < t.CH)
+                    (part == 1 ? t.Kt : t.Vt)[(pos - lo) * ld + d] = v;
+                else
+                    t.cur[d + (part - 1) * hd] = v; /* kept for its chunk */
+            } else {
+                fatal(s, p, kErrTimeoutInput);
+            }
+        }
+    }
+    __threadfence(); /* acquire: the tags order the older cache rows */
+    if (!healthy(s)) {
+        cp_async_wait_all();
+        return false;
+    }
+    m = -INFINITY, total = 0.0f, acc = 0.0f; /* running state of dim threadIdx.x */
+    for (int p0 = lo; p0 <= hi; p0 += t.CH) {
+        const int n = min(t.CH, hi + 1 - p0);
+        if (p0 > lo) {
+            long_fetch(t, p, l, g, p0, n, pos);
+            if (pos >= p0 && pos < p0 + n && threadIdx.x < hd) {
+                t.Kt[(pos - p0) * ld + threadIdx.x] = t.cur[threadIdx.x];
+                t.Vt[(pos - p0) * ld + threadIdx.x] = t.cur[hd + threadIdx.x];
+            }
+        }
+        cp_async_wait_all();
+        cbar();
+        const int j0 = 32 * wi, j = j0 + lane;
+        if (j0 < n) {
+            float sc = -INFINITY;
+            if (j < n) {
+                const float4 *k4 = reinterpret_cast<const float4 *>(t.Kt + j * ld);
+                const float4 *q4 = reinterpret_cast<const float4 *>(t.q);
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                for (int d = 0; d < hd / 4; d++) {
+                    const float4 kk = k4[d], qq = q4[d];
+                    a0 = fmaf(qq.x, kk.x, a0);
+                    a1 = fmaf(qq.y, kk.y, a1);
+                    a2 = fmaf(qq.z, kk.z, a2);
+                    a3 = fmaf(qq.w, kk.w, a3);
+                }
+                sc = ((a0 + a1) + (a2 + a3)) * scale;
+            }
+            const float mw = warp_max(sc);
+            const float e = j < n ? expf(sc - mw) : 0.0f;
+            const float lw = warp_sum(e);
+            if (j < n)
+                t.w[j] = e;
+            __syncwarp();
+            const int jn = min(32, n - j0);
+            for (int d = lane; d < hd; d += 32) {
+                const float *vj = t.Vt + j0 * ld + d;
+                const float *ew = t.w + j0;
+                float c = 0.0f;
+                for (int k = 0; k < jn; k++)
+                    c = fmaf(ew[k], vj[k * ld], c);
+                t.part[wi * hd + d] = c;
+            }
+            if (lane == 0) {
+                t.wm[wi] = mw;
+                t.wl[wi] = lw;
+            }
+        }
+        cbar();
+        if (threadIdx.x < hd) {
+            const int nw = (n + 31) / 32;
+            float mc = m;
+            for (int k = 0; k < nw; k++)
+                mc = fmaxf(mc, t.wm[k]);
+            const float f0 = expf(m - mc);
+            float tn = total * f0, an = acc * f0;
+            for (int k = 0; k < nw; k++) {
+                const float f = expf(t.wm[k] - mc);
+                tn = fmaf(t.wl[k], f, tn);
+                an = fmaf(t.part[k * hd + threadIdx.x], f, an);
+            }
+            m = mc;
+            total = tn;
+            acc = an;
+        }
+        cbar(); /* tiles and partials are reused by the next chunk */
+    }
+    return true;
+}
+
+/* Whether the cpp CTAs of a block pair split head attention by positions
+ * at position pos: when the history needs more than one chunk, the pair's
+ * 64 columns lie inside one head (hd a multiple of 64), there is more than
+ * one CTA per pair, every share holds a position, and the merge's
+ * [cpp][hd + 2] states fit the key tile.  Every CTA decides the same. */
+__device__ __forceinline__ bool split_history(const Shared &s, const MkParams &p, int pos) {
+    const LongScratch t(s, p);
+    return p.cpp > 1 && p.hd % 64 == 0 && pos + 1 > t.CH && pos + 1 >= p.cpp &&
+           p.cpp * (p.hd + 2) <= t.CH * t.ld;
+}
+
+/* Combines the partial states of the cpp CTAs of block pair P (each over its
+ * share of the positions) into the head's context out[0, hd): this CTA's
+ * state (threads d < hd: m, total, acc) is published as tagged elements
+ * [acc[0..hd), m, total] in slot P cpp + part of p.xchg, the other CTAs'
+ * states are read as their tags arrive, and every CTA merges them in slot
+ * order (m = max m_k, total = sum total_k e^(m_k - m), context = sum acc_k
+ * e^(m_k - m) / total), so the pair's CTAs compute the same context.
+ * Collective. */
+__device__ bool merge_history(const Shared &s, const MkParams &p, int P, int part,
+                              uint32_t tag, float m, float total, float acc, float *out) {
+    const int hd = p.hd, E = hd + 2, cpp = p.cpp;
+    const LongScratch t(s, p);
+    float *X = t.Kt; /* [cpp][E]: the tiles are free after head_partial */
+    Tagged *mine = p.xchg + size_t(P * cpp + part) * E;
+    if (int(threadIdx.x) < hd) {
+        st_relaxed(mine + threadIdx.x, acc, tag);
+        X[part * E + threadIdx.x] = acc;
+        if (threadIdx.x == 0) {
+            st_relaxed(mine + hd, m, tag);
+            st_relaxed(mine + hd + 1, total, tag);
+            X[part * E + hd] = m;
+            X[part * E + hd + 1] = total;
+        }
+    }
+    for (int idx = threadIdx.x; idx < cpp * E; idx += NT) {
+        const int k = idx / E;
+        if (k == part)
+            continue;
+        float v;
+        if (wait_tag<false>(p.xchg + size_t(P * cpp) * E + idx, tag, p.limit_ns, v))
+            X[idx] = v;
+        else
+            fatal(s, p, kErrTimeoutInput);
+    }
+    if (!healthy(s))
+        return false;
+    if (int(threadIdx.x) < hd) {
+        float M = -INFINITY;
+        for (int k = 0; k < cpp; k++)
+            M = fmaxf(M, X[k * E + hd]);
+        float L = 0.0f, c = 0.0f;
+        for (int k = 0; k < cpp; k++) {
+            const float f = expf(X[k * E + hd] - M);
+            L = fmaf(X[k * E + hd + 1], f, L);
+            c = fmaf(X[k * E + threadIdx.x], f, c);
+        }
+        out[threadIdx.x] = c / L;
+    }
+    cbar(); /* X is reused by the next head */
+    return true;
+}
+
 /* ATTWO (hA = h + Wo ctx), split by K: CTA c < count_aw owns the block pair
  * P = c / cpp (ctx columns 64 P .. 64 P + 63) for share c mod cpp of Wo's
  * row tiles.  It computes the attention of every head those columns cover
  * (a head may be computed by several CTAs), multiplies its Wo tiles, adds
  * the residual rows when P == 0, and adds its rows into step 2 (i L + l). */
-template <int TYPE, int STAGES>
+template <int TYPE, int STAGES, bool LONG>
 __device__ bool phase_attwo(const Shared &s, const MkParams &p, Trace &tr, Cursor &cur,
                             int i, int l, int token, int pos) {
     const int c = blockIdx.x;
@@ -743,9 +984,34 @@ __device__ bool phase_attwo(const Shared &s, const MkParams &p, Trace &tr, Curso
     if (threadIdx.x < 64)
         xs[threadIdx.x] = 0.0f;
     const int h0 = e0 / p.hd, h1 = min(p.heads - 1, (e0 + 63) / p.hd);
+    /* LONG: past one chunk of history the pair's CTAs take equal shares of
+     * the positions and merge their partial states (h0 == h1 then) */
+    bool split = false;
+    int lo = 0, hi = pos;
+    if constexpr (LONG) {
+        split = split_history(s, p, pos);
+        if (split) {
+            lo = int(unsigned(pos + 1) * unsigned(part) / unsigned(p.cpp));
+            hi = int(unsigned(pos + 1) * unsigned(part + 1) / unsigned(p.cpp)) - 1;
+        }
+    }
     for (int h = h0; h <= h1; h++) {
-        if (!head_context(s, p, l, h, pos, tag_in, hc))
-            return false;
+        if constexpr (LONG) {
+            float m, total, acc;
+            if (!head_partial(s, p, l, h, pos, tag_in, lo, hi, m, total, acc))
+                return false;
+            if (split) {
+                if (!merge_history(s, p, P, part, tag_in, m, total, acc, hc))
+                    return false;
+            } else {
+                if (int(threadIdx.x) < p.hd)
+                    hc[threadIdx.x] = acc / total;
+                cbar();
+            }
+        } else {
+            if (!head_context(s, p, l, h, pos, tag_in, hc))
+                return false;
+        }
         if (threadIdx.x < 64) {
             const int e = e0 + threadIdx.x;
             if (e < p.dim && e / p.hd == h)
@@ -1106,7 +1372,7 @@ __device__ void producer(const Shared &s, const MkParams &p) {
     }
 }
 
-template <int TYPE, int STAGES>
+template <int TYPE, int STAGES, bool LONG>
 __global__ void __launch_bounds__(THREADS, 1) decode_mk_kernel(const MkParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve<STAGES>(smem, p);
@@ -1149,7 +1415,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_mk_kernel(const MkParams p)
             if (!ok)
                 break;
             tr.open(p, occ++, 1);
-            ok = phase_attwo<TYPE, STAGES>(s, p, tr, cur, i, l, token, pos);
+            ok = phase_attwo<TYPE, STAGES, LONG>(s, p, tr, cur, i, l, token, pos);
             tr.mark(7);
             if (!ok)
                 break;
@@ -1199,14 +1465,15 @@ size_t tail_smem(int stages, int dim) {
     return off + size_t(stages) * 16 + 64; /* barriers, and slack */
 }
 
-/* Per-head attention scratch floats for a chunk of `ch` positions. */
+/* Per-head attention scratch floats for a chunk of `ch` positions (mirrors
+ * HeadScratch). */
 size_t att_floats(int hd, int ch) {
-    return size_t(hd) * (3 + W) + 2 * W + size_t(ch) * (2 * size_t(hd + 1) + 1);
+    return size_t(hd) * (3 + W) + 2 * W + 3 + size_t(ch) * (2 * size_t(hd + 4) + 1);
 }
 
-template <int TYPE, int STAGES>
+template <int TYPE, int STAGES, bool LONG>
 cudaError_t launch_t(MkParams p, int sms, size_t smem, cudaStream_t stream) {
-    auto kernel = decode_mk_kernel<TYPE, STAGES>;
+    auto kernel = decode_mk_kernel<TYPE, STAGES, LONG>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(smem));
     if (e != cudaSuccess)
@@ -1231,7 +1498,7 @@ bool plan(int dim, int ffn, int hd, int nbmax, int max_smem, int &stages,
             continue;
         stages = st;
         union_bytes = avail;
-        chunk = int((avail / 4 - (size_t(hd) * (3 + W) + 2 * W)) / (2 * size_t(hd + 1) + 1));
+        chunk = int((avail / 4 - (size_t(hd) * (3 + W) + 2 * W + 3)) / (2 * size_t(hd + 4) + 1));
         return true;
     }
     return false;
@@ -1266,6 +1533,25 @@ bool mk_supported(int dim, int ffn, int kvd, int head_dim, int heads, int type,
                 chunk);
 }
 
+namespace {
+template <bool LONG>
+cudaError_t launch_type(const MkParams &p, int type, int stages, int sms, size_t smem,
+                        cudaStream_t stream) {
+    if (type == 1) {
+        if (stages == 8)
+            return launch_t<1, 8, LONG>(p, sms, smem, stream);
+        if (stages == 6)
+            return launch_t<1, 6, LONG>(p, sms, smem, stream);
+        return launch_t<1, 4, LONG>(p, sms, smem, stream);
+    }
+    if (stages == 8)
+        return launch_t<0, 8, LONG>(p, sms, smem, stream);
+    if (stages == 6)
+        return launch_t<0, 6, LONG>(p, sms, smem, stream);
+    return launch_t<0, 4, LONG>(p, sms, smem, stream);
+}
+} // namespace
+
 cudaError_t launch_decode_mk(const MkParams &pin, int type, int sms, cudaStream_t stream) {
     int dev = 0, max_smem = 0;
     cudaGetDevice(&dev);
@@ -1279,18 +1565,14 @@ cudaError_t launch_decode_mk(const MkParams &pin, int type, int sms, cudaStream_
     p.att_chunk = chunk;
     p.union_floats = int(ub / 4);
     const size_t smem = fixed_smem(stages, p.dim, p.ffn) + ub + tail_smem(stages, p.dim);
-    if (type == 1) {
-        if (stages == 8)
-            return launch_t<1, 8>(p, sms, smem, stream);
-        if (stages == 6)
-            return launch_t<1, 6>(p, sms, smem, stream);
-        return launch_t<1, 4>(p, sms, smem, stream);
-    }
-    if (stages == 8)
-        return launch_t<0, 8>(p, sms, smem, stream);
-    if (stages == 6)
-        return launch_t<0, 6>(p, sms, smem, stream);
-    return launch_t<0, 4>(p, sms, smem, stream);
+    /* the LONG kernel when some pass of this launch attends to more
+     * positions than one chunk holds (and its 16-byte copies apply) */
+    const int chunk_short = int((ub / 4 - (size_t(p.hd) * (3 + W) + 2 * W)) /
+                                (2 * size_t(p.hd + 1) + 1));
+    const bool lng = p.hd % 4 == 0 && p.start_pos + p.n_tokens > std::min(chunk_short, NT);
+    if (lng)
+        return launch_type<true>(p, type, stages, sms, smem, stream);
+    return launch_type<false>(p, type, stages, sms, smem, stream);
 }
 
 } // namespace nut

@@ -81,6 +81,9 @@ struct MkParams {
     uint64_t limit_ns;
     int att_chunk;                      /* positions per attention chunk */
     int union_floats;                   /* floats in the digits/attention union */
+    Tagged *xchg;                       /* [count_aw][hd + 2] tagged partial
+                                           attention states of split histories
+                                           (the LONG kernel) */
 };
 
 /* Launches the kernel cooperatively on `stream`.  Returns the launch
