@@ -107,33 +107,32 @@ __global__ void rope_kv_rows_kernel(float *qkv, int M, int ldq, int start, const
  * CTA (tile, kv head g, sequence) owns kTileRows (token, head) rows: the
  * G = heads / kv_heads query heads of group g for QT = kTileRows / G
  * consecutive tokens, i.e. every row of the tile reads the same keys and
- * values.  Those are staged once per CTA, kChunk positions at a time, in a
- * double-buffered shared-memory ring (cp.async), and used by all 64 rows;
- * the previous kernel (one warp per row) read each key and value row from
- * L2 once per (token, head).  Warp w takes rows 8 w .. 8 w + 7:
- *   scores  lane j holds position c0 + j of the chunk for the warp's 8
- *           rows (key rows padded to hd + 1 floats: conflict-free; query
- *           rows broadcast as float4);
+ * values.  Those are staged once per CTA, 32 PPL positions at a time, in a
+ * double-buffered shared-memory ring (16-byte cp.async), and used by all 64
+ * rows.  Warp w takes rows 8 w .. 8 w + 7:
+ *   scores  lane j holds positions c0 + j and, with PPL = 2, c0 + j + 32
+ *           for the warp's 8 rows (key rows padded to hd + 4 floats and read
+ *           as float4: the 8 lanes of a quarter-warp hit distinct 16-byte
+ *           bank groups when hd is a multiple of 8; query rows broadcast as
+ *           float4);
  *   softmax online per row: chunk maximum by shuffles, the running
  *           maximum, exp weights (0 past the row's own position), the
  *           lane's share of the exp sum, the context rescaled;
  *   context lane owns dims lane, lane + 32, ... (DPL of them), weights
  *           broadcast from the warp's slice of shared memory.
  * After the last chunk the exp sums are reduced across lanes and the
- * context row is divided by it and rounded to fp16.  fp32 throughout; the
- * summation order differs from the reference's double sums only by
- * rounding.  Tiles with the longest histories are scheduled first. */
+ * context row is divided by it and rounded to fp16.  HD > 0 fixes the head
+ * dim at compile time (the dot products unroll fully); HD = 0 takes it at
+ * run time (up to 128).  fp32 throughout; the summation order differs from
+ * the reference's double sums only by rounding.  Tiles with the longest
+ * histories are scheduled first.  Measured (ncu, one launch at TinyLlama's
+ * shape, 512 tokens, with one position per lane and a run-time head dim):
+ * bound by instruction issue (56.5 M warp instructions for 17.8 M warp
+ * FMAs, 61 % issue-active), not by shared memory (26 % of its wavefronts). */
 constexpr int kTileRows = 64;
 constexpr int kTileWarps = 8;
 constexpr int kWarpRows = kTileRows / kTileWarps; /* 8 */
-constexpr int kChunk = 32;
 
-__device__ __forceinline__ void cp_async4(float *dst, const float *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(
-                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-                 "l"(src)
-                 : "memory");
-}
 __device__ __forceinline__ void cp_async16(float *dst, const float *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
                      static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -148,47 +147,46 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-template <int DPL>
+template <int HD, int PPL>
 __global__ void __launch_bounds__(kTileWarps * 32)
 attention_tiles_kernel(float *qkv, int ldq, int n, int seq0, int cache_seqs, int start,
                        const float *kcache, const float *vcache, int layer, int heads,
-                       int kv_heads, int hd, int max_seq, int Kp, __half *ctx, int zero_q) {
+                       int kv_heads, int hd_rt, int max_seq, int Kp, __half *ctx, int zero_q) {
+    constexpr int DPL = HD > 0 ? (HD + 31) / 32 : 4; /* context dims per lane */
+    constexpr int CHUNK = 32 * PPL;                  /* positions per stage */
     extern __shared__ __align__(16) float att_smem[];
+    const int hd = HD > 0 ? HD : hd_rt;
     const int G = heads / kv_heads, QT = kTileRows / G;
     const int ntiles = (n + QT - 1) / QT;
     const int tile = ntiles - 1 - int(blockIdx.x); /* longest histories first */
     const int g = int(blockIdx.y), sq = int(blockIdx.z);
     const int t0 = tile * QT, nt = min(QT, n - t0), R = nt * G;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ldk = hd + 1;
+    const int ldk = hd + 4, q4n = hd / 4;
     float *Qs = att_smem;                       /* [kTileRows][hd] */
-    float *Ks = Qs + kTileRows * hd;            /* [2][kChunk][hd + 1] */
-    float *Vs = Ks + 2 * kChunk * ldk;          /* [2][kChunk][hd] */
-    float *Ps = Vs + 2 * kChunk * hd;           /* [kTileWarps][kWarpRows][kChunk] */
+    float *Ks = Qs + kTileRows * hd;            /* [2][CHUNK][hd + 4] */
+    float *Vs = Ks + 2 * CHUNK * ldk;           /* [2][CHUNK][hd] */
+    float *Ps = Vs + 2 * CHUNK * hd;            /* [kTileWarps][kWarpRows][CHUNK] */
     const size_t base =
         ((size_t(layer) * cache_seqs + size_t(seq0 + sq)) * kv_heads + g) * size_t(max_seq) * hd;
     /* positions 0 .. P - 1 cover every row of the tile */
-    const int P = start + t0 + nt, nch = (P + kChunk - 1) / kChunk;
+    const int P = start + t0 + nt, nch = (P + CHUNK - 1) / CHUNK;
     auto stage = [&](int c) {
-        const int buf = c & 1, j0 = c * kChunk;
-        float *kd = Ks + buf * kChunk * ldk, *vd = Vs + buf * kChunk * hd;
+        const int buf = c & 1, j0 = c * CHUNK;
+        float *kd = Ks + buf * CHUNK * ldk, *vd = Vs + buf * CHUNK * hd;
         /* rows past P repeat row P - 1 (finite values; their weights are 0) */
-        for (int i = threadIdx.x; i < kChunk * hd; i += kTileWarps * 32) {
-            const int jj = i / hd, d = i - jj * hd;
-            const int j = min(j0 + jj, P - 1);
-            cp_async4(kd + jj * ldk + d, kcache + base + size_t(j) * hd + d);
-        }
-        for (int i = threadIdx.x; i < kChunk * hd / 4; i += kTileWarps * 32) {
-            const int jj = i / (hd / 4), d = (i - jj * (hd / 4)) * 4;
-            const int j = min(j0 + jj, P - 1);
-            cp_async16(vd + jj * hd + d, vcache + base + size_t(j) * hd + d);
+        for (int i = threadIdx.x; i < CHUNK * q4n; i += kTileWarps * 32) {
+            const int jj = i / q4n, d = (i - jj * q4n) * 4;
+            const size_t off = base + size_t(min(j0 + jj, P - 1)) * hd + d;
+            cp_async16(kd + jj * ldk + d, kcache + off);
+            cp_async16(vd + jj * hd + d, vcache + off);
         }
         cp_async_commit();
     };
     stage(0);
     /* the tile's query rows (row i: token t0 + i / G, head g G + i % G) */
-    for (int i = threadIdx.x; i < kTileRows * hd / 4; i += kTileWarps * 32) {
-        const int r = i / (hd / 4), d = (i - r * (hd / 4)) * 4;
+    for (int i = threadIdx.x; i < kTileRows * q4n; i += kTileWarps * 32) {
+        const int r = i / q4n, d = (i - r * q4n) * 4;
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (r < R) {
             const int t = t0 + r / G, h = g * G + r % G;
@@ -212,7 +210,7 @@ attention_tiles_kernel(float *qkv, int ldq, int n, int seq0, int cache_seqs, int
         for (int k = 0; k < DPL; k++)
             acc[r][k] = 0.0f;
     }
-    float *pw = Ps + warp * kWarpRows * kChunk;
+    float *pw = Ps + warp * kWarpRows * CHUNK;
     for (int c = 0; c < nch; c++) {
         if (c + 1 < nch) {
             stage(c + 1);
@@ -221,45 +219,70 @@ attention_tiles_kernel(float *qkv, int ldq, int n, int seq0, int cache_seqs, int
             cp_async_wait<0>();
         }
         __syncthreads();
-        const int buf = c & 1, j = c * kChunk + lane;
-        if (c * kChunk <= wmax) {
-            const float *kr = Ks + buf * kChunk * ldk + lane * ldk;
-            float s[kWarpRows];
+        const int buf = c & 1, c0 = c * CHUNK;
+        if (c0 <= wmax) {
+            float s[PPL][kWarpRows];
 #pragma unroll
-            for (int r = 0; r < kWarpRows; r++)
-                s[r] = 0.0f;
+            for (int u = 0; u < PPL; u++)
+#pragma unroll
+                for (int r = 0; r < kWarpRows; r++)
+                    s[u][r] = 0.0f;
+            const float *kb = Ks + buf * CHUNK * ldk + lane * ldk;
+#pragma unroll(HD > 0 ? HD / 4 : 4)
             for (int d = 0; d < hd; d += 4) {
-                const float k0 = kr[d], k1 = kr[d + 1], k2 = kr[d + 2], k3 = kr[d + 3];
+                float4 k4[PPL];
+#pragma unroll
+                for (int u = 0; u < PPL; u++)
+                    k4[u] = *reinterpret_cast<const float4 *>(kb + u * 32 * ldk + d);
 #pragma unroll
                 for (int r = 0; r < kWarpRows; r++) {
                     const float4 q = *reinterpret_cast<const float4 *>(Qs + (r0 + r) * hd + d);
-                    s[r] = fmaf(q.x, k0, s[r]);
-                    s[r] = fmaf(q.y, k1, s[r]);
-                    s[r] = fmaf(q.z, k2, s[r]);
-                    s[r] = fmaf(q.w, k3, s[r]);
+#pragma unroll
+                    for (int u = 0; u < PPL; u++) {
+                        s[u][r] = fmaf(q.x, k4[u].x, s[u][r]);
+                        s[u][r] = fmaf(q.y, k4[u].y, s[u][r]);
+                        s[u][r] = fmaf(q.z, k4[u].z, s[u][r]);
+                        s[u][r] = fmaf(q.w, k4[u].w, s[u][r]);
+                    }
                 }
             }
 #pragma unroll
             for (int r = 0; r < kWarpRows; r++) {
                 const int row = r0 + r;
-                const bool live = row < R && j <= start + t0 + row / G;
-                const float sc = live ? s[r] * scale : -INFINITY;
-                const float mn = fmaxf(m[r], warp_max(sc));
-                float p = 0.0f, corr = 1.0f;
+                const int last = row < R ? start + t0 + row / G : -1;
+                float sc[PPL], mx = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < PPL; u++) {
+                    sc[u] = c0 + u * 32 + lane <= last ? s[u][r] * scale : -INFINITY;
+                    mx = fmaxf(mx, sc[u]);
+                }
+                const float mn = fmaxf(m[r], warp_max(mx));
+                float corr = 1.0f, lsum = 0.0f;
                 if (mn != -INFINITY) {
                     corr = expf(m[r] - mn); /* 0 while m is still -inf */
-                    p = expf(sc - mn);      /* 0 past the row's position */
+#pragma unroll
+                    for (int u = 0; u < PPL; u++) {
+                        sc[u] = expf(sc[u] - mn); /* 0 past the row's position */
+                        lsum += sc[u];
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < PPL; u++)
+                        sc[u] = 0.0f;
                 }
-                l[r] = fmaf(l[r], corr, p);
+                l[r] = fmaf(l[r], corr, lsum);
 #pragma unroll
                 for (int k = 0; k < DPL; k++)
                     acc[r][k] *= corr;
                 m[r] = mn;
-                pw[r * kChunk + lane] = p;
+#pragma unroll
+                for (int u = 0; u < PPL; u++)
+                    pw[r * CHUNK + u * 32 + lane] = sc[u];
             }
             __syncwarp();
-            const float *vb = Vs + buf * kChunk * hd;
-            for (int jj = 0; jj < kChunk; jj += 4) {
+            const float *vb = Vs + buf * CHUNK * hd;
+#pragma unroll 2
+            for (int jj = 0; jj < CHUNK; jj += 4) {
                 float v[4][DPL];
 #pragma unroll
                 for (int u = 0; u < 4; u++)
@@ -270,7 +293,7 @@ attention_tiles_kernel(float *qkv, int ldq, int n, int seq0, int cache_seqs, int
                     }
 #pragma unroll
                 for (int r = 0; r < kWarpRows; r++) {
-                    const float4 p4 = *reinterpret_cast<const float4 *>(pw + r * kChunk + jj);
+                    const float4 p4 = *reinterpret_cast<const float4 *>(pw + r * CHUNK + jj);
 #pragma unroll
                     for (int k = 0; k < DPL; k++) {
                         acc[r][k] = fmaf(p4.x, v[0][k], acc[r][k]);
@@ -367,19 +390,20 @@ bool attention_prefill_supported(int heads, int kv_heads, int hd, int ldq) {
     if (kv_heads <= 0 || heads % kv_heads != 0)
         return false;
     const int G = heads / kv_heads;
-    return G <= kTileRows && kTileRows % G == 0 && hd > 0 && hd % 4 == 0 && hd <= 256 &&
+    return G <= kTileRows && kTileRows % G == 0 && hd > 0 && hd % 4 == 0 && hd <= 128 &&
            ldq % 4 == 0;
 }
 
-template <int DPL>
+template <int HD, int PPL>
 cudaError_t launch_tiles(float *qkv, int n, int nseq, int ldq, int seq0, int cache_seqs,
                          int start, const float *kcache, const float *vcache, int layer,
                          int heads, int kv_heads, int hd, int max_seq, int Kp, __half *ctx,
                          int zero_q, cudaStream_t s) {
-    const size_t smem = (size_t(kTileRows) * hd + size_t(2 * kChunk) * (hd + 1) +
-                         size_t(2 * kChunk) * hd + size_t(kTileRows) * kChunk) *
+    constexpr int CHUNK = 32 * PPL;
+    const size_t smem = (size_t(kTileRows) * hd + size_t(2 * CHUNK) * (hd + 4) +
+                         size_t(2 * CHUNK) * hd + size_t(kTileRows) * CHUNK) *
                         sizeof(float);
-    auto k = attention_tiles_kernel<DPL>;
+    auto k = attention_tiles_kernel<HD, PPL>;
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess)
@@ -401,26 +425,25 @@ cudaError_t attention_prefill(float *qkv, int n, int nseq, int ldq, int seq0, in
         return cudaErrorInvalidValue;
     auto *c = reinterpret_cast<__half *>(ctx);
     const int zq = zero_q ? 1 : 0;
-    switch ((hd + 31) / 32) {
-    case 1:
-        return launch_tiles<1>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
-                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
-    case 2:
-        return launch_tiles<2>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
-                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
-    case 3:
-        return launch_tiles<3>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
-                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
-    case 4:
-        return launch_tiles<4>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
-                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
-    case 5:
-    case 6:
-        return launch_tiles<6>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
-                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    /* compile-time head dims of the common shapes; two positions per lane
+     * where the staging ring of 64 positions leaves room for two CTAs per
+     * SM (hd <= 64) */
+    switch (hd) {
+    case 32:
+        return launch_tiles<32, 2>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache,
+                                   layer, heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 48:
+        return launch_tiles<48, 2>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache,
+                                   layer, heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 64:
+        return launch_tiles<64, 2>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache,
+                                   layer, heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+    case 128:
+        return launch_tiles<128, 1>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache,
+                                    layer, heads, kv_heads, hd, max_seq, Kp, c, zq, s);
     default:
-        return launch_tiles<8>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache, layer,
-                               heads, kv_heads, hd, max_seq, Kp, c, zq, s);
+        return launch_tiles<0, 1>(qkv, n, nseq, ldq, seq0, cache_seqs, start, kcache, vcache,
+                                  layer, heads, kv_heads, hd, max_seq, Kp, c, zq, s);
     }
 }
 

@@ -18,7 +18,7 @@ cudaError_t rope_kv_rows(float *qkv, int M, int ldq, int start, const float *rop
                          const float *rope_sin, int heads, int kv_heads, int hd, int dim, int kvd,
                          float *kcache, float *vcache, int layer, int max_seq, cudaStream_t s);
 /* Shapes attention_prefill takes: G = heads / kv_heads divides 64,
- * head_dim a multiple of 4 up to 256, ldq a multiple of 4. */
+ * head_dim a multiple of 4 up to 128, ldq a multiple of 4. */
 bool attention_prefill_supported(int heads, int kv_heads, int hd, int ldq);
 /* Causal attention of nseq prompts of n tokens each at positions start ..
  * start + n - 1: row b = sq n + t of qkv [nseq n][ldq] (q of head h at
