@@ -968,7 +968,11 @@ nut_status nut_batch_generate(nut_batch *b, const int32_t *prompts, int64_t n, i
         /* the prompt: as GEMMs over whole sequences, or one position per
          * pass (its classifier only after the last prompt token; the pass
          * before the last advances the position, so the last runs at n - 1) */
-        const bool gemm_prefill = n >= b->prefill_min && b->prefill_min > 0;
+        /* (shapes the tiled prompt attention does not take keep the
+         * per-pass prompt) */
+        const bool gemm_prefill =
+            n >= b->prefill_min && b->prefill_min > 0 &&
+            nut::attention_prefill_supported(b->heads_r, b->kvh_r, b->hd, b->nqkv);
         if (gemm_prefill)
             prefill(*b, int(n));
         for (int64_t t = 0; t < n && !gemm_prefill; t++) {
