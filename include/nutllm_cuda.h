@@ -198,9 +198,11 @@ nut_status nut_model_stream(const nut_model *model, void **stream);
  * fp16; fp32 accumulation), instead of the per-token loop of
  * prefill_quantized (src/quant_model.cpp:208-220).  Hidden states and the
  * KV cache then carry fp16 rounding (a looser bound than the per-token
- * path's parity); set 0 to keep every prompt on the per-token path.
- * Applies to nut_prefill and nut_generate_greedy.  No counterpart in the
- * reference. */
+ * path's parity); set 0 to keep every prompt on the per-token path.  The
+ * batch's causal attention runs in tiles that share their keys and values;
+ * shapes those tiles do not take (head_dim above 128 or not a multiple of
+ * 4) keep the per-token path whatever the threshold.  Applies to
+ * nut_prefill and nut_generate_greedy.  No counterpart in the reference. */
 nut_status nut_model_set_prefill_threshold(nut_model *model, int64_t min_tokens);
 
 /* Total kernels this library has launched in this process (all devices),
@@ -300,7 +302,9 @@ nut_status nut_batch_ipc_handle(nut_batch *batch, uint8_t *handle, int64_t size)
 nut_status nut_batch_open_peers(nut_batch *batch, const uint8_t *handles, int64_t stride);
 /* Prompts of at least min_tokens tokens (default 16; 0 = never) are
  * prefilled as GEMMs over chunks of whole sequences (causal attention per
- * sequence) instead of one position per pass. */
+ * sequence, in tiles that share their keys and values) instead of one
+ * position per pass; shapes the tiles do not take (per-rank head_dim above
+ * 128 or not a multiple of 4) keep one position per pass. */
 nut_status nut_batch_set_prefill_threshold(nut_batch *batch, int64_t min_tokens);
 /* This rank's shard without creating anything (host only): shard[8] =
  * {first head, heads, first kv head, kv heads, first ffn unit, ffn units,
